@@ -1,0 +1,374 @@
+"""Benchmark of the KERNIX-B200 .knx forward path (one JSON line on rank 0).
+
+Workload: config c2 -- the int8-quantised MLP 1024-4096-4096-1024 with GELU hidden layers (I8_COL weights), batch
+4096 per GPU, seeded synthetic inputs ~N(0,1) and random-init weights ~N(0,0.02). A step is one forward pass over
+one batch. With N GPUs (torchrun, one process per GPU) every rank runs its own replica on its own 4096 samples:
+the path has no cross-sample exchange, so there is no collective in the data path ("scaling": "weak").
+
+  value        samples/s over all ranks with inputs already in HBM (kernix_model_forward_device), each step
+               timed with CUDA events on the launching stream after an L2 flush, max over ranks
+  e2e          samples/s through the public C ABI kernix_capi_forward with page-locked host input and output
+               (host->device copy of the inputs and device->host copy of the outputs inside the timed region)
+  roofline     the dominant kernel (tcgen05 kind::i8 GEMM, all three layers), algorithmic int8 ops / CUDA-event time
+  cpu_baseline the reference's own CPU forward (oracle/_ref, compiled from the reference sources) on a bounded
+               sample, all host threads (one model instance per thread; the reference's forward is per-model serial)
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kernix|reference]
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = "c2"
+BATCH = 4096
+DIMS = [1024, 4096, 4096, 1024]
+METRIC = "samples/s, int8 MLP 1024-4096-4096-1024 (config c2), batch 4096 per GPU"
+WORKLOAD = "c2: int8-quantised MLP 1024-4096-4096-1024, GELU hidden, I8_COL per-output-channel weights, batch 4096"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["kernix", "reference"], default="kernix")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="time box of the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def model_file(rank):
+    from kernix_b200 import configs
+    return configs.model_path(CFG, os.environ.get("KERNIX_MODEL_DIR", f"/tmp/kernix_models_r{rank}"))
+
+
+# ------------------------------------------------------------------------------ reference CPU forward
+def reference_throughput(path, seconds, samples_per_call=8, threads=None):
+    """The reference's own forward (oracle/_ref: include/kernix_model.h compiled from source) on host cores: one
+    model per thread (kernix_model_forward is not reentrant per model; different models may run concurrently),
+    default workspace limit, so the int8 layers run the reference's kernix_qmatmul (x86: its scalar loop).
+    Returns (samples/s, threads, samples processed, seconds)."""
+    import numpy as np
+
+    from kernix_b200 import configs
+    from oracle import ref_lib
+
+    threads = threads or os.cpu_count() or 1
+    models = [ref_lib.RefModel(path) for _ in range(threads)]
+    x = configs.inputs(CFG, samples_per_call, seed=7)
+    models[0].forward(x)  # warm
+    counts = [0] * threads
+    stop = time.perf_counter() + seconds
+
+    def work(i):
+        m = models[i]
+        while time.perf_counter() < stop:
+            m.forward(x)
+            counts[i] += samples_per_call
+
+    t0 = time.perf_counter()
+    ts = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    dt = time.perf_counter() - t0
+    n = sum(counts)
+    for m in models:
+        m.close()
+    del np
+    return n / dt, threads, n, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import ref_lib
+    if not ref_lib.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libkernix_ref.so was not built (make -C oracle/ref)"}))
+        return
+    path = model_file(0)
+    threads = os.cpu_count() or 1
+    per_step = max(8, threads * 2)  # samples per step: a bounded sample of the workload
+    from oracle import ref_lib as rl
+    from kernix_b200 import configs
+    models = [rl.RefModel(path) for _ in range(threads)]
+    x = configs.inputs(CFG, per_step, seed=7)
+    chunks = [x[i::threads] for i in range(threads)]
+
+    def step():
+        ts = [threading.Thread(target=models[i].forward, args=(chunks[i],)) for i in range(threads) if len(chunks[i])]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    v = per_step * args.steps / dt
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_step": per_step},
+            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "reference",
+                             "sample": f"{per_step} samples per step, split over {threads} threads, one reference model each"},
+            "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi samples (200 ms) of this GPU's SM clock and throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------- GPU bench
+def run_kernix(args):
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from kernix_b200 import Model, build, configs, kx_abi
+    build.build()
+    L = kx_abi.lib()
+    L.kernix_model_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    L.kernix_model_forward_device.restype = ctypes.c_int
+    L.kernix_model_check.argtypes = [ctypes.c_void_p]
+    L.kernix_model_check.restype = ctypes.c_int
+
+    os.environ["KERNIX_DEVICE"] = str(local)
+    path = model_file(rank)
+    m = Model(path)
+    x_np = configs.inputs(CFG, BATCH, seed=100 + rank)
+    x_pin = torch.from_numpy(x_np).pin_memory()
+    out_pin = torch.empty((BATCH, DIMS[-1]), dtype=torch.float32).pin_memory()
+    x_dev = x_pin.cuda()
+    y_dev = torch.empty((BATCH, DIMS[-1]), dtype=torch.float32, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def fwd_device():
+        if L.kernix_model_forward_device(m._h, x_dev.data_ptr(), BATCH, y_dev.data_ptr(), stream.cuda_stream) != 0:
+            raise RuntimeError("forward_device failed")
+
+    # ---- value: device-resident forward, events per step, L2 flushed before each step
+    for _ in range(args.warmup):
+        fwd_device()
+    torch.cuda.synchronize()
+    if L.kernix_model_check(m._h) != 0:
+        raise RuntimeError("a kernel reported a failure")
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    with Clocks(local) as clk:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fwd_device()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    if L.kernix_model_check(m._h) != 0:
+        raise RuntimeError("a kernel reported a failure")
+    t_dev = sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3
+    t_dev = max_over_ranks(t_dev)
+    ms_step = t_dev / args.steps * 1e3
+    value = world * BATCH * args.steps / t_dev
+
+    # ---- e2e: public C ABI with page-locked host buffers (H2D + forward + D2H inside the timed region)
+    def fwd_host():
+        if L.kernix_capi_forward(m._h, x_pin.data_ptr(), BATCH, out_pin.data_ptr()) != 0:
+            raise RuntimeError("kernix_capi_forward failed")
+
+    for _ in range(args.warmup):
+        fwd_host()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fwd_host()
+    torch.cuda.synchronize()
+    t_e2e = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e = world * BATCH * args.steps / t_e2e
+    y_e2e = out_pin.numpy().copy()
+    if not np.array_equal(y_e2e, y_dev.cpu().numpy()):
+        raise RuntimeError("host-memory and device-memory forward disagree")
+
+    # ---- roofline of the dominant kernel: the int8 GEMM of each layer, CUDA events on the launching stream
+    roof = None
+    if rank == 0:
+        roof = gemm_roofline(L, torch, np, args.steps, flush)
+
+    # ---- CPU baseline: the reference's own forward on this host (rank 0 at N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1:
+        from oracle import ref_lib
+        if ref_lib.available():
+            v, thr, n, dt = reference_throughput(path, args.cpu_seconds)
+            cpu = {"value": v, "unit": "samples/s", "cores": thr, "kind": "reference",
+                   "sample": f"{n} samples of the c2 workload in {dt:.1f} s, {thr} threads with one reference model each "
+                             "(default workspace: int8 layers run the reference's kernix_qmatmul scalar loop on x86)"}
+        else:
+            cpu = {"value": None, "unit": "samples/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+
+    if rank == 0:
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except (OSError, ValueError):
+            pass
+        line = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic: inputs ~N(0,1) seeded per rank, random-init weights ~N(0,0.02) quantised per output column",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "global_batch": BATCH * world,
+                       "parallelism": f"dp{world} (independent replicas, batch sharded)",
+                       "l2": "flushed (256 MB write) before every timed device step, flush not timed; weights 25 MB"},
+            "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": BATCH * DIMS[0] * 4,
+                    "d2h_bytes_per_step": BATCH * DIMS[-1] * 4, "api": "kernix_capi_forward, page-locked host buffers"},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": 6 * args.steps,
+            "peaks_file": bool(peaks),
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def gemm_roofline(L, torch, np, steps, flush):
+    """Time kx_gemm_i8 on the three c2 layer shapes (M = 4096) with CUDA events around each launch."""
+    rng = np.random.default_rng(3)
+    st = torch.cuda.current_stream()
+    tot_ops, tot_t, per = 0.0, 0.0, []
+    for k, n in zip(DIMS[:-1], DIMS[1:]):
+        xq = torch.from_numpy(rng.integers(-127, 128, (BATCH, k), dtype=np.int8)).cuda()
+        wq = torch.from_numpy(rng.integers(-127, 128, (n, k), dtype=np.int8)).cuda()
+        sx = torch.full((BATCH,), 0.01, device="cuda")
+        sc = torch.full((n,), 0.001, device="cuda")
+        b = torch.zeros(n, device="cuda")
+        y = torch.empty((BATCH, n), device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+        def launch():
+            if L.kx_gemm_i8(xq.data_ptr(), k, sx.data_ptr(), wq.data_ptr(), k, sc.data_ptr(), b.data_ptr(), y.data_ptr(), n,
+                            BATCH, n, k, 1, 0.0, status.data_ptr(), st.cuda_stream) != 0:
+                raise RuntimeError("kx_gemm_i8 failed")
+
+        for _ in range(3):
+            launch()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(st)
+            launch()
+            e1.record(st)
+        torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise RuntimeError("GEMM reported a timeout")
+        t = sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3 / steps
+        ops = 2.0 * BATCH * k * n
+        per.append({"m": BATCH, "k": k, "n": n, "us": t * 1e6, "tops": ops / t / 1e12})
+        tot_ops += ops
+        tot_t += t
+    achieved = tot_ops / tot_t / 1e12
+    peak, basis = None, None
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak = 2.0 * float(peaks["bf16_tflops"])
+        basis = "2 x measured dense bf16 burst (MEASURED_PEAKS.json); the int8 tensor rate is twice bf16 on B200"
+    except (OSError, ValueError, KeyError):
+        peak = 2.0 * 1590.0
+        basis = "2 x fallback dense bf16 1.59 PFLOP/s"
+    return {"kernel": "k_gemm_i8 (tcgen05 kind::i8, 128x256 tiles)", "bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TOP/s (int8, 2 ops per MAC)", "frac": achieved / peak, "peak_basis": basis,
+            "traffic": None, "per_layer": per,
+            "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_kernix(a)

@@ -1,0 +1,129 @@
+/* KERNIX-B200 kernel-level C ABI: the sm_100a CUDA kernels behind the model runtime.
+ *
+ * Plain device pointers, sizes and a cudaStream_t passed as void*; no CUDA or torch types. All matrices
+ * are row-major with an explicit leading dimension (elements). Every function returns 0 when the launch
+ * was accepted and -1 on bad arguments or a launch error. Kernels whose waits are bounded write
+ * KX_STATUS_TIMEOUT into *status (device memory, may be NULL) instead of hanging.
+ * Each entry names the reference computation it replaces (KERNIX reference file:line).
+ */
+#ifndef KX_KERNELS_H
+#define KX_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kernix.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KX_STATUS_OK 0
+#define KX_STATUS_TIMEOUT 1
+
+/* ---- int8 path (include/kernix_model.h:99-182 kernix_qmatmul) ---- */
+
+/* Per-row dynamic int8 quantisation (kernix_qmatmul :110-142): m = max|x| over the row (NaN wins),
+ * sx = m > 0 ? m / 127 : 1, xq = clamp(rint(x * (1/sx)), -127, 127); rows whose m is NaN/inf get sx = NaN
+ * (their GEMM output becomes NaN, as the reference's NaN rows). xq columns k..ldq-1 are zeroed. */
+KERNIX_API int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream);
+
+/* y = act(((float)acc * sx[row]) * scale[col] + bias[col]) with acc = sum_t xq[row][t] * wq[col][t] in int32
+ * on tcgen05 kind::i8 (kernix_qmatmul :143-177 and the step's activation :1854-1856). wq: n x ldw int8,
+ * K-major (see kx_prep_i8_weight). ldq, ldw multiples of 16. bias may be NULL (adds 0). */
+KERNIX_API int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
+               const float* bias, float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, void* stream);
+
+/* int32 accumulators only (acc[row][col], leading dimension ldacc): exposes the integer result for tests. */
+KERNIX_API int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
+                   int* status, void* stream);
+
+/* Load-time repack of an I8_COL weight block (the file's k x n, in x out) into n x ldw K-major, zero padded
+ * (replaces kernix_qweight_pack :62-81, whose layout served NEON sdot). */
+KERNIX_API int kx_prep_i8_weight(const int8_t* q_kn, int k, int n, int8_t* wq, int ldw, void* stream);
+
+/* ---- fp32 dense path (kernix_dense :544-550 -> kernix_matmul_ep_into include/kernix.h:955-976,
+ *      src/kernix_metal.m:161-265 MPS+AMX split with the bias_act epilogue :269-299) ---- */
+
+/* y = act(x . W + bias) in 3xTF32 on tcgen05 kind::tf32, fp32 accumulation in TMEM. W is given as the
+ * tf32 split planes w_hi, w_lo (n x ldw, K-major, ldw % 4 == 0; see kx_prep_f32_weight). bias may be NULL. */
+KERNIX_API int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
+                int ldy, int m, int n, int k, int act, float alpha, int* status, void* stream);
+
+/* Load-time transpose + split of a float weight (k x n, in x out) into n x ldw K-major planes
+ * hi = tf32(w), lo = w - hi (exact), zero padded. */
+KERNIX_API int kx_prep_f32_weight(const float* w_kn, int k, int n, float* w_hi, float* w_lo, int ldw, void* stream);
+
+/* ---- elementwise / row ops (memory-bound) ---- */
+
+/* y[r][c] = act(x[r][c] + bias[c]) (kernix_bias_act :528-541; ACT step :1864-1866). x == y allowed; bias may be NULL. */
+KERNIX_API int kx_bias_act(const float* x, float* y, long rows, int cols, const float* bias, int act, float alpha, void* stream);
+
+/* row softmax (floats_softmax_into include/kernix.h:652-657); x == y allowed */
+KERNIX_API int kx_softmax_rows(const float* x, float* y, long rows, int cols, void* stream);
+
+/* row layer norm, biased variance, (x-mean)*rstd*gamma + beta (kernix_layer_norm_rows_into include/kernix.h:667-677);
+ * gamma/beta may be NULL; x == y allowed */
+KERNIX_API int kx_layernorm_rows(const float* x, float* y, long rows, int cols, const float* gamma, const float* beta, float eps,
+                      void* stream);
+
+/* y = x * g[c] + b[c] per row (AFFINE step :1882-1890); x == y allowed */
+KERNIX_API int kx_affine_rows(const float* x, float* y, long rows, int cols, const float* g, const float* b, void* stream);
+
+/* y[s][i] = x[s][i] + cst[i] per sample of `per` floats (ADD_CONST step :1891-1895); x == y allowed */
+KERNIX_API int kx_add_const(const float* x, float* y, long samples, long per, const float* cst, void* stream);
+
+/* elementwise op with size-1 row/column broadcast inside each sample (kernix_binary_run :877-906).
+ * a: samples x ra x ca, b: samples x rb x cb, y: samples x R x C; y may alias a or b when shapes match. */
+KERNIX_API int kx_binary(const float* a, int ra, int ca, const float* b, int rb, int cb, float* y, long samples, int R, int C, int op,
+              void* stream);
+
+/* max / avg k x k pooling, NHWC (kernix_pooling_run :773-807) */
+KERNIX_API int kx_pool2d(const float* x, float* y, int B, int H, int W, int C, int Ho, int Wo, int kh, int kw, int sh, int sw, int pt,
+              int pl, int type, int count_pad, void* stream);
+
+/* per-sample max / mean over R rows (kernix_global_pool_run :810-830) */
+KERNIX_API int kx_global_pool(const float* x, float* y, long B, int R, int C, int type, void* stream);
+
+/* per-sample axis permutation, output axis k = input axis perm[k] (kernix_permute_run :833-862) */
+KERNIX_API int kx_permute(const float* x, float* y, long B, int nd, const int* dims, const int* perm, void* stream);
+
+/* copy `cols` columns of each row from x (leading dimension ldx) into y at column offset yoff (leading dimension ldy):
+ * CONCAT on the channel axis (:908-921) and SELECT on the last axis (:944-947) */
+KERNIX_API int kx_copy_cols(const float* x, long ldx, float* y, long ldy, long yoff, long rows, long cols, void* stream);
+
+/* zero-pad H and W of an NHWC image (kernix_pad_run :949-966) */
+KERNIX_API int kx_pad2d(const float* x, float* y, int B, int H, int W, int C, int Ho, int Wo, int pt, int pl, void* stream);
+
+/* nearest upsampling (kernix_upsample_run :968-983) */
+KERNIX_API int kx_upsample2d(const float* x, float* y, int B, int H, int W, int C, int Ho, int Wo, int sh, int sw, void* stream);
+
+/* table rows for float ids, NaN rows for ids out of range or not integral (kernix_embedding_run :986-1000) */
+KERNIX_API int kx_embedding(const float* ids, long n, const float* table, int vocab, int dim, float* y, void* stream);
+
+/* depthwise conv (groups == cin): out = bias, += x * w per in-range tap, then act (kernix_conv_run :724-752) */
+KERNIX_API int kx_conv_depthwise(const float* x, const float* w, const float* bias, float* y, int B, int H, int W, int C, int Co,
+                      int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl, int act, float alpha,
+                      void* stream);
+
+/* Implicit-GEMM convolution (NHWC, weights (ky,kx,ci) x cout as the file stores them) on tcgen05 3xTF32 with
+ * fused bias + act; the im2col rows are gathered straight into shared memory, never materialised
+ * (replaces kernix_conv_run's im2col + sgemm tiles :662-771). w_hi/w_lo: cout x ldw split planes of the
+ * weight (kx_prep_f32_weight), ldw >= kh*kw*cin/groups. Output group g writes channels [g*cog, (g+1)*cog). */
+KERNIX_API int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y, int B, int H,
+                int W, int C, int Co, int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl,
+                int groups, int act, float alpha, int* status, void* stream);
+
+/* scaled dot-product attention per (sample, head): ctx = softmax(scale * Q K^T [+ causal -inf]) V with
+ * scale = 1/sqrt(dk) (kernix_attention_run :1015-1046). q: (B*Rq) rows of H*dk at leading dim ldq, k: (B*S) rows
+ * of H*dk (ldk), v: (B*S) rows of H*dv (ldv), ctx: (B*Rq) rows of H*dv (ldc). */
+KERNIX_API int kx_attention(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* ctx, int ldc, int B,
+                 int Rq, int S, int H, int dk, int dv, int causal, void* stream);
+
+/* y = max(a*x + b, 0), fused multiply-add then max (src/kernix_metal.m:331-338; include/kernix.h:990) */
+KERNIX_API int kx_fma_relu(const float* a, const float* x, const float* b, float* y, size_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

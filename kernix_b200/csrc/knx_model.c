@@ -1,0 +1,752 @@
+/* KERNIX-B200 model runtime: device weights, device workspace, chunked forward, public API.
+ *
+ * Replaces the reference's executor (include/kernix_model.h: workspace kernix_model_shape :1629-1676,
+ * kernix_model_alloc :1679-1688, per-step dispatch kernix_step_run :1844-1905, kernix_model_run :1995-2016,
+ * kernix_model_forward :2023-2064). Each model owns one CUDA stream on one device; a forward copies each
+ * chunk of input rows host -> device, launches one kernel chain over the chunk, and copies the output rows
+ * back, all ordered on that stream. Storage buffers follow the loader's plan (knx_load.c), so in-place steps
+ * and RESHAPE views behave as in the reference. The workspace is a single device arena sized for one chunk.
+ */
+#define _GNU_SOURCE
+#include <cuda_runtime_api.h>
+#include <limits.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "kernix_capi.h"
+#include "kernix_cuda.h"
+#include "kernix_model.h"
+#include "kx_internal.h"
+#include "kx_kernels.h"
+
+#define KX_ALIGN 256
+
+struct kx_model_impl {
+    kx_graph* g;
+    int device;
+    cudaStream_t stream;
+    /* workspace (one arena) */
+    void* arena;
+    size_t arena_bytes;
+    float** st;           /* device storage buffers */
+    float* xin;           /* device input rows */
+    uint8_t* scratch;     /* per-step scratch: int8 activations, attention Q/K/V/context */
+    int* status;          /* device status word of bounded waits */
+    int* status_h;        /* pinned host copy */
+    size_t scratch_per_row_max;
+    /* host output owned by the model (pinned) */
+    float* out_host;
+    size_t out_host_floats;
+    float_tensor out_t;
+};
+
+static int dev_guard_enter(const kernix_model* m, int* prev) {
+    if (cudaGetDevice(prev) != cudaSuccess) *prev = -1;
+    if (*prev != m->impl->device && cudaSetDevice(m->impl->device) != cudaSuccess) return -1;
+    return 0;
+}
+
+static void dev_guard_leave(const kernix_model* m, int prev) {
+    if (prev >= 0 && prev != m->impl->device) cudaSetDevice(prev);
+}
+
+static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+/* ------------------------------------------------------------------------------- weight upload */
+static int upload(void** dst, const void* src, size_t bytes) {
+    if (cudaMalloc(dst, bytes ? bytes : 4) != cudaSuccess) return -1;
+    if (bytes && cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    return 0;
+}
+
+static int upload_f(float** dst, const float* src, size_t n) {
+    if (src == NULL) {
+        *dst = NULL;
+        return 0;
+    }
+    return upload((void**)dst, src, n * sizeof(float));
+}
+
+/* float weight k x n -> tf32 split planes n x ldw at rows [row0, row0+n) of (hi, lo) */
+static int prep_f32_into(const kx_weight* w, float* hi, float* lo, int ldw, size_t row0, cudaStream_t st) {
+    float* raw = NULL;
+    if (upload((void**)&raw, w->f, (size_t)w->k * w->n * sizeof(float)) != 0) {
+        cudaFree(raw);
+        return -1;
+    }
+    int rc = kx_prep_f32_weight(raw, w->k, w->n, hi + row0 * (size_t)ldw, lo + row0 * (size_t)ldw, ldw, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) rc = -1;
+    cudaFree(raw);
+    return rc;
+}
+
+static int prep_f32(kx_weight* w, cudaStream_t st) {
+    w->ldw = (int)round_up((size_t)w->k, 32);
+    const size_t bytes = (size_t)w->n * w->ldw * sizeof(float);
+    if (cudaMalloc((void**)&w->d_hi, bytes) != cudaSuccess || cudaMalloc((void**)&w->d_lo, bytes) != cudaSuccess) return -1;
+    return prep_f32_into(w, w->d_hi, w->d_lo, w->ldw, 0, st);
+}
+
+static int prep_i8(kx_weight* w, cudaStream_t st) {
+    w->ldw = (int)round_up((size_t)w->k, 16);
+    int8_t* raw = NULL;
+    if (cudaMalloc((void**)&w->d_q, (size_t)w->n * w->ldw) != cudaSuccess) return -1;
+    if (upload((void**)&raw, w->q, (size_t)w->k * w->n) != 0 || upload_f(&w->d_scale, w->scale_h, (size_t)w->n) != 0) {
+        cudaFree(raw);
+        return -1;
+    }
+    int rc = kx_prep_i8_weight(raw, w->k, w->n, w->d_q, w->ldw, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) rc = -1;
+    cudaFree(raw);
+    return rc;
+}
+
+static void weight_dev_free(kx_weight* w) {
+    cudaFree(w->d_hi);
+    cudaFree(w->d_lo);
+    cudaFree(w->d_q);
+    cudaFree(w->d_scale);
+    cudaFree(w->d_raw);
+    w->d_hi = w->d_lo = w->d_raw = w->d_scale = NULL;
+    w->d_q = NULL;
+}
+
+static int conv_pointwise(const kx_step* s) {
+    return s->kh == 1 && s->kw == 1 && s->sh == 1 && s->sw == 1 && s->pt == 0 && s->pb == 0 && s->pl == 0 && s->pr == 0;
+}
+
+static int conv_depthwise(const kx_step* s) { return s->groups > 1 && s->in / s->groups == 1; }
+
+/* device copies of one step's parameters, in the layouts the kernels want */
+static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
+    switch (s->kind) {
+    case KERNIX_OP_LINEAR:
+        if (s->w.int8 ? prep_i8(&s->w, st) : prep_f32(&s->w, st)) return -1;
+        return upload_f(&s->d_bias, s->bias, (size_t)s->out);
+    case KERNIX_OP_CONV:
+        if (conv_depthwise(s)) {
+            if (upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n) != 0) return -1;
+        } else if (prep_f32(&s->w, st) != 0) {
+            return -1;
+        }
+        return upload_f(&s->d_bias, s->bias, (size_t)s->out);
+    case KERNIX_OP_LAYERNORM:
+        return upload_f(&s->d_gamma, s->gamma, (size_t)s->in) || upload_f(&s->d_beta, s->beta, (size_t)s->in) ? -1 : 0;
+    case KERNIX_OP_AFFINE:
+        return upload_f(&s->d_gamma, s->gamma, (size_t)s->in) || upload_f(&s->d_beta, s->beta, (size_t)s->in) ? -1 : 0;
+    case KERNIX_OP_ADD_CONST:
+        return upload_f(&s->d_cst, s->cst, (size_t)s->in);
+    case KERNIX_OP_EMBEDDING:
+        return upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n);
+    case KERNIX_OP_ATTENTION: {
+        const size_t hk = (size_t)s->heads * s->dk, hv = (size_t)s->heads * s->dv;
+        s->qkv_fused = s->n_in == 1;
+        if (s->qkv_fused) { /* one GEMM: rows [Wq^T; Wk^T; Wv^T], columns of the product = [Q | K | V] */
+            kx_weight* f = &s->wqkv;
+            f->k = s->w.k;
+            f->n = (int)(2 * hk + hv);
+            f->ldw = (int)round_up((size_t)f->k, 32);
+            const size_t bytes = (size_t)f->n * f->ldw * sizeof(float);
+            if (cudaMalloc((void**)&f->d_hi, bytes) != cudaSuccess || cudaMalloc((void**)&f->d_lo, bytes) != cudaSuccess)
+                return -1;
+            if (prep_f32_into(&s->w, f->d_hi, f->d_lo, f->ldw, 0, st) || prep_f32_into(&s->wk, f->d_hi, f->d_lo, f->ldw, hk, st) ||
+                prep_f32_into(&s->wv, f->d_hi, f->d_lo, f->ldw, 2 * hk, st))
+                return -1;
+            if (s->bias) {
+                if (cudaMalloc((void**)&s->d_bqkv, (2 * hk + hv) * sizeof(float)) != cudaSuccess) return -1;
+                if (cudaMemcpy(s->d_bqkv, s->bias, hk * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                    cudaMemcpy(s->d_bqkv + hk, s->bk, hk * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                    cudaMemcpy(s->d_bqkv + 2 * hk, s->bv, hv * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                    return -1;
+            }
+        } else {
+            if (prep_f32(&s->w, st) || prep_f32(&s->wk, st) || prep_f32(&s->wv, st)) return -1;
+            if (upload_f(&s->d_bias, s->bias, hk) || upload_f(&s->d_bk, s->bk, hk) || upload_f(&s->d_bv, s->bv, hv)) return -1;
+        }
+        if (prep_f32(&s->wo, st) != 0) return -1;
+        return upload_f(&s->d_bo, s->bo, (size_t)s->out);
+    }
+    default:
+        (void)g;
+        return 0;
+    }
+}
+
+static void step_dev_free(kx_step* s) {
+    weight_dev_free(&s->w);
+    weight_dev_free(&s->wk);
+    weight_dev_free(&s->wv);
+    weight_dev_free(&s->wo);
+    weight_dev_free(&s->wqkv);
+    cudaFree(s->d_bias); cudaFree(s->d_bk); cudaFree(s->d_bv); cudaFree(s->d_bo);
+    cudaFree(s->d_gamma); cudaFree(s->d_beta); cudaFree(s->d_cst); cudaFree(s->d_bqkv);
+    s->d_bias = s->d_bk = s->d_bv = s->d_bo = s->d_gamma = s->d_beta = s->d_cst = s->d_bqkv = NULL;
+}
+
+/* scratch bytes per input row (per sample for attention) that a step needs during its launch */
+static size_t step_scratch(const kx_graph* g, const kx_step* s, size_t* per_sample) {
+    *per_sample = 0;
+    const kx_val* vi = &g->vals[s->inp[0]];
+    if (s->kind == KERNIX_OP_LINEAR && s->w.int8) {
+        const size_t ldq = round_up((size_t)s->in, 16);
+        *per_sample = (size_t)vi->r * (round_up(ldq, 16) + 4 * 4);
+    } else if (s->kind == KERNIX_OP_ATTENTION) {
+        const kx_val* vv = &g->vals[s->inp[s->n_in > 1 ? 1 : 0]];
+        const size_t hk = (size_t)s->heads * s->dk, hv = (size_t)s->heads * s->dv;
+        const size_t rq = (size_t)vi->r, S = (size_t)vv->r;
+        *per_sample = (rq * hk + S * hk + S * hv + rq * hv) * sizeof(float) + 4 * KX_ALIGN;
+    }
+    return *per_sample;
+}
+
+static void model_release(kernix_model* m) {
+    struct kx_model_impl* im = m->impl;
+    if (im->arena) cudaFree(im->arena);
+    im->arena = NULL;
+    im->arena_bytes = 0;
+    free(im->st);
+    im->st = NULL;
+    im->xin = NULL;
+    im->scratch = NULL;
+    im->status = NULL;
+    if (im->out_host) cudaFreeHost(im->out_host);
+    im->out_host = NULL;
+    im->out_host_floats = 0;
+    m->batch = -1;
+}
+
+/* arena for `rows` input rows: storage buffers, input rows, scratch, status word */
+static int model_alloc(kernix_model* m, int rows);
+
+static int model_alloc(kernix_model* m, int rows) {
+    struct kx_model_impl* im = m->impl;
+    kx_graph* g = im->g;
+    float* keep_out = im->out_host;
+    size_t keep_n = im->out_host_floats;
+    im->out_host = NULL;
+    model_release(m);
+    im->out_host = keep_out;
+    im->out_host_floats = keep_n;
+    const size_t B = (size_t)rows / (size_t)m->seq_len;
+    size_t off = 0;
+    size_t* st_off = calloc((size_t)g->n_st + 1, sizeof(size_t));
+    im->st = calloc((size_t)g->n_st + 1, sizeof(float*));
+    if (st_off == NULL || im->st == NULL) {
+        free(st_off);
+        return -1;
+    }
+    for (int k = 0; k < g->n_st; k++) {
+        st_off[k] = off;
+        off = round_up(off + B * g->st_cap[k] * sizeof(float), KX_ALIGN);
+    }
+    const size_t xin_off = off;
+    off = round_up(off + (size_t)rows * m->in_dim * sizeof(float), KX_ALIGN);
+    const size_t scr_off = off;
+    off = round_up(off + B * im->scratch_per_row_max + KX_ALIGN, KX_ALIGN);
+    const size_t status_off = off;
+    off += KX_ALIGN;
+    if (cudaMalloc(&im->arena, off) != cudaSuccess) {
+        im->arena = NULL;
+        free(st_off);
+        fprintf(stderr, "forward: cannot allocate %zu bytes of device workspace\n", off);
+        return -1;
+    }
+    im->arena_bytes = off;
+    uint8_t* base = (uint8_t*)im->arena;
+    for (int k = 0; k < g->n_st; k++) im->st[k] = (float*)(base + st_off[k]);
+    im->xin = (float*)(base + xin_off);
+    im->scratch = base + scr_off;
+    im->status = (int*)(base + status_off);
+    free(st_off);
+    if (cudaMemset(im->status, 0, sizeof(int)) != cudaSuccess) return -1;
+    m->batch = rows;
+    return 0;
+}
+
+/* device pointer of value v in the current chunk */
+static float* val_ptr(const struct kx_model_impl* im, int v) {
+    const kx_val* val = &im->g->vals[v];
+    return val->st < 0 ? im->xin : im->st[val->st];
+}
+
+static void* align_ptr(void* p) { return (void*)round_up((uintptr_t)p, KX_ALIGN); }
+
+/* one step over B samples */
+static int step_run(kernix_model* m, int i, int B) {
+    struct kx_model_impl* im = m->impl;
+    kx_graph* g = im->g;
+    kx_step* s = &g->steps[i];
+    const kx_val* vi = &g->vals[s->inp[0]];
+    const kx_val* vo = &g->vals[i + 1];
+    const float* a = val_ptr(im, s->inp[0]);
+    float* y = val_ptr(im, i + 1);
+    const long rin = (long)B * vi->r, rout = (long)B * vo->r;
+    cudaStream_t st = im->stream;
+    switch (s->kind) {
+    case KERNIX_OP_LINEAR:
+        if (s->w.int8) {
+            const int ldq = (int)round_up((size_t)s->in, 16);
+            int8_t* xq = (int8_t*)im->scratch;
+            float* sx = (float*)align_ptr(xq + (size_t)rin * ldq);
+            if (kx_quant_rows(a, s->in, (int)rin, s->in, xq, ldq, sx, st) != 0) return -1;
+            return kx_gemm_i8(xq, ldq, sx, s->w.d_q, s->w.ldw, s->w.d_scale, s->d_bias, y, s->out, (int)rin, s->out, s->in,
+                              s->act, s->alpha, im->status, st);
+        }
+        return kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act,
+                           s->alpha, im->status, st);
+    case KERNIX_OP_ACT:
+        return kx_bias_act(a, y, rout, vo->c, NULL, s->act, s->alpha, st);
+    case KERNIX_OP_LAYERNORM:
+        return kx_layernorm_rows(a, y, rout, vo->c, s->d_gamma, s->d_beta, s->eps, st);
+    case KERNIX_OP_SOFTMAX:
+        return kx_softmax_rows(a, y, rout, vo->c, st);
+    case KERNIX_OP_CONV: {
+        const int H = vi->d[0], W = vi->nd == 3 ? vi->d[1] : 1, Ho = vo->d[0], Wo = vo->nd == 3 ? vo->d[1] : 1;
+        if (s->groups == 1 && conv_pointwise(s))
+            return kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in,
+                               s->act, s->alpha, im->status, st);
+        if (conv_depthwise(s))
+            return kx_conv_depthwise(a, s->w.d_raw, s->d_bias, y, B, H, W, vi->c, vo->c, Ho, Wo, s->kh, s->kw, s->sh, s->sw,
+                                     s->dh, s->dw, s->pt, s->pl, s->act, s->alpha, st);
+        return kx_conv_f32(a, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, B, H, W, vi->c, vo->c, Ho, Wo, s->kh, s->kw, s->sh,
+                           s->sw, s->dh, s->dw, s->pt, s->pl, s->groups, s->act, s->alpha, im->status, st);
+    }
+    case KERNIX_OP_POOL: {
+        const int H = vi->d[0], W = vi->nd == 3 ? vi->d[1] : 1, Ho = vo->d[0], Wo = vo->nd == 3 ? vo->d[1] : 1;
+        return kx_pool2d(a, y, B, H, W, vi->c, Ho, Wo, s->kh, s->kw, s->sh, s->sw, s->pt, s->pl, s->ptype, s->count_pad, st);
+    }
+    case KERNIX_OP_GLOBAL_POOL:
+        return kx_global_pool(a, y, B, vi->r, vi->c, s->ptype, st);
+    case KERNIX_OP_RESHAPE:
+        return 0;
+    case KERNIX_OP_PERMUTE:
+        return kx_permute(a, y, B, vi->nd, vi->d, s->perm, st);
+    case KERNIX_OP_BINARY: {
+        const kx_val* vb = &g->vals[s->inp[1]];
+        return kx_binary(a, vi->r, vi->c, val_ptr(im, s->inp[1]), vb->r, vb->c, y, B, vo->r, vo->c, s->bop, st);
+    }
+    case KERNIX_OP_CONCAT: {
+        long off = 0;
+        for (int k = 0; k < s->n_in; k++) {
+            const kx_val* v = &g->vals[s->inp[k]];
+            const float* src = val_ptr(im, s->inp[k]);
+            if (s->axis == KERNIX_AXIS_LAST) {
+                if (kx_copy_cols(src, v->c, y, vo->c, off, rout, v->c, st) != 0) return -1;
+                off += v->c;
+            } else {
+                const long per = (long)v->r * v->c;
+                if (kx_copy_cols(src, per, y, (long)vo->r * vo->c, off, B, per, st) != 0) return -1;
+                off += per;
+            }
+        }
+        return 0;
+    }
+    case KERNIX_OP_EMBEDDING:
+        return kx_embedding(a, rin * vi->c, s->w.d_raw, s->w.k, s->w.n, y, st);
+    case KERNIX_OP_AFFINE:
+        return kx_affine_rows(a, y, rout, vo->c, s->d_gamma, s->d_beta, st);
+    case KERNIX_OP_ADD_CONST:
+        return kx_add_const(a, y, B, s->in, s->d_cst, st);
+    case KERNIX_OP_SELECT:
+        if (s->axis == KERNIX_AXIS_FIRST) {
+            const long per = (long)vi->r * vi->c, blk = per / vi->d[0];
+            return kx_copy_cols(a + (long)s->start * blk, per, y, blk * s->len, 0, B, blk * s->len, st);
+        }
+        return kx_copy_cols(a + s->start, vi->c, y, s->len, 0, rin, s->len, st);
+    case KERNIX_OP_PAD: {
+        const int H = vi->d[0], W = vi->nd == 3 ? vi->d[1] : 1, Ho = vo->d[0], Wo = vo->nd == 3 ? vo->d[1] : 1;
+        return kx_pad2d(a, y, B, H, W, vi->c, Ho, Wo, s->pt, s->pl, st);
+    }
+    case KERNIX_OP_UPSAMPLE: {
+        const int H = vi->d[0], W = vi->nd == 3 ? vi->d[1] : 1, Ho = vo->d[0], Wo = vo->nd == 3 ? vo->d[1] : 1;
+        return kx_upsample2d(a, y, B, H, W, vi->c, Ho, Wo, s->sh, s->sw, st);
+    }
+    case KERNIX_OP_ATTENTION: {
+        const int vid = s->inp[s->n_in > 1 ? 1 : 0], kid = s->inp[s->n_in > 2 ? 2 : s->n_in > 1 ? 1 : 0];
+        const kx_val* vv = &g->vals[vid];
+        const int hk = s->heads * s->dk, hv = s->heads * s->dv;
+        const long S = (long)B * vv->r;
+        float* ctx;
+        if (s->qkv_fused) {
+            const int nq = 2 * hk + hv;
+            float* qkv = (float*)align_ptr(im->scratch);
+            ctx = (float*)align_ptr(qkv + (size_t)rin * nq);
+            if (kx_gemm_f32(a, s->in, s->wqkv.d_hi, s->wqkv.d_lo, s->wqkv.ldw, s->d_bqkv, qkv, nq, (int)rin, nq, s->in,
+                            KERNIX_ACT_NONE, 0.0f, im->status, st) != 0 ||
+                kx_attention(qkv, nq, qkv + hk, nq, qkv + 2 * hk, nq, ctx, hv, B, vi->r, vv->r, s->heads, s->dk, s->dv,
+                             s->causal, st) != 0)
+                return -1;
+        } else {
+            float* Q = (float*)align_ptr(im->scratch);
+            float* K = (float*)align_ptr(Q + (size_t)rin * hk);
+            float* V = (float*)align_ptr(K + (size_t)S * hk);
+            ctx = (float*)align_ptr(V + (size_t)S * hv);
+            const kx_val* vk = &g->vals[kid];
+            if (kx_gemm_f32(a, vi->c, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, Q, hk, (int)rin, hk, vi->c, KERNIX_ACT_NONE,
+                            0.0f, im->status, st) != 0 ||
+                kx_gemm_f32(val_ptr(im, kid), vk->c, s->wk.d_hi, s->wk.d_lo, s->wk.ldw, s->d_bk, K, hk, (int)S, hk, vk->c,
+                            KERNIX_ACT_NONE, 0.0f, im->status, st) != 0 ||
+                kx_gemm_f32(val_ptr(im, vid), vv->c, s->wv.d_hi, s->wv.d_lo, s->wv.ldw, s->d_bv, V, hv, (int)S, hv, vv->c,
+                            KERNIX_ACT_NONE, 0.0f, im->status, st) != 0 ||
+                kx_attention(Q, hk, K, hk, V, hv, ctx, hv, B, vi->r, vv->r, s->heads, s->dk, s->dv, s->causal, st) != 0)
+                return -1;
+        }
+        return kx_gemm_f32(ctx, hv, s->wo.d_hi, s->wo.d_lo, s->wo.ldw, s->d_bo, y, s->out, (int)rin, s->out, hv,
+                           KERNIX_ACT_NONE, 0.0f, im->status, st);
+    }
+    case KERNIX_OP_LSTM:
+    case KERNIX_OP_GRU:
+    case KERNIX_OP_RNN:
+        fprintf(stderr, "forward: LSTM/GRU/RNN steps are not implemented on the B200 path\n");
+        return -1;
+    default:
+        return -1;
+    }
+}
+
+static const char* kind_name(int k) {
+    static const char* names[] = {"LINEAR", "ACT", "LAYERNORM", "SOFTMAX", "LSTM", "GRU", "RNN", "CONV", "POOL",
+                                  "GLOBAL_POOL", "RESHAPE", "PERMUTE", "BINARY", "CONCAT", "EMBEDDING", "AFFINE",
+                                  "ADD_CONST", "ATTENTION", "SELECT", "PAD", "UPSAMPLE"};
+    return k >= 0 && k <= KERNIX_OP_LAST ? names[k] : "?";
+}
+
+static int chunk_run(kernix_model* m, int B) {
+    for (int i = 0; i < m->impl->g->n_steps; i++)
+        if (step_run(m, i, B) != 0) {
+            fprintf(stderr, "forward: step %d (%s) failed to launch: %s\n", i, kind_name(m->impl->g->steps[i].kind),
+                    cudaGetErrorString(cudaGetLastError()));
+            return -1;
+        }
+    return 0;
+}
+
+/* Enqueue the forward of rows of x into out (samples x out_dim) on im->stream. x / out are host memory
+ * (copied per chunk) or, with on_device, device memory (the first chunk's input is read in place). */
+static int forward_enqueue(kernix_model* m, const float* x, int rows, float* out, int on_device) {
+    struct kx_model_impl* im = m->impl;
+    const int samples = rows / m->seq_len;
+    if (samples == 0) return 0;
+    int chunk = samples;
+    if (m->ws_limit > 0 && m->ws_per_sample > 0) {
+        const size_t fixed = m->ws_fixed * sizeof(float), avail = m->ws_limit > fixed ? m->ws_limit - fixed : 0;
+        size_t c = avail / (m->ws_per_sample * sizeof(float));
+        if (c < 1) c = 1;
+        if (c < (size_t)samples) chunk = (int)c;
+    }
+    const int crow = chunk * m->seq_len;
+    if (crow != m->batch && model_alloc(m, crow) != 0) return -1;
+    cudaStream_t st = im->stream;
+    const float* yv = val_ptr(im, im->g->out_v);
+    const enum cudaMemcpyKind h2d = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    const enum cudaMemcpyKind d2h = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+    float* const xin_own = im->xin;
+    for (int s0 = 0; s0 < samples; s0 += chunk) {
+        const int n = samples - s0 < chunk ? samples - s0 : chunk;
+        const size_t in_floats = (size_t)n * m->seq_len * m->in_dim;
+        const float* src = x + (size_t)s0 * m->seq_len * m->in_dim;
+        int rc;
+        const float* yc = yv;
+        if (on_device) { /* the model input is never written (the plan keeps it read-only): read it in place */
+            im->xin = (float*)src;
+            rc = chunk_run(m, n);
+            yc = val_ptr(im, im->g->out_v); /* the input itself when the graph is only views of it */
+            im->xin = xin_own;
+        } else {
+            if (cudaMemcpyAsync(im->xin, src, in_floats * sizeof(float), h2d, st) != cudaSuccess) return -1;
+            rc = chunk_run(m, n);
+        }
+        if (rc != 0) return -1;
+        if (cudaMemcpyAsync(out + (size_t)s0 * m->out_dim, yc, (size_t)n * m->out_dim * sizeof(float), d2h, st) !=
+            cudaSuccess)
+            return -1;
+    }
+    return 0;
+}
+
+/* host-memory forward: enqueue, then wait and check the status word */
+static int forward_into(kernix_model* m, const float* x, int rows, float* out) {
+    struct kx_model_impl* im = m->impl;
+    if (rows / m->seq_len == 0) return 0;
+    cudaStream_t st = im->stream;
+    if (m->batch > 0 && cudaMemsetAsync(im->status, 0, sizeof(int), st) != cudaSuccess) return -1;
+    if (forward_enqueue(m, x, rows, out, 0) != 0) return -1;
+    if (m->batch <= 0) return -1;
+    cudaMemcpyAsync(im->status_h, im->status, sizeof(int), cudaMemcpyDeviceToHost, st);
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "forward: CUDA error %s\n", cudaGetErrorString(e));
+        return -1;
+    }
+    if (*im->status_h != KX_STATUS_OK) {
+        fprintf(stderr, "forward: a kernel gave up waiting (status %d)\n", *im->status_h);
+        cudaMemsetAsync(im->status, 0, sizeof(int), st);
+        return -1;
+    }
+    return 0;
+}
+
+/* workspace floats per sample: storage buffers, input rows, step scratch */
+static size_t ws_count(kernix_model* m) {
+    kx_graph* g = m->impl->g;
+    size_t n = 0;
+    for (int k = 0; k < g->n_st; k++) n += g->st_cap[k];
+    n += (size_t)m->seq_len * m->in_dim;
+    size_t mx = 0;
+    for (int i = 0; i < g->n_steps; i++) {
+        size_t ps;
+        step_scratch(g, &g->steps[i], &ps);
+        if (ps > mx) mx = ps;
+    }
+    m->impl->scratch_per_row_max = mx;
+    return n + (mx + 3) / 4;
+}
+
+/* ------------------------------------------------------------------------------------ public API */
+KERNIX_API kernix_model* kernix_model_load(const char* path) {
+    const char* err = NULL;
+    kx_graph* g = kx_graph_load(path, &err);
+    if (g == NULL) {
+        fprintf(stderr, "model load failed (%s): %s\n", path ? path : "NULL", err);
+        return NULL;
+    }
+    kernix_model* m = calloc(1, sizeof *m);
+    struct kx_model_impl* im = calloc(1, sizeof *im);
+    if (m == NULL || im == NULL) {
+        free(m);
+        free(im);
+        kx_graph_free(g);
+        fprintf(stderr, "model load failed (%s): out of memory\n", path);
+        return NULL;
+    }
+    m->impl = im;
+    im->g = g;
+    m->batch = -1;
+    const kx_val* vin = &g->vals[0];
+    const kx_val* vout = &g->vals[g->out_v];
+    m->n_steps = g->n_steps;
+    m->in_dim = vin->c;
+    m->seq_len = vin->r;
+    m->out_dim = vout->r * vout->c;
+    m->in_nd = vin->nd;
+    memcpy(m->in_shape, vin->d, sizeof m->in_shape);
+    m->out_nd = vout->nd;
+    memcpy(m->out_shape, vout->d, sizeof m->out_shape);
+    m->layout = g->layout;
+    m->ws_limit = KERNIX_WORKSPACE_LIMIT;
+    m->ws_fixed = 0;
+    m->ws_per_sample = ws_count(m);
+
+    const char* env = getenv("KERNIX_DEVICE");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    im->device = env && *env ? atoi(env) : (prev >= 0 ? prev : 0);
+    const char* why = NULL;
+    if (cudaSetDevice(im->device) != cudaSuccess) why = "no CUDA device";
+    else if (cudaStreamCreateWithFlags(&im->stream, cudaStreamNonBlocking) != cudaSuccess) why = "cannot create a CUDA stream";
+    else if (cudaHostAlloc((void**)&im->status_h, sizeof(int), cudaHostAllocDefault) != cudaSuccess) why = "cannot allocate host memory";
+    for (int i = 0; why == NULL && i < g->n_steps; i++)
+        if (step_upload(g, &g->steps[i], im->stream) != 0) why = "cannot copy the weights to the GPU";
+    if (prev >= 0 && prev != im->device) cudaSetDevice(prev);
+    if (why != NULL) {
+        fprintf(stderr, "model load failed (%s): %s (%s)\n", path, why, cudaGetErrorString(cudaGetLastError()));
+        kernix_model_free(m);
+        return NULL;
+    }
+    /* weights live on the device now: drop the file mapping and dequantised host copies */
+    for (int i = 0; i < g->n_steps; i++) {
+        kx_step* s = &g->steps[i];
+        kx_weight* ws[4] = {&s->w, &s->wk, &s->wv, &s->wo};
+        for (int k = 0; k < 4; k++) {
+            free(ws[k]->own);
+            ws[k]->own = NULL;
+            ws[k]->f = NULL;
+            ws[k]->q = NULL;
+            ws[k]->scale_h = NULL;
+        }
+        s->bias = s->bk = s->bv = s->bo = s->gamma = s->beta = s->cst = NULL;
+    }
+    return m;
+}
+
+KERNIX_API void kernix_model_free(kernix_model* m) {
+    if (m == NULL) return;
+    struct kx_model_impl* im = m->impl;
+    if (im != NULL) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(im->device);
+        if (im->stream) cudaStreamSynchronize(im->stream);
+        model_release(m);
+        if (im->g != NULL)
+            for (int i = 0; i < im->g->n_steps; i++) step_dev_free(&im->g->steps[i]);
+        if (im->status_h) cudaFreeHost(im->status_h);
+        if (im->stream) cudaStreamDestroy(im->stream);
+        kx_graph_free(im->g);
+        if (prev >= 0) cudaSetDevice(prev);
+        free(im);
+    }
+    free(m);
+}
+
+KERNIX_API void kernix_model_trim(kernix_model* m) {
+    if (m == NULL) return;
+    int prev;
+    if (dev_guard_enter(m, &prev) != 0) return;
+    cudaStreamSynchronize(m->impl->stream);
+    model_release(m);
+    dev_guard_leave(m, prev);
+}
+
+KERNIX_API void kernix_model_set_workspace_limit(kernix_model* m, size_t bytes) {
+    if (m != NULL) m->ws_limit = bytes;
+}
+
+KERNIX_API int kernix_model_set_ane(kernix_model* m, int on) {
+    if (m == NULL) return -1;
+    return on ? -1 : 0;
+}
+
+KERNIX_API void kernix_model_ane_info(const kernix_model* m, kernix_ane_info* out) {
+    (void)m;
+    if (out) memset(out, 0, sizeof *out);
+}
+
+KERNIX_API const float_tensor* kernix_model_forward(kernix_model* m, const float_tensor* x) {
+    if (m == NULL || x == NULL || x->tensor == NULL || x->row < 0 || x->col != m->in_dim || x->row % m->seq_len != 0)
+        return NULL;
+    struct kx_model_impl* im = m->impl;
+    if (im->out_host != NULL && x->tensor == im->out_host) {
+        fprintf(stderr, "forward: this model's output buffer cannot be its own input (copy it first)\n");
+        return NULL;
+    }
+    const int samples = x->row / m->seq_len;
+    const size_t need = (size_t)samples * m->out_dim;
+    int prev;
+    if (dev_guard_enter(m, &prev) != 0) return NULL;
+    if (need > im->out_host_floats || im->out_host == NULL) {
+        if (im->out_host) cudaFreeHost(im->out_host);
+        im->out_host = NULL;
+        im->out_host_floats = 0;
+        if (cudaHostAlloc((void**)&im->out_host, need ? need * sizeof(float) : 4, cudaHostAllocDefault) != cudaSuccess) {
+            im->out_host = NULL;
+            dev_guard_leave(m, prev);
+            return NULL;
+        }
+        im->out_host_floats = need;
+    }
+    const int rc = forward_into(m, x->tensor, x->row, im->out_host);
+    dev_guard_leave(m, prev);
+    if (rc != 0) return NULL;
+    im->out_t.row = samples;
+    im->out_t.col = m->out_dim;
+    im->out_t.tensor = im->out_host;
+    return &im->out_t;
+}
+
+/* ------------------------------------------------------------------------ device-memory forward */
+KERNIX_API int kernix_model_forward_device(kernix_model* m, const float* d_x, int rows, float* d_out, void* stream) {
+    if (m == NULL || d_x == NULL || d_out == NULL || rows <= 0 || rows % m->seq_len != 0) return -1;
+    struct kx_model_impl* im = m->impl;
+    int prev;
+    if (dev_guard_enter(m, &prev) != 0) return -1;
+    cudaStream_t own = im->stream;
+    if (stream != NULL) im->stream = (cudaStream_t)stream;
+    const int rc = forward_enqueue(m, d_x, rows, d_out, 1);
+    im->stream = own;
+    dev_guard_leave(m, prev);
+    return rc;
+}
+
+KERNIX_API int kernix_model_check(kernix_model* m) {
+    if (m == NULL || m->impl->status == NULL) return 0;
+    int prev, v = 0;
+    if (dev_guard_enter(m, &prev) != 0) return -1;
+    if (cudaMemcpy(&v, m->impl->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) v = -1;
+    if (v != 0) cudaMemset(m->impl->status, 0, sizeof(int));
+    dev_guard_leave(m, prev);
+    return v == 0 ? 0 : -1;
+}
+
+/* -------------------------------------------------------------------------------- C ABI (capi) */
+KERNIX_API void* kernix_capi_load(const char* path) { return kernix_model_load(path); }
+KERNIX_API void kernix_capi_free(void* m) { kernix_model_free((kernix_model*)m); }
+KERNIX_API void kernix_capi_trim(void* m) { kernix_model_trim((kernix_model*)m); }
+KERNIX_API void kernix_capi_set_workspace_limit(void* m, size_t bytes) { kernix_model_set_workspace_limit((kernix_model*)m, bytes); }
+
+KERNIX_API void kernix_capi_dims(const void* mv, int* in_dim, int* out_dim, int* seq_len) {
+    const kernix_model* m = (const kernix_model*)mv;
+    *in_dim = m->in_dim;
+    *out_dim = m->out_dim;
+    *seq_len = m->seq_len;
+}
+
+KERNIX_API int kernix_capi_forward(void* mv, const float* x, int rows, float* out) {
+    kernix_model* m = (kernix_model*)mv;
+    if (m == NULL || x == NULL || out == NULL || rows <= 0 || rows % m->seq_len != 0) return -1;
+    int prev;
+    if (dev_guard_enter(m, &prev) != 0) return -1;
+    const int rc = forward_into(m, x, rows, out);
+    dev_guard_leave(m, prev);
+    return rc;
+}
+
+KERNIX_API int kernix_capi_set_ane(void* m, int on) { return kernix_model_set_ane((kernix_model*)m, on); }
+
+KERNIX_API void kernix_capi_ane_info(const void* m, int* out) {
+    (void)m;
+    out[0] = out[1] = out[2] = out[3] = 0;
+}
+
+KERNIX_API int kernix_capi_ane_dump(const void* m, int seg, int batch, const char* path) {
+    (void)m; (void)seg; (void)batch; (void)path;
+    return -1;
+}
+
+KERNIX_API void kernix_capi_shapes(const void* mv, int* in_nd, int* in_shape, int* out_nd, int* out_shape, int* layout) {
+    const kernix_model* m = (const kernix_model*)mv;
+    *in_nd = m->in_nd;
+    *out_nd = m->out_nd;
+    *layout = m->layout;
+    for (int k = 0; k < KERNIX_MAX_DIMS; k++) {
+        in_shape[k] = m->in_shape[k];
+        out_shape[k] = m->out_shape[k];
+    }
+}
+
+/* -------------------------------------------------------------------------------- kernix.h extras */
+KERNIX_API void float_free(float_tensor* t) {
+    if (t == NULL) return;
+    free(t->tensor);
+    free(t);
+}
+
+KERNIX_API float_tensor* floats_fma_relu(const float_tensor* a, const float_tensor* x, const float_tensor* b) {
+    if (a == NULL || x == NULL || b == NULL || a->tensor == NULL || x->tensor == NULL || b->tensor == NULL ||
+        a->row != x->row || a->col != x->col || b->row != x->row || b->col != x->col || x->row < 0 || x->col < 0)
+        return NULL;
+    const size_t n = (size_t)x->row * (size_t)x->col, np = round_up(n ? n : 1, 4); /* planes 16-byte aligned */
+    float_tensor* y = malloc(sizeof *y);
+    if (y == NULL) return NULL;
+    y->row = x->row;
+    y->col = x->col;
+    y->tensor = malloc(np * sizeof(float));
+    float* d = NULL;
+    int ok = y->tensor != NULL && cudaMalloc((void**)&d, 4 * np * sizeof(float)) == cudaSuccess;
+    if (ok && n) {
+        ok = cudaMemcpy(d, a->tensor, n * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(d + np, x->tensor, n * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(d + 2 * np, b->tensor, n * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+             kx_fma_relu(d, d + np, d + 2 * np, d + 3 * np, n, NULL) == 0 && cudaDeviceSynchronize() == cudaSuccess &&
+             cudaMemcpy(y->tensor, d + 3 * np, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    cudaFree(d);
+    if (!ok) {
+        float_free(y);
+        return NULL;
+    }
+    return y;
+}

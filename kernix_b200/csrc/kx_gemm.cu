@@ -1,0 +1,647 @@
+// KERNIX-B200 dense GEMMs on the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
+//
+//  * kx_gemm_i8   : int8 x int8 -> int32 (kind::i8) with the dequant / bias / activation epilogue of the
+//                   reference's kernix_qmatmul (include/kernix_model.h:143-177) and the LINEAR step's
+//                   activation (:1854-1856). Operands: A = per-row quantised activations [M][lda] int8,
+//                   B = weights [N][ldb] int8 (K-major, transposed from the file's in x out q at load).
+//  * kx_gemm_f32  : fp32 GEMM in 3xTF32 split precision with fused bias + activation, replacing
+//                   kernix_dense -> kernix_matmul_ep_into (include/kernix_model.h:544-550,
+//                   include/kernix.h:955-976, src/kernix_metal.m:161-265). A is read from global memory by
+//                   converter warps that split every value into a tf32 "hi" part (rounded to 10 mantissa
+//                   bits) and the exact remainder "lo", written into swizzled shared memory; B arrives
+//                   pre-split (hi/lo planes, [N][ldb] K-major) by TMA. Each K step issues
+//                   hi*hi + hi*lo + lo*hi into one fp32 TMEM accumulator.
+//
+// CTA layout (one 128 x BN output tile per CTA):
+//   warp 0      TMA producer (elected lane)
+//   warp 1      TMEM allocator + MMA issuer (elected lane)
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31), then
+//               dequant/bias/act and global stores
+//   warps 6-9   (3xTF32 only) A converters
+// Shared memory holds STAGES operand stages in the canonical K-major 128-byte-swizzle layout; full/empty
+// mbarriers form the ring. Every wait is bounded (kx_sm100.cuh); a timeout sets the status word, the CTA
+// drains its in-flight copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <climits>
+#include <mutex>
+
+#include "kx_act.cuh"
+#include "kx_kernels.h"
+#include "kx_sm100.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// bounded wait that ignores the abort flag: used to drain work already issued before leaving the CTA
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = kx::globaltimer();
+    while (!kx::mbar_try_wait(bar, parity)) {
+        if (kx::globaltimer() - t0 > KX_WAIT_NS) return;
+        __nanosleep(128);
+    }
+}
+
+struct SmemCtl {
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t accf;
+    uint32_t tmem;
+    int abort;
+};
+
+// epilogue store of 32 consecutive columns of one row
+__device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], int ncols_valid, bool vec_ok) {
+    if (vec_ok && ncols_valid >= 32) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 8; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+            if (j < ncols_valid) dst[j] = v[j];
+    }
+}
+
+// ------------------------------------------------------------------------------------------ int8
+template <int BN, int STAGES>
+struct I8Cfg {
+    static constexpr int BK = 128;  // bytes of K per stage (one 128-byte swizzle row)
+    static constexpr int A_BYTES = BM * BK;
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 + static_cast<int>(sizeof(SmemCtl));
+    static constexpr uint32_t TMEM_COLS = BN;
+};
+
+template <int BN, int STAGES, bool ACC_ONLY>
+__global__ void __launch_bounds__(192, 1)
+k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+          const float* __restrict__ sx, const float* __restrict__ scale, const float* __restrict__ bias,
+          float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N, int K, int act, float alpha,
+          int* status) {
+    using C = I8Cfg<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(sB + STAGES * C::B_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nk = (K + C::BK - 1) / C::BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1);
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        kx::tmem_alloc(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish();
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmA);
+            kx::tma_prefetch_desc(&tmB);
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                kx::mbar_arrive_expect_tx(&ctl->full[s], C::A_BYTES + C::B_BYTES);
+                kx::tma_load_2d(sA + s * C::A_BYTES, &tmA, kb * C::BK, m0, &ctl->full[s]);
+                kx::tma_load_2d(sB + s * C::B_BYTES, &tmB, kb * C::BK, n0, &ctl->full[s]);
+                issued = kb + 1;
+            }
+            if (*abort_flag)  // let copies already in flight land before the CTA's shared memory goes away
+                for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
+                    drain_wait(&ctl->full[kb % STAGES], (kb / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = kx::idesc_i8(BM, BN);
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                if (!kx::mbar_wait(&ctl->full[s], (kb / STAGES) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t a0 = kx::smem_u32(sA + s * C::A_BYTES), b0 = kx::smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < C::BK / 32; kk++)
+                    kx::mma_i8(tmem, kx::desc_sw128_kmajor(a0 + kk * 32), kx::desc_sw128_kmajor(b0 + kk * 32), idesc,
+                               (kb | kk) != 0);
+                kx::mma_commit(&ctl->empty[s]);
+            }
+            kx::mma_commit(&ctl->accf);  // arrives once every MMA above has completed
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        const bool ok = !*abort_flag;
+        const float sxr = (ok && row < M && !ACC_ONLY) ? sx[row] : 0.0f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            kx::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+            kx::tmem_ld_wait();
+            const int col = n0 + c0;
+            if (!ok || row >= M || col >= N) continue;
+            const int nv = N - col;
+            if (ACC_ONLY) {
+                int32_t* dst = acc_out + static_cast<size_t>(row) * ldy + col;
+                for (int j = 0; j < 32; j++)
+                    if (j < nv) dst[j] = static_cast<int32_t>(r[j]);
+            } else {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const int cc = col + (j < nv ? j : 0);
+                    float t = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sxr), __ldg(scale + cc));
+                    t = __fadd_rn(t, bias ? __ldg(bias + cc) : 0.0f);
+                    v[j] = kx::act_apply(act, t, alpha);
+                }
+                float* dst = y + static_cast<size_t>(row) * ldy + col;
+                store_row32(dst, v, nv, ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0));
+            }
+        }
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------------ 3xTF32
+template <int BN, int STAGES>
+struct F32Cfg {
+    static constexpr int BK = 32;  // fp32 elements of K per stage (128 bytes per row)
+    static constexpr int A_BYTES = BM * BK * 4;
+    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // A hi, A lo, B hi, B lo
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + static_cast<int>(sizeof(SmemCtl));
+    static constexpr uint32_t TMEM_COLS = BN;
+};
+
+// split v into hi (v rounded to tf32: 10 explicit mantissa bits, ties away from zero) and lo = v - hi (exact)
+__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
+    const uint32_t b = __float_as_uint(v);
+    if ((b & 0x7F800000u) == 0x7F800000u) {  // inf / nan pass through unchanged
+        hi = v;
+        lo = 0.0f;
+        return;
+    }
+    hi = __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+    lo = __fsub_rn(v, hi);
+}
+
+// Implicit-GEMM convolution geometry: output row m = (b, oy, ox), reduction index k = (ky, kx, ci) with ci
+// fastest, matching the file's weight row order (tools/knx3.py:93-104). Group g = blockIdx.z reads input
+// channels [g*cg, (g+1)*cg) and writes output channels [g*cog, (g+1)*cog).
+struct ConvGeom {
+    int H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog;
+};
+
+template <int BN, int STAGES, bool CONV>
+__global__ void __launch_bounds__(320, 1)
+k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
+              const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
+              int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv) {
+    using C = F32Cfg<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + STAGES * C::STAGE_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    auto sAhi = [&](int s) { return smem + s * C::STAGE_BYTES; };
+    auto sAlo = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto sBhi = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::A_BYTES; };
+    auto sBlo = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nk = (K + C::BK - 1) / C::BK;
+    const int grp = CONV ? static_cast<int>(blockIdx.z) : 0;
+    const int brow0 = grp * (CONV ? cv.cog : 0);  // first weight row / output column of this group
+    if (CONV) {
+        A += grp * cv.cg;
+        y += brow0;
+        if (bias) bias += brow0;
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1 + 4);  // TMA producer + 4 converter warps
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        kx::tmem_alloc(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish();
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmBhi);
+            kx::tma_prefetch_desc(&tmBlo);
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * C::B_BYTES);
+                kx::tma_load_2d(sBhi(s), &tmBhi, kb * C::BK, brow0 + n0, &ctl->full[s]);
+                kx::tma_load_2d(sBlo(s), &tmBlo, kb * C::BK, brow0 + n0, &ctl->full[s]);
+                issued = kb + 1;
+            }
+            if (*abort_flag)
+                for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
+                    drain_wait(&ctl->full[kb % STAGES], (kb / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = kx::idesc_tf32(BM, BN);
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                if (!kx::mbar_wait(&ctl->full[s], (kb / STAGES) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t ah = kx::smem_u32(sAhi(s)), al = kx::smem_u32(sAlo(s));
+                const uint32_t bh = kx::smem_u32(sBhi(s)), bl = kx::smem_u32(sBlo(s));
+#pragma unroll
+                for (int kk = 0; kk < C::BK / 8; kk++) {
+                    const uint32_t o = kk * 32;  // 8 tf32 = 32 bytes of K per MMA
+                    kx::mma_tf32(tmem, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
+                    kx::mma_tf32(tmem, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                    kx::mma_tf32(tmem, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
+                }
+                kx::mma_commit(&ctl->empty[s]);
+            }
+            kx::mma_commit(&ctl->accf);
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        const bool ok = !*abort_flag;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            kx::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+            kx::tmem_ld_wait();
+            const int col = n0 + c0;
+            if (!ok || row >= M || col >= N) continue;
+            const int nv = N - col;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int cc = col + (j < nv ? j : 0);
+                float t = __uint_as_float(r[j]);
+                if (bias) t = __fadd_rn(t, __ldg(bias + cc));
+                v[j] = kx::act_apply(act, t, alpha);
+            }
+            store_row32(y + static_cast<size_t>(row) * ldy + col, v, nv,
+                        ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0));
+        }
+    } else {
+        // A converters: warp cw covers tile rows 32*cw .. 32*cw+31; per pass, lanes 8i..8i+7 read one row's
+        // 128 contiguous bytes (coalesced), split, and write the 16-byte chunks to their swizzled places.
+        const int cw = warp - 6;
+        const bool vec = CONV ? ((cv.cg & 3) == 0 && (cv.C & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0)
+                              : (((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0));
+        // conv: per-thread output-row geometry of its 8 rows, computed once
+        long rbase[8];
+        int iy0[8], ix0[8];
+        if (CONV) {
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+                const int gm = m0 + cw * 32 + it * 4 + (lane >> 3);
+                const int hw = cv.Ho * cv.Wo;
+                const int b = gm / hw, rem = gm - b * hw, oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+                rbase[it] = static_cast<long>(b) * cv.H;
+                iy0[it] = oy * cv.sh - cv.pt;
+                ix0[it] = ox * cv.sw - cv.pl;
+            }
+        }
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % STAGES;
+            if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
+            const int k0 = kb * C::BK;
+            const int gk = k0 + (lane & 7) * 4;
+            int ky = 0, kx2 = 0, ci = 0;
+            if (CONV && gk < K) {
+                const int tap = gk / cv.cg;
+                ci = gk - tap * cv.cg;
+                ky = tap / cv.kw;
+                kx2 = tap - ky * cv.kw;
+            }
+            float4 v[8];
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+                const int r = cw * 32 + it * 4 + (lane >> 3);
+                const int gm = m0 + r;
+                float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (gm < M && gk < K) {
+                    if (!CONV) {
+                        const float* src = A + static_cast<size_t>(gm) * lda + gk;
+                        if (vec && gk + 3 < K) {
+                            t = __ldg(reinterpret_cast<const float4*>(src));
+                        } else {
+                            t.x = __ldg(src);
+                            if (gk + 1 < K) t.y = __ldg(src + 1);
+                            if (gk + 2 < K) t.z = __ldg(src + 2);
+                            if (gk + 3 < K) t.w = __ldg(src + 3);
+                        }
+                    } else if (vec) {  // 4 consecutive channels of one tap
+                        const int iy = iy0[it] + ky * cv.dh, ix = ix0[it] + kx2 * cv.dw;
+                        if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
+                            t = __ldg(reinterpret_cast<const float4*>(A + ((rbase[it] + iy) * cv.W + ix) * cv.C + ci));
+                    } else {  // channels per group not a multiple of 4: element by element
+                        float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const int kq = gk + q;
+                            if (kq >= K) break;
+                            const int tap = kq / cv.cg, c = kq - tap * cv.cg, yy = tap / cv.kw, xx = tap - yy * cv.kw;
+                            const int iy = iy0[it] + yy * cv.dh, ix = ix0[it] + xx * cv.dw;
+                            if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
+                                e[q] = __ldg(A + ((rbase[it] + iy) * cv.W + ix) * cv.C + c);
+                        }
+                        t = make_float4(e[0], e[1], e[2], e[3]);
+                    }
+                }
+                v[it] = t;
+            }
+            uint8_t* hi = sAhi(s);
+            uint8_t* lo = sAlo(s);
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+                const int r = cw * 32 + it * 4 + (lane >> 3);
+                const int j = lane & 7;
+                const int off = r * 128 + ((j ^ (r & 7)) << 4);
+                float4 h, l;
+                tf32_split(v[it].x, h.x, l.x);
+                tf32_split(v[it].y, h.y, l.y);
+                tf32_split(v[it].z, h.z, l.z);
+                tf32_split(v[it].w, h.w, l.w);
+                *reinterpret_cast<float4*>(hi + off) = h;
+                *reinterpret_cast<float4*>(lo + off) = l;
+            }
+            kx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) kx::mbar_arrive(&ctl->full[s]);
+        }
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------- host side
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled_t encode_fn() {
+    static PFN_encodeTiled_t fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+    });
+    return fn;
+}
+
+// 2-D row-major tensor [outer][inner] with row pitch row_bytes; box box_inner x box_outer; 128-byte swizzle
+struct MapKey {
+    const void* base;
+    uint64_t inner, outer, row_bytes;
+    uint32_t box_inner, box_outer;
+    int dt;
+};
+
+struct MapEntry {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+};
+
+thread_local MapEntry t_maps[64];
+
+bool same_key(const MapKey& a, const MapKey& b) { return std::memcmp(&a, &b, sizeof(MapKey)) == 0; }
+
+int make_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+    MapKey k;
+    std::memset(&k, 0, sizeof k);
+    k.base = base; k.inner = inner; k.outer = outer; k.row_bytes = row_bytes;
+    k.box_inner = box_inner; k.box_outer = box_outer; k.dt = static_cast<int>(dt);
+    const size_t h = (reinterpret_cast<uintptr_t>(base) >> 8 ^ inner * 31 ^ outer * 131 ^ box_outer) & 63;
+    if (t_maps[h].used && same_key(t_maps[h].key, k)) {
+        *out = t_maps[h].map;
+        return 0;
+    }
+    PFN_encodeTiled_t enc = encode_fn();
+    if (enc == nullptr) return -1;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) return -1;  // TMA alignment rules
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    if (enc(out, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return -1;
+    t_maps[h].key = k;
+    t_maps[h].map = *out;
+    t_maps[h].used = true;
+    return 0;
+}
+
+// raise the dynamic shared-memory limit of a kernel once per device (the attribute is per device context)
+template <typename Kern>
+int set_smem_once(Kern k, int bytes) {
+    static uint64_t done = 0;  // bit d: done on device d
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    std::lock_guard<std::mutex> g(mu);
+    if (dev < 64 && (done >> dev) & 1) return 0;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -1;
+    if (dev < 64) done |= uint64_t(1) << dev;
+    return 0;
+}
+
+template <int BN, bool ACC_ONLY>
+int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
+              const float* bias, float* y, int32_t* acc, int ldy, int m, int n, int k, int act, float alpha, int* status,
+              cudaStream_t st) {
+    constexpr int STAGES = 4;
+    using C = I8Cfg<BN, STAGES>;
+    CUtensorMap ta, tb;
+    if (make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, static_cast<uint64_t>(ldq), static_cast<uint64_t>(m),
+                    static_cast<uint64_t>(ldq), C::BK, BM) != 0 ||
+        make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, static_cast<uint64_t>(ldw), static_cast<uint64_t>(n),
+                    static_cast<uint64_t>(ldw), C::BK, BN) != 0)
+        return -1;
+    auto kern = k_gemm_i8<BN, STAGES, ACC_ONLY>;
+    if (set_smem_once(kern, C::SMEM) != 0) return -1;
+    dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
+    kern<<<grid, 192, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <int BN, bool CONV>
+int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
+               int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
+               int groups) {
+    constexpr int STAGES = BN == 256 ? 2 : 3;
+    using C = F32Cfg<BN, STAGES>;
+    CUtensorMap th, tl;
+    if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BN) != 0 ||
+        make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BN) != 0)
+        return -1;
+    auto kern = k_gemm_tf32x3<BN, STAGES, CONV>;
+    if (set_smem_once(kern, C::SMEM) != 0) return -1;
+    dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
+    kern<<<grid, 320, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ---------------------------------------------------------------------------- weight preparation
+// q_kn: k x n int8 row-major (in x out, the file's order) -> wq: n x ldw (K-major), zero padded
+__global__ void k_prep_i8(const int8_t* __restrict__ q, int k, int n, int8_t* __restrict__ wq, int ldw) {
+    __shared__ int8_t tile[32][33];
+    const int kb = blockIdx.x * 32, nb = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int kk = kb + i, nn = nb + threadIdx.x;
+        tile[i][threadIdx.x] = (kk < k && nn < n) ? q[static_cast<size_t>(kk) * n + nn] : 0;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int nn = nb + i, kk = kb + threadIdx.x;
+        if (nn < n && kk < ldw) wq[static_cast<size_t>(nn) * ldw + kk] = tile[threadIdx.x][i];
+    }
+}
+
+// w_kn: k x n fp32 -> hi, lo: n x ldw (K-major) tf32 split planes, zero padded
+__global__ void k_prep_f32(const float* __restrict__ w, int k, int n, float* __restrict__ hi, float* __restrict__ lo,
+                           int ldw) {
+    __shared__ float tile[32][33];
+    const int kb = blockIdx.x * 32, nb = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int kk = kb + i, nn = nb + threadIdx.x;
+        tile[i][threadIdx.x] = (kk < k && nn < n) ? w[static_cast<size_t>(kk) * n + nn] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int nn = nb + i, kk = kb + threadIdx.x;
+        if (nn < n && kk < ldw) {
+            float h, l;
+            tf32_split(tile[threadIdx.x][i], h, l);
+            hi[static_cast<size_t>(nn) * ldw + kk] = h;
+            lo[static_cast<size_t>(nn) * ldw + kk] = l;
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
+               const float* bias, float* y, int ldy, int m, int n, int k, int act, float alpha, int* status,
+               void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15)) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n <= 128)
+        return launch_i8<128, false>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+    return launch_i8<256, false>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+}
+
+int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
+                   int* status, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15)) return -1;
+    return launch_i8<256, true>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, acc, ldacc, m, n, k, -1, 0.0f,
+                                status, static_cast<cudaStream_t>(stream));
+}
+
+int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
+                int ldy, int m, int n, int k, int act, float alpha, int* status, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldx || k > ldw || (ldw & 3)) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const ConvGeom cv{};
+    if (n <= 128) return launch_f32<128, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
+    return launch_f32<256, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
+}
+
+int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y, int B, int H,
+                int W, int C, int Co, int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl,
+                int groups, int act, float alpha, int* status, void* stream) {
+    if (B <= 0) return 0;
+    if (groups < 1 || C % groups || Co % groups || (ldw & 3)) return -1;
+    const long m = static_cast<long>(B) * Ho * Wo;
+    const int cg = C / groups, cog = Co / groups, k = kh * kw * cg;
+    if (m > INT32_MAX || k > ldw) return -1;
+    const ConvGeom cv{H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cog <= 128)
+        return launch_f32<128, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status, st,
+                                     cv, groups);
+    return launch_f32<256, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status, st,
+                                 cv, groups);
+}
+
+int kx_prep_i8_weight(const int8_t* q_kn, int k, int n, int8_t* wq, int ldw, void* stream) {
+    if (k <= 0 || n <= 0 || ldw < k) return -1;
+    dim3 grid((ldw + 31) / 32, (n + 31) / 32), block(32, 8);
+    k_prep_i8<<<grid, block, 0, static_cast<cudaStream_t>(stream)>>>(q_kn, k, n, wq, ldw);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int kx_prep_f32_weight(const float* w_kn, int k, int n, float* w_hi, float* w_lo, int ldw, void* stream) {
+    if (k <= 0 || n <= 0 || ldw < k) return -1;
+    dim3 grid((ldw + 31) / 32, (n + 31) / 32), block(32, 8);
+    k_prep_f32<<<grid, block, 0, static_cast<cudaStream_t>(stream)>>>(w_kn, k, n, w_hi, w_lo, ldw);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // extern "C"

@@ -1,0 +1,744 @@
+// KERNIX-B200 memory-bound graph ops, the int8 row quantiser, depthwise conv, attention core and fma_relu.
+// Each kernel restates one reference computation (named on its kx_* entry in include/kx_kernels.h) with
+// coalesced, vectorised (float4) accesses; row ops use one warp per row up to 1024 columns and one
+// 256-thread block per row above that.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cmath>
+#include <cstdint>
+
+#include "kx_act.cuh"
+#include "kx_kernels.h"
+
+namespace {
+
+inline int launch_ok() { return cudaGetLastError() == cudaSuccess ? 0 : -1; }
+
+inline unsigned grid_for(long n, int per_block) {
+    long g = (n + per_block - 1) / per_block;
+    if (g > 148L * 64) g = 148L * 64;  // grid-stride loops above this
+    return static_cast<unsigned>(g < 1 ? 1 : g);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float u = __shfl_xor_sync(0xffffffffu, v, o);
+        v = u > v ? u : v;
+    }
+    return v;
+}
+__device__ __forceinline__ uint32_t warp_umax(uint32_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------------------------- int8 quantise
+// One 128-thread block per row. max|x| is reduced on the IEEE bit patterns of |x| (non-negative floats order
+// like their bits; NaN > inf > finite), so a NaN anywhere makes the row's max NaN as in the reference.
+constexpr int QT = 128;
+constexpr int QV = 8;  // float4 per thread kept in registers (rows up to 4096 columns in one read)
+
+__global__ void __launch_bounds__(QT) k_quant_rows(const float* __restrict__ x, int ldx, int k, int8_t* __restrict__ xq,
+                                                   int ldq, float* __restrict__ sx) {
+    const long row = blockIdx.x;
+    const float* xr = x + row * ldx;
+    int8_t* qr = xq + row * ldq;
+    const bool vec = ((ldx & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((k & 3) == 0);
+    __shared__ uint32_t red[QT / 32];
+    __shared__ float s_inv;
+    __shared__ float s_sx;
+    float4 v[QV];
+    uint32_t m = 0;
+    const int nvec = vec ? (k >> 2) : 0;
+#pragma unroll
+    for (int i = 0; i < QV; i++) {
+        const int c = threadIdx.x + i * QT;
+        v[i] = c < nvec ? __ldg(reinterpret_cast<const float4*>(xr) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        m = max(m, max(max(__float_as_uint(fabsf(v[i].x)), __float_as_uint(fabsf(v[i].y))),
+                       max(__float_as_uint(fabsf(v[i].z)), __float_as_uint(fabsf(v[i].w)))));
+    }
+    for (int c = threadIdx.x + QV * QT; c < nvec; c += QT) {  // columns beyond the register window
+        const float4 t = __ldg(reinterpret_cast<const float4*>(xr) + c);
+        m = max(m, max(max(__float_as_uint(fabsf(t.x)), __float_as_uint(fabsf(t.y))),
+                       max(__float_as_uint(fabsf(t.z)), __float_as_uint(fabsf(t.w)))));
+    }
+    if (!vec)
+        for (int c = threadIdx.x; c < k; c += QT) m = max(m, __float_as_uint(fabsf(__ldg(xr + c))));
+    m = warp_umax(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t mm = red[0];
+        for (int i = 1; i < QT / 32; i++) mm = max(mm, red[i]);
+        const float mf = __uint_as_float(mm);
+        if (mm >= 0x7F800000u) {  // NaN or infinite: the whole output row is NaN
+            s_sx = __uint_as_float(0x7FC00000u);
+            s_inv = 0.0f;
+        } else {
+            const float sxv = mf > 0.0f ? __fdiv_rn(mf, 127.0f) : 1.0f;
+            s_sx = sxv;
+            s_inv = __fdiv_rn(1.0f, sxv);
+        }
+        sx[row] = s_sx;
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    auto q1 = [&](float a) -> int {
+        float t = rintf(__fmul_rn(a, inv));
+        t = t > 127.0f ? 127.0f : (t < -127.0f ? -127.0f : t);
+        return t == t ? static_cast<int>(t) : 0;
+    };
+    if (vec) {
+#pragma unroll
+        for (int i = 0; i < QV; i++) {
+            const int c = threadIdx.x + i * QT;
+            if (c < nvec) {
+                char4 o = make_char4(q1(v[i].x), q1(v[i].y), q1(v[i].z), q1(v[i].w));
+                reinterpret_cast<char4*>(qr)[c] = o;
+            }
+        }
+        for (int c = threadIdx.x + QV * QT; c < nvec; c += QT) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(xr) + c);
+            reinterpret_cast<char4*>(qr)[c] = make_char4(q1(t.x), q1(t.y), q1(t.z), q1(t.w));
+        }
+    } else {
+        for (int c = threadIdx.x; c < k; c += QT) qr[c] = static_cast<int8_t>(q1(__ldg(xr + c)));
+    }
+    for (int c = k + threadIdx.x; c < ldq; c += QT) qr[c] = 0;
+}
+
+// ------------------------------------------------------------------------------------ bias + act
+__global__ void k_bias_act(const float* x, float* y, long rows, int cols, const float* __restrict__ bias,
+                           int act, float alpha) {
+    const long n = rows * cols;
+    const bool vec = (cols & 3) == 0;
+    if (vec) {
+        const long n4 = n >> 2;
+        for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n4; i += static_cast<long>(gridDim.x) * blockDim.x) {
+            float4 v = reinterpret_cast<const float4*>(x)[i];
+            const int c = static_cast<int>((i << 2) % cols);
+            if (bias) {
+                v.x = __fadd_rn(v.x, bias[c]);
+                v.y = __fadd_rn(v.y, bias[c + 1]);
+                v.z = __fadd_rn(v.z, bias[c + 2]);
+                v.w = __fadd_rn(v.w, bias[c + 3]);
+            }
+            v.x = kx::act_apply(act, v.x, alpha);
+            v.y = kx::act_apply(act, v.y, alpha);
+            v.z = kx::act_apply(act, v.z, alpha);
+            v.w = kx::act_apply(act, v.w, alpha);
+            reinterpret_cast<float4*>(y)[i] = v;
+        }
+    } else {
+        for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+            float v = x[i];
+            if (bias) v = __fadd_rn(v, bias[i % cols]);
+            y[i] = kx::act_apply(act, v, alpha);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------ rows
+// softmax: m = max (NaN-ignoring compare like vDSP_maxv), e = exp(x - m), s = sum e, y = e * (1/s)
+template <int WARPS>
+__global__ void k_softmax_warp(const float* x, float* y, long rows, int cols) {
+    const long row = blockIdx.x * static_cast<long>(WARPS) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * cols;
+    float* yr = y + row * cols;
+    float m = -INFINITY;
+    for (int c = lane; c < cols; c += 32) {
+        const float v = xr[c];
+        m = v > m ? v : m;
+    }
+    m = warp_max(m);
+    float s = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+        const float e = expf(__fsub_rn(xr[c], m));
+        yr[c] = e;
+        s = __fadd_rn(s, e);
+    }
+    s = warp_sum(s);
+    const float inv = __fdiv_rn(1.0f, s);
+    __syncwarp();
+    for (int c = lane; c < cols; c += 32) yr[c] = __fmul_rn(yr[c], inv);
+}
+
+__global__ void k_softmax_block(const float* x, float* y, int cols) {
+    const long row = blockIdx.x;
+    const float* xr = x + row * cols;
+    float* yr = y + row * cols;
+    __shared__ float red[32];
+    __shared__ float bc;
+    float m = -INFINITY;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float v = xr[c];
+        m = v > m ? v : m;
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float mm = red[0];
+        for (int i = 1; i < static_cast<int>(blockDim.x >> 5); i++) mm = red[i] > mm ? red[i] : mm;
+        bc = mm;
+    }
+    __syncthreads();
+    m = bc;
+    float s = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float e = expf(__fsub_rn(xr[c], m));
+        yr[c] = e;
+        s = __fadd_rn(s, e);
+    }
+    s = warp_sum(s);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float ss = 0.0f;
+        for (int i = 0; i < static_cast<int>(blockDim.x >> 5); i++) ss = __fadd_rn(ss, red[i]);
+        bc = __fdiv_rn(1.0f, ss);
+    }
+    __syncthreads();
+    const float inv = bc;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) yr[c] = __fmul_rn(yr[c], inv);
+}
+
+// layer norm: mean = sum/cols, o = x - mean, rstd = 1/sqrt(sum(o^2)/cols + eps), y = o*rstd*g + b
+template <int WARPS>
+__global__ void k_layernorm_warp(const float* x, float* y, long rows, int cols, const float* __restrict__ g,
+                                 const float* __restrict__ b, float eps) {
+    const long row = blockIdx.x * static_cast<long>(WARPS) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * cols;
+    float* yr = y + row * cols;
+    float s = 0.0f;
+    for (int c = lane; c < cols; c += 32) s = __fadd_rn(s, xr[c]);
+    const float mean = __fdiv_rn(warp_sum(s), static_cast<float>(cols));
+    float ss = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+        const float o = __fsub_rn(xr[c], mean);
+        ss = __fadd_rn(ss, __fmul_rn(o, o));
+    }
+    ss = warp_sum(ss);
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(cols)), eps)));
+    __syncwarp();
+    for (int c = lane; c < cols; c += 32) {
+        float o = __fmul_rn(__fsub_rn(xr[c], mean), rstd);
+        if (g && b) o = __fadd_rn(__fmul_rn(o, g[c]), b[c]);
+        else if (g) o = __fmul_rn(o, g[c]);
+        else if (b) o = __fadd_rn(o, b[c]);
+        yr[c] = o;
+    }
+}
+
+__global__ void k_layernorm_block(const float* x, float* y, int cols, const float* __restrict__ g,
+                                  const float* __restrict__ b, float eps) {
+    const long row = blockIdx.x;
+    const float* xr = x + row * cols;
+    float* yr = y + row * cols;
+    __shared__ float red[32];
+    __shared__ float bc;
+    const int nw = blockDim.x >> 5;
+    float s = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) s = __fadd_rn(s, xr[c]);
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < nw; i++) t = __fadd_rn(t, red[i]);
+        bc = __fdiv_rn(t, static_cast<float>(cols));
+    }
+    __syncthreads();
+    const float mean = bc;
+    float ss = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float o = __fsub_rn(xr[c], mean);
+        ss = __fadd_rn(ss, __fmul_rn(o, o));
+    }
+    ss = warp_sum(ss);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < nw; i++) t = __fadd_rn(t, red[i]);
+        bc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(cols)), eps)));
+    }
+    __syncthreads();
+    const float rstd = bc;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        float o = __fmul_rn(__fsub_rn(xr[c], mean), rstd);
+        if (g && b) o = __fadd_rn(__fmul_rn(o, g[c]), b[c]);
+        else if (g) o = __fmul_rn(o, g[c]);
+        else if (b) o = __fadd_rn(o, b[c]);
+        yr[c] = o;
+    }
+}
+
+// ------------------------------------------------------------------------------ elementwise misc
+__global__ void k_affine(const float* x, float* y, long n, int cols, const float* __restrict__ g,
+                         const float* __restrict__ b) {
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % cols);
+        y[i] = __fadd_rn(__fmul_rn(x[i], g[c]), b[c]);
+    }
+}
+
+__global__ void k_add_const(const float* x, float* y, long n, long per, const float* __restrict__ cst) {
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x)
+        y[i] = __fadd_rn(x[i], cst[i % per]);
+}
+
+__device__ __forceinline__ float bin1(int op, float a, float b) {
+    switch (op) {
+    case 0: return __fadd_rn(a, b);
+    case 1: return __fsub_rn(a, b);
+    case 2: return __fmul_rn(a, b);
+    case 3: return __fdiv_rn(a, b);
+    case 4: return a > b ? a : b;
+    default: return a < b ? a : b;
+    }
+}
+
+__global__ void k_binary(const float* a, int ra, int ca, const float* b, int rb, int cb, float* y,
+                         long samples, int R, int C, int op) {
+    const long n = samples * R * C;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % C);
+        const long rr = i / C;
+        const int r = static_cast<int>(rr % R);
+        const long s = rr / R;
+        const float av = a[(s * ra + (ra == 1 ? 0 : r)) * ca + (ca == 1 ? 0 : c)];
+        const float bv = b[(s * rb + (rb == 1 ? 0 : r)) * cb + (cb == 1 ? 0 : c)];
+        y[i] = bin1(op, av, bv);
+    }
+}
+
+__global__ void k_binary_same4(const float4* a, const float4* b, float4* y, long n4, int op) {
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n4; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const float4 u = a[i], v = b[i];
+        y[i] = make_float4(bin1(op, u.x, v.x), bin1(op, u.y, v.y), bin1(op, u.z, v.z), bin1(op, u.w, v.w));
+    }
+}
+
+// one thread per output (b, oy, ox, c); max starts at -inf, average multiplies by 1/count
+__global__ void k_pool2d(const float* __restrict__ x, float* __restrict__ y, int B, int H, int W, int C, int Ho, int Wo,
+                         int kh, int kw, int sh, int sw, int pt, int pl, int type, int count_pad) {
+    const long n = static_cast<long>(B) * Ho * Wo * C;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % C);
+        long r = i / C;
+        const int ox = static_cast<int>(r % Wo);
+        r /= Wo;
+        const int oy = static_cast<int>(r % Ho);
+        const long b = r / Ho;
+        float acc = type == 0 ? -INFINITY : 0.0f;
+        int cnt = 0;
+        for (int ky = 0; ky < kh; ky++) {
+            const int iy = oy * sh - pt + ky;
+            if (iy < 0 || iy >= H) continue;
+            for (int kx2 = 0; kx2 < kw; kx2++) {
+                const int ix = ox * sw - pl + kx2;
+                if (ix < 0 || ix >= W) continue;
+                const float v = x[((b * H + iy) * W + ix) * C + c];
+                acc = type == 0 ? (acc > v ? acc : v) : __fadd_rn(acc, v);
+                cnt++;
+            }
+        }
+        if (type == 1) acc = __fmul_rn(acc, __fdiv_rn(1.0f, static_cast<float>(count_pad ? kh * kw : (cnt ? cnt : 1))));
+        y[i] = acc;
+    }
+}
+
+// sequential over the R rows of each sample, like the reference (first row copied, then combined)
+__global__ void k_global_pool(const float* __restrict__ x, float* __restrict__ y, long B, int R, int C, int type) {
+    const long n = B * C;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % C);
+        const long b = i / C;
+        const float* xs = x + b * R * C + c;
+        float acc = xs[0];
+        for (int r = 1; r < R; r++) {
+            const float v = xs[static_cast<long>(r) * C];
+            acc = type == 0 ? (acc > v ? acc : v) : __fadd_rn(acc, v);
+        }
+        if (type == 1) acc = __fmul_rn(acc, __fdiv_rn(1.0f, static_cast<float>(R)));
+        y[i] = acc;
+    }
+}
+
+struct PermGeom {
+    int nd;
+    long od[4];   // output dims
+    long ist[4];  // input stride of the input axis that feeds output axis k
+    long per;
+};
+
+__global__ void k_permute(const float* __restrict__ x, float* __restrict__ y, long B, PermGeom g) {
+    const long n = B * g.per;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long b = i / g.per;
+        long rem = i % g.per, src = 0;
+        for (int k = g.nd - 1; k >= 0; k--) {
+            src += (rem % g.od[k]) * g.ist[k];
+            rem /= g.od[k];
+        }
+        y[i] = x[b * g.per + src];
+    }
+}
+
+__global__ void k_copy_cols(const float* __restrict__ x, long ldx, float* __restrict__ y, long ldy, long yoff, long rows,
+                            long cols) {
+    const long n = rows * cols;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long r = i / cols, c = i % cols;
+        y[r * ldy + yoff + c] = x[r * ldx + c];
+    }
+}
+
+__global__ void k_pad2d(const float* __restrict__ x, float* __restrict__ y, int B, int H, int W, int C, int Ho, int Wo,
+                        int pt, int pl) {
+    const long n = static_cast<long>(B) * Ho * Wo * C;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % C);
+        long r = i / C;
+        const int ox = static_cast<int>(r % Wo);
+        r /= Wo;
+        const int oy = static_cast<int>(r % Ho);
+        const long b = r / Ho;
+        const int iy = oy - pt, ix = ox - pl;
+        y[i] = (iy >= 0 && iy < H && ix >= 0 && ix < W) ? x[((b * H + iy) * W + ix) * C + c] : 0.0f;
+    }
+}
+
+__global__ void k_upsample2d(const float* __restrict__ x, float* __restrict__ y, int B, int H, int W, int C, int Ho, int Wo,
+                             int sh, int sw) {
+    const long n = static_cast<long>(B) * Ho * Wo * C;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(i % C);
+        long r = i / C;
+        const int ox = static_cast<int>(r % Wo);
+        r /= Wo;
+        const int oy = static_cast<int>(r % Ho);
+        const long b = r / Ho;
+        y[i] = x[((b * H + oy / sh) * W + ox / sw) * C + c];
+    }
+}
+
+__global__ void k_embedding(const float* __restrict__ ids, long n, const float* __restrict__ table, int vocab, int dim,
+                            float* __restrict__ y) {
+    const long total = n * dim;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long t = i / dim;
+        const int d = static_cast<int>(i % dim);
+        const float id = ids[t];
+        y[i] = (id >= 0.0f && id < static_cast<float>(vocab) && id == floorf(id)) ? table[static_cast<long>(id) * dim + d]
+                                                                                   : __uint_as_float(0x7FC00000u);
+    }
+}
+
+// depthwise: output channel co = ci*mult + mi reads input channel ci; out = bias then += x*w per valid tap
+__global__ void k_conv_dw(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+                          float* __restrict__ y, int B, int H, int W, int C, int Co, int Ho, int Wo, int kh, int kw, int sh,
+                          int sw, int dh, int dw, int pt, int pl, int act, float alpha) {
+    const long n = static_cast<long>(B) * Ho * Wo * Co;
+    const int mult = Co / C;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int co = static_cast<int>(i % Co);
+        long r = i / Co;
+        const int ox = static_cast<int>(r % Wo);
+        r /= Wo;
+        const int oy = static_cast<int>(r % Ho);
+        const long b = r / Ho;
+        const int ci = co / mult;
+        float acc = bias ? bias[co] : 0.0f;
+        for (int ky = 0; ky < kh; ky++) {
+            const int iy = oy * sh - pt + ky * dh;
+            if (iy < 0 || iy >= H) continue;
+            for (int kx2 = 0; kx2 < kw; kx2++) {
+                const int ix = ox * sw - pl + kx2 * dw;
+                if (ix < 0 || ix >= W) continue;
+                acc = __fadd_rn(__fmul_rn(x[((b * H + iy) * W + ix) * C + ci], w[(ky * kw + kx2) * Co + co]), acc);
+            }
+        }
+        y[i] = kx::act_apply(act, acc, alpha);
+    }
+}
+
+// ----------------------------------------------------------------------------------- attention
+// One block per (sample, head, tile of T query rows); one thread per query row. Scores for the thread's row
+// live in shared memory (transposed so that a key index is one bank row), K/V stream through shared memory
+// in chunks of KC keys. Two passes over the scores as the reference: max, then exp/sum, then P = e * (1/s)
+// and ctx = P V.
+template <int D>
+__global__ void k_attention(const float* __restrict__ q, int ldq, const float* __restrict__ k, int ldk,
+                            const float* __restrict__ v, int ldv, float* __restrict__ ctx, int ldc, int Rq, int S, int H,
+                            int dk, int dv, int causal, float scale, int T) {
+    constexpr int KC = 32;
+    extern __shared__ float sm[];
+    float* sc = sm;                          // S x T scores
+    float* kv = sm + static_cast<size_t>(S) * T;  // KC x D chunk
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int r = blockIdx.x * T + threadIdx.x;
+    const bool live = r < Rq;
+    float qr[D];
+#pragma unroll
+    for (int d = 0; d < D; d++) qr[d] = (live && d < dk) ? q[(static_cast<long>(b) * Rq + r) * ldq + h * dk + d] : 0.0f;
+    const float* kb = k + static_cast<long>(b) * S * ldk + h * dk;
+    const float* vb = v + static_cast<long>(b) * S * ldv + h * dv;
+    float m = -INFINITY;
+    for (int j0 = 0; j0 < S; j0 += KC) {
+        const int nj = min(KC, S - j0);
+        __syncthreads();
+        for (int t = threadIdx.x; t < KC * D; t += blockDim.x) {
+            const int jj = t / D, d = t % D;
+            kv[t] = (jj < nj && d < dk) ? kb[static_cast<long>(j0 + jj) * ldk + d] : 0.0f;
+        }
+        __syncthreads();
+        for (int jj = 0; jj < nj; jj++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int d = 0; d < D; d++) s = __fadd_rn(s, __fmul_rn(qr[d], kv[jj * D + d]));
+            s = __fmul_rn(s, scale);
+            if (causal && j0 + jj > r) s = -INFINITY;
+            sc[static_cast<size_t>(j0 + jj) * T + threadIdx.x] = s;
+            m = s > m ? s : m;
+        }
+    }
+    float sum = 0.0f;
+    for (int j = 0; j < S; j++) {
+        const float e = expf(__fsub_rn(sc[static_cast<size_t>(j) * T + threadIdx.x], m));
+        sc[static_cast<size_t>(j) * T + threadIdx.x] = e;
+        sum = __fadd_rn(sum, e);
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+    float acc[D];
+#pragma unroll
+    for (int d = 0; d < D; d++) acc[d] = 0.0f;
+    for (int j0 = 0; j0 < S; j0 += KC) {
+        const int nj = min(KC, S - j0);
+        __syncthreads();
+        for (int t = threadIdx.x; t < KC * D; t += blockDim.x) {
+            const int jj = t / D, d = t % D;
+            kv[t] = (jj < nj && d < dv) ? vb[static_cast<long>(j0 + jj) * ldv + d] : 0.0f;
+        }
+        __syncthreads();
+        for (int jj = 0; jj < nj; jj++) {
+            const float p = __fmul_rn(sc[static_cast<size_t>(j0 + jj) * T + threadIdx.x], inv);
+#pragma unroll
+            for (int d = 0; d < D; d++) acc[d] = __fadd_rn(acc[d], __fmul_rn(p, kv[jj * D + d]));
+        }
+    }
+    if (live) {
+        float* dst = ctx + (static_cast<long>(b) * Rq + r) * ldc + h * dv;
+#pragma unroll
+        for (int d = 0; d < D; d++)
+            if (d < dv) dst[d] = acc[d];
+    }
+}
+
+__global__ void k_fma_relu(const float* __restrict__ a, const float* __restrict__ x, const float* __restrict__ b,
+                           float* __restrict__ y, size_t n) {
+    const size_t n4 = n >> 2;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4; i += stride) {
+        const float4 u = reinterpret_cast<const float4*>(a)[i], v = reinterpret_cast<const float4*>(x)[i],
+                     w = reinterpret_cast<const float4*>(b)[i];
+        reinterpret_cast<float4*>(y)[i] = make_float4(fmaxf(__fmaf_rn(u.x, v.x, w.x), 0.0f), fmaxf(__fmaf_rn(u.y, v.y, w.y), 0.0f),
+                                                      fmaxf(__fmaf_rn(u.z, v.z, w.z), 0.0f), fmaxf(__fmaf_rn(u.w, v.w, w.w), 0.0f));
+    }
+    for (size_t i = (n4 << 2) + blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += stride)
+        y[i] = fmaxf(__fmaf_rn(a[i], x[i], b[i]), 0.0f);
+}
+
+}  // namespace
+
+extern "C" {
+
+int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream) {
+    if (rows <= 0) return 0;
+    if (k <= 0 || ldq < k || ldx < k) return -1;
+    k_quant_rows<<<rows, QT, 0, static_cast<cudaStream_t>(stream)>>>(x, ldx, k, xq, ldq, sx);
+    return launch_ok();
+}
+
+int kx_bias_act(const float* x, float* y, long rows, int cols, const float* bias, int act, float alpha, void* stream) {
+    const long n = rows * cols;
+    if (n <= 0) return 0;
+    const bool vec = (cols % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) % 16 == 0);
+    if (!vec) {
+        k_bias_act<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, rows, cols, bias, act, alpha);
+    } else {
+        k_bias_act<<<grid_for(n / 4, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, rows, cols, bias, act, alpha);
+    }
+    return launch_ok();
+}
+
+int kx_softmax_rows(const float* x, float* y, long rows, int cols, void* stream) {
+    if (rows <= 0 || cols <= 0) return 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cols <= 1024) k_softmax_warp<8><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(x, y, rows, cols);
+    else k_softmax_block<<<static_cast<unsigned>(rows), 256, 0, st>>>(x, y, cols);
+    return launch_ok();
+}
+
+int kx_layernorm_rows(const float* x, float* y, long rows, int cols, const float* gamma, const float* beta, float eps,
+                      void* stream) {
+    if (rows <= 0 || cols <= 0) return 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cols <= 1024)
+        k_layernorm_warp<8><<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(x, y, rows, cols, gamma, beta, eps);
+    else k_layernorm_block<<<static_cast<unsigned>(rows), 256, 0, st>>>(x, y, cols, gamma, beta, eps);
+    return launch_ok();
+}
+
+int kx_affine_rows(const float* x, float* y, long rows, int cols, const float* g, const float* b, void* stream) {
+    const long n = rows * cols;
+    if (n <= 0) return 0;
+    k_affine<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n, cols, g, b);
+    return launch_ok();
+}
+
+int kx_add_const(const float* x, float* y, long samples, long per, const float* cst, void* stream) {
+    const long n = samples * per;
+    if (n <= 0) return 0;
+    k_add_const<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n, per, cst);
+    return launch_ok();
+}
+
+int kx_binary(const float* a, int ra, int ca, const float* b, int rb, int cb, float* y, long samples, int R, int C, int op,
+              void* stream) {
+    const long n = samples * R * C;
+    if (n <= 0) return 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool same = ra == R && rb == R && ca == C && cb == C;
+    const bool al = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    if (same && al && (n & 3) == 0) {
+        k_binary_same4<<<grid_for(n / 4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(a),
+                                                             reinterpret_cast<const float4*>(b),
+                                                             reinterpret_cast<float4*>(y), n / 4, op);
+    } else {
+        k_binary<<<grid_for(n, 256), 256, 0, st>>>(a, ra, ca, b, rb, cb, y, samples, R, C, op);
+    }
+    return launch_ok();
+}
+
+int kx_pool2d(const float* x, float* y, int B, int H, int W, int C, int Ho, int Wo, int kh, int kw, int sh, int sw, int pt,
+              int pl, int type, int count_pad, void* stream) {
+    const long n = static_cast<long>(B) * Ho * Wo * C;
+    if (n <= 0) return 0;
+    k_pool2d<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, B, H, W, C, Ho, Wo, kh, kw, sh, sw, pt,
+                                                                               pl, type, count_pad);
+    return launch_ok();
+}
+
+int kx_global_pool(const float* x, float* y, long B, int R, int C, int type, void* stream) {
+    const long n = B * C;
+    if (n <= 0) return 0;
+    k_global_pool<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, B, R, C, type);
+    return launch_ok();
+}
+
+int kx_permute(const float* x, float* y, long B, int nd, const int* dims, const int* perm, void* stream) {
+    if (nd < 1 || nd > 4) return -1;
+    PermGeom g;
+    long ist[4], n = 1;
+    for (int k = nd - 1; k >= 0; k--) {
+        ist[k] = n;
+        n *= dims[k];
+    }
+    g.nd = nd;
+    g.per = n;
+    for (int k = 0; k < nd; k++) {
+        g.od[k] = dims[perm[k]];
+        g.ist[k] = ist[perm[k]];
+    }
+    if (B * n <= 0) return 0;
+    k_permute<<<grid_for(B * n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, B, g);
+    return launch_ok();
+}
+
+int kx_copy_cols(const float* x, long ldx, float* y, long ldy, long yoff, long rows, long cols, void* stream) {
+    if (rows * cols <= 0) return 0;
+    k_copy_cols<<<grid_for(rows * cols, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, ldx, y, ldy, yoff, rows, cols);
+    return launch_ok();
+}
+
+int kx_pad2d(const float* x, float* y, int B, int H, int W, int C, int Ho, int Wo, int pt, int pl, void* stream) {
+    const long n = static_cast<long>(B) * Ho * Wo * C;
+    if (n <= 0) return 0;
+    k_pad2d<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, B, H, W, C, Ho, Wo, pt, pl);
+    return launch_ok();
+}
+
+int kx_upsample2d(const float* x, float* y, int B, int H, int W, int C, int Ho, int Wo, int sh, int sw, void* stream) {
+    const long n = static_cast<long>(B) * Ho * Wo * C;
+    if (n <= 0) return 0;
+    k_upsample2d<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, B, H, W, C, Ho, Wo, sh, sw);
+    return launch_ok();
+}
+
+int kx_embedding(const float* ids, long n, const float* table, int vocab, int dim, float* y, void* stream) {
+    if (n * dim <= 0) return 0;
+    k_embedding<<<grid_for(n * dim, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(ids, n, table, vocab, dim, y);
+    return launch_ok();
+}
+
+int kx_conv_depthwise(const float* x, const float* w, const float* bias, float* y, int B, int H, int W, int C, int Co,
+                      int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl, int act, float alpha,
+                      void* stream) {
+    const long n = static_cast<long>(B) * Ho * Wo * Co;
+    if (n <= 0) return 0;
+    if (C <= 0 || Co % C) return -1;
+    k_conv_dw<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, w, bias, y, B, H, W, C, Co, Ho, Wo, kh, kw,
+                                                                                sh, sw, dh, dw, pt, pl, act, alpha);
+    return launch_ok();
+}
+
+int kx_attention(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* ctx, int ldc, int B,
+                 int Rq, int S, int H, int dk, int dv, int causal, void* stream) {
+    if (B <= 0 || Rq <= 0) return 0;
+    if (S <= 0 || dk <= 0 || dv <= 0 || dk > 128 || dv > 128) return -1;
+    int T = 128;
+    while (T > 32 && static_cast<size_t>(S) * T * 4 > 160 * 1024) T >>= 1;
+    const int D = (dk <= 64 && dv <= 64) ? 64 : 128;
+    const size_t smem = (static_cast<size_t>(S) * T + 32 * static_cast<size_t>(D)) * sizeof(float);
+    if (smem > 220 * 1024) return -1;
+    const float scale = 1.0f / sqrtf(static_cast<float>(dk)); /* IEEE on the host, as the reference's 1.0f / sqrtf */
+    dim3 grid((Rq + T - 1) / T, H, B);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (D == 64) {
+        if (cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+            return -1;
+        k_attention<64><<<grid, T, smem, st>>>(q, ldq, k, ldk, v, ldv, ctx, ldc, Rq, S, H, dk, dv, causal, scale, T);
+    } else {
+        if (cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+            return -1;
+        k_attention<128><<<grid, T, smem, st>>>(q, ldq, k, ldk, v, ldv, ctx, ldc, Rq, S, H, dk, dv, causal, scale, T);
+    }
+    return launch_ok();
+}
+
+int kx_fma_relu(const float* a, const float* x, const float* b, float* y, size_t n, void* stream) {
+    if (n == 0) return 0;
+    if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(b) |
+          reinterpret_cast<uintptr_t>(y)) & 15) != 0)
+        return -1;
+    k_fma_relu<<<grid_for(static_cast<long>((n + 3) / 4), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(a, x, b, y, n);
+    return launch_ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,338 @@
+"""GPU parity of each kernel, called through the kernel-level C ABI (include/kx_kernels.h), against the oracle
+(oracle/knx_oracle.py) or a float64 reference of the same op. Integer work (int8 quantisation, int32
+accumulators) must be bit-exact; float work within the tolerance stated per test."""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+from oracle import knx_oracle as ko
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+F32 = np.float32
+
+
+@pytest.fixture(scope="module")
+def kx(libkx):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from kernix_b200 import kx_abi
+    return kx_abi
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def sp():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def status():
+    return torch.zeros(1, dtype=torch.int32, device="cuda")
+
+
+def check_status(st):
+    assert int(st.item()) == 0, "kernel reported a timeout"
+
+
+# ------------------------------------------------------------------------------------------ int8
+def _quant(kx, x, ldq):
+    rows, k = x.shape
+    dx = dev(x)
+    xq = torch.full((rows, ldq), 99, dtype=torch.int8, device="cuda")
+    sx = torch.empty(rows, dtype=torch.float32, device="cuda")
+    kx.call("kx_quant_rows", dx.data_ptr(), k, rows, k, xq.data_ptr(), ldq, sx.data_ptr(), sp())
+    return host(xq), host(sx)
+
+
+@pytest.mark.parametrize("rows,k", [(7, 1024), (33, 55), (5, 4096), (3, 5000), (2, 16)])
+def test_quant_rows_bitexact(kx, rows, k):
+    rng = np.random.default_rng(rows * 1000 + k)
+    x = (rng.standard_normal((rows, k)) * rng.uniform(0.01, 10, (rows, 1))).astype(F32)
+    x[0, :] = 0.0                      # zero row: sx = 1, all zeros
+    if rows > 2:
+        x[1, k // 2] = np.nan          # NaN row
+        x[2, 0] = np.inf               # infinite row
+    # values exactly on rounding ties after scaling
+    x[-1, : min(k, 8)] = np.array([0.5, -0.5, 1.5, -2.5, 127, -127, 63.5, 0.0], F32)[: min(k, 8)]
+    ldq = (k + 15) // 16 * 16
+    xq, sx = _quant(kx, x, ldq)
+    wq, wsx, bad = ko.quantize_rows(x)
+    assert np.array_equal(xq[~bad, :k], wq[~bad]), "int8 values differ"
+    assert np.array_equal(sx[~bad].view(np.uint32), wsx[~bad].view(np.uint32)), "row scales differ"
+    assert np.all(np.isnan(sx[bad]))
+    assert np.all(xq[:, k:] == 0), "padding columns must be zero"
+
+
+def _prep_i8(kx, q):
+    k, n = q.shape
+    ldw = (k + 15) // 16 * 16
+    wq = torch.empty((n, ldw), dtype=torch.int8, device="cuda")
+    kx.call("kx_prep_i8_weight", dev(q).data_ptr(), k, n, wq.data_ptr(), ldw, sp())
+    return wq, ldw
+
+
+@pytest.mark.parametrize("m,k,n", [(300, 1000, 520), (128, 256, 256), (5, 55, 31), (1, 16, 16), (130, 4096, 384)])
+def test_gemm_i8_accumulators_bitexact(kx, m, k, n):
+    rng = np.random.default_rng(m + k + n)
+    xq = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    q = rng.integers(-127, 128, (k, n), dtype=np.int8)
+    ldq = (k + 15) // 16 * 16
+    xqp = np.zeros((m, ldq), np.int8)
+    xqp[:, :k] = xq
+    wq, ldw = _prep_i8(kx, q)
+    acc = torch.zeros((m, n), dtype=torch.int32, device="cuda")
+    st = status()
+    kx.call("kx_gemm_i8_acc", dev(xqp).data_ptr(), ldq, wq.data_ptr(), ldw, acc.data_ptr(), n, m, n, k, st.data_ptr(), sp())
+    got = host(acc)
+    check_status(st)
+    assert np.array_equal(got, ko.int8_acc(xq, q))
+
+
+def test_gemm_i8_int32_overflow_edge(kx):
+    """reference test/model_test.c:430-440: K = 131072, q = -128, x = 1 stays inside int32."""
+    k, n = ko.INT8_MAX_K, 16
+    xq = np.full((1, k), 127, np.int8)
+    q = np.full((k, n), -128, np.int8)
+    wq, ldw = _prep_i8(kx, q)
+    acc = torch.zeros((1, n), dtype=torch.int32, device="cuda")
+    kx.call("kx_gemm_i8_acc", dev(xq).data_ptr(), k, wq.data_ptr(), ldw, acc.data_ptr(), n, 1, n, k, None, sp())
+    assert np.all(host(acc) == -128 * 127 * k)
+
+
+@pytest.mark.parametrize("act", [ko.ACT_NONE, 0, 1])
+@pytest.mark.parametrize("m,k,n,bias", [(257, 1024, 4096, True), (33, 55, 31, False), (3, 128, 1000, True)])
+def test_gemm_i8_dequant_epilogue(kx, m, k, n, bias, act):
+    """quantise + int8 GEMM + ((float)acc*sx)*scale + bias (+act) vs the oracle's kernix_qmatmul restatement."""
+    rng = np.random.default_rng(m * n + k)
+    x = rng.standard_normal((m, k)).astype(F32)
+    x[0] = 0.0
+    if m > 2:
+        x[1, 3] = np.nan
+    w = (rng.standard_normal((k, n)) * 0.02).astype(F32)
+    from kernix_b200.knx_writer import quantize_int8
+    scale, q = quantize_int8(w)
+    b = rng.standard_normal(n).astype(F32) if bias else None
+    ldq = (k + 15) // 16 * 16
+    dx = dev(x)
+    xq = torch.empty((m, ldq), dtype=torch.int8, device="cuda")
+    sx = torch.empty(m, dtype=torch.float32, device="cuda")
+    kx.call("kx_quant_rows", dx.data_ptr(), k, m, k, xq.data_ptr(), ldq, sx.data_ptr(), sp())
+    wq, ldw = _prep_i8(kx, q)
+    dscale = dev(scale)
+    db = dev(b) if bias else None
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    st = status()
+    kx.call("kx_gemm_i8", xq.data_ptr(), ldq, sx.data_ptr(), wq.data_ptr(), ldw, dscale.data_ptr(),
+            db.data_ptr() if bias else None, y.data_ptr(), n, m, n, k, act, 0.0, st.data_ptr(), sp())
+    got = host(y)
+    check_status(st)
+    want = ko.act(ko.qlinear(x, q, scale, b), act)
+    if act in (ko.ACT_NONE, 0):  # same IEEE operations in the same order: bit-exact
+        assert np.array_equal(np.isnan(got), np.isnan(want))
+        assert np.array_equal(np.nan_to_num(got), np.nan_to_num(want))
+    else:  # GELU uses the device expf (a few ulp from glibc's)
+        assert rel_err(got, want) <= 1e-6
+
+
+# ------------------------------------------------------------------------------------------ fp32
+def _prep_f32(kx, w):
+    k, n = w.shape
+    ldw = (k + 31) // 32 * 32
+    hi = torch.empty((n, ldw), dtype=torch.float32, device="cuda")
+    lo = torch.empty((n, ldw), dtype=torch.float32, device="cuda")
+    kx.call("kx_prep_f32_weight", dev(w).data_ptr(), k, n, hi.data_ptr(), lo.data_ptr(), ldw, sp())
+    return hi, lo, ldw
+
+
+def test_prep_f32_split_is_exact(kx):
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((37, 19)) * 10.0 ** rng.integers(-8, 8, (37, 19))).astype(F32)
+    hi, lo, ldw = _prep_f32(kx, w)
+    h, lo_ = host(hi), host(lo)
+    assert np.array_equal((h[:, :37] + lo_[:, :37]).T, w), "hi + lo must reproduce w exactly"
+    assert np.all(h.view(np.uint32) & 0x1FFF == 0), "hi must be a tf32 value"
+    assert np.all(h[:, 37:] == 0) and np.all(lo_[:, 37:] == 0)
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 784, 512), (300, 27, 64), (129, 250, 10), (1, 8192, 300), (512, 512, 1536)])
+@pytest.mark.parametrize("act", [ko.ACT_NONE, 0])
+def test_gemm_f32_3xtf32(kx, m, k, n, act):
+    """3xTF32 GEMM + bias + act vs float64: max abs error <= 1e-5 x output scale (the dense-MLP bound)."""
+    rng = np.random.default_rng(m + 7 * k + n)
+    x = rng.standard_normal((m, k)).astype(F32)
+    w = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(F32)
+    b = rng.standard_normal(n).astype(F32)
+    hi, lo, ldw = _prep_f32(kx, w)
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    st = status()
+    db = dev(b)
+    kx.call("kx_gemm_f32", dev(x).data_ptr(), k, hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y.data_ptr(), n, m, n, k,
+            act, 0.0, st.data_ptr(), sp())
+    got = host(y)
+    check_status(st)
+    ref = x.astype(np.float64) @ w.astype(np.float64) + b
+    if act == 0:
+        ref = np.maximum(ref, 0)
+    assert rel_err(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(B=2, H=8, W=8, C=3, Co=16, k=3, s=1, d=1, p=1, g=1),
+    dict(B=3, H=9, W=7, C=64, Co=64, k=3, s=1, d=1, p=1, g=1),
+    dict(B=2, H=10, W=10, C=32, Co=48, k=3, s=2, d=1, p=1, g=2),
+    dict(B=1, H=12, W=12, C=16, Co=24, k=3, s=1, d=2, p=2, g=1),
+    dict(B=2, H=6, W=5, C=8, Co=300, k=2, s=1, d=1, p=0, g=1),
+])
+def test_conv_implicit_gemm(kx, cfg):
+    """implicit-GEMM conv (no im2col buffer) vs the oracle's im2col + sgemm restatement of kernix_conv_run."""
+    rng = np.random.default_rng(cfg["C"] * cfg["Co"])
+    B, H, W, C, Co, kk, s, d, p, g = (cfg[k] for k in ("B", "H", "W", "C", "Co", "k", "s", "d", "p", "g"))
+    Ho = (H + 2 * p - d * (kk - 1) - 1) // s + 1
+    Wo = (W + 2 * p - d * (kk - 1) - 1) // s + 1
+    x = rng.standard_normal((B * H * W, C)).astype(F32)
+    K = kk * kk * (C // g)
+    w = (rng.standard_normal((K, Co)) / np.sqrt(K)).astype(F32)
+    b = rng.standard_normal(Co).astype(F32)
+    hi, lo, ldw = _prep_f32(kx, w)
+    y = torch.empty((B * Ho * Wo, Co), dtype=torch.float32, device="cuda")
+    st = status()
+    db = dev(b)
+    kx.call("kx_conv_f32", dev(x).data_ptr(), hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y.data_ptr(), B, H, W, C, Co,
+            Ho, Wo, kk, kk, s, s, d, d, p, p, g, 0, 0.0, st.data_ptr(), sp())
+    got = host(y)
+    check_status(st)
+    step = dict(kind=ko.OP["CONV"], act=0, alpha=0.0, groups=g, kh=kk, kw=kk, sh=s, sw=s, dh=d, dw=d, pt=p, pb=p, pl=p, pr=p,
+                w=("f32", w), bias=b)
+    want = ko.conv(step, ko._val([H, W, C]), ko._val([Ho, Wo, Co]), x)
+    assert rel_err(got, want) <= 1e-5
+
+
+# ------------------------------------------------------------------------------------ memory-bound
+@pytest.mark.parametrize("act", list(range(-1, 16)))
+def test_bias_act_all_activations(kx, act):
+    rng = np.random.default_rng(act + 10)
+    x = (rng.standard_normal((37, 100)) * 4).astype(F32)
+    x[0, :4] = [0.0, -0.0, 25.0, -25.0]
+    b = rng.standard_normal(100).astype(F32)
+    y = torch.empty_like(dev(x))
+    kx.call("kx_bias_act", dev(x).data_ptr(), y.data_ptr(), 37, 100, dev(b).data_ptr(), act, 0.3, sp())
+    want = ko.act((x + b).astype(F32), act, 0.3)
+    assert rel_err(host(y), want) <= 2e-6
+
+
+@pytest.mark.parametrize("rows,cols", [(256, 10), (64, 512), (7, 3000), (3, 1)])
+def test_softmax_layernorm_rows(kx, rows, cols):
+    rng = np.random.default_rng(rows + cols)
+    x = (rng.standard_normal((rows, cols)) * 3).astype(F32)
+    g = rng.standard_normal(cols).astype(F32)
+    b = rng.standard_normal(cols).astype(F32)
+    d = dev(x)
+    y = torch.empty_like(d)
+    kx.call("kx_softmax_rows", d.data_ptr(), y.data_ptr(), rows, cols, sp())
+    assert rel_err(host(y), ko.softmax_rows(x)) <= 1e-6
+    kx.call("kx_layernorm_rows", d.data_ptr(), d.data_ptr(), rows, cols, dev(g).data_ptr(), dev(b).data_ptr(), 1e-5, sp())
+    assert rel_err(host(d), ko.layer_norm_rows(x, g, b, 1e-5)) <= 1e-5
+
+
+def test_binary_broadcast_and_inplace(kx):
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((4 * 6, 5)).astype(F32)
+    for (rb, cb) in [(6, 5), (1, 5), (6, 1), (1, 1)]:
+        b = rng.standard_normal((4 * rb, cb)).astype(F32) + 3
+        for op in range(6):
+            y = torch.empty((24, 5), dtype=torch.float32, device="cuda")
+            kx.call("kx_binary", dev(a).data_ptr(), 6, 5, dev(b).data_ptr(), rb, cb, y.data_ptr(), 4, 6, 5, op, sp())
+            s = dict(bop=op)
+            want = ko.binary(s, ko._val([6, 5]), a, ko._val([rb, cb]), b, ko._val([6, 5]))
+            assert rel_err(host(y), want) <= 1e-7
+    da = dev(a)
+    kx.call("kx_binary", da.data_ptr(), 6, 5, da.data_ptr(), 6, 5, da.data_ptr(), 4, 6, 5, 0, sp())
+    assert np.array_equal(host(da), a + a)
+
+
+def test_pool_gpool_permute_pad_upsample(kx):
+    rng = np.random.default_rng(11)
+    B, H, W, C = 2, 7, 6, 5
+    x = rng.standard_normal((B * H * W, C)).astype(F32)
+    dx = dev(x)
+    for ptype, k, s, p, cp in [(0, 2, 2, 0, 0), (1, 3, 2, 1, 0), (1, 3, 2, 1, 1), (0, 3, 1, 1, 0)]:
+        Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+        y = torch.empty((B * Ho * Wo, C), dtype=torch.float32, device="cuda")
+        kx.call("kx_pool2d", dx.data_ptr(), y.data_ptr(), B, H, W, C, Ho, Wo, k, k, s, s, p, p, ptype, cp, sp())
+        st = dict(ptype=ptype, kh=k, kw=k, sh=s, sw=s, pt=p, pb=p, pl=p, pr=p, count_pad=cp)
+        assert rel_err(host(y), ko.pool(st, ko._val([H, W, C]), ko._val([Ho, Wo, C]), x)) <= 1e-6
+    for ptype in (0, 1):
+        y = torch.empty((B, C), dtype=torch.float32, device="cuda")
+        kx.call("kx_global_pool", dx.data_ptr(), y.data_ptr(), B, H * W, C, ptype, sp())
+        assert rel_err(host(y), ko.global_pool(dict(ptype=ptype), ko._val([H, W, C]), x)) <= 1e-6
+    import ctypes
+    for perm in [(2, 0, 1), (1, 0, 2), (0, 2, 1)]:
+        dims = (ctypes.c_int * 4)(H, W, C, 0)
+        pm = (ctypes.c_int * 4)(*perm, 0)
+        y = torch.empty_like(dx)
+        kx.call("kx_permute", dx.data_ptr(), y.data_ptr(), B, 3, dims, pm, sp())
+        assert np.array_equal(host(y).reshape(-1), ko.permute(dict(perm=list(perm)), ko._val([H, W, C]), x).reshape(-1))
+    y = torch.empty((B * (H + 3) * (W + 2), C), dtype=torch.float32, device="cuda")
+    kx.call("kx_pad2d", dx.data_ptr(), y.data_ptr(), B, H, W, C, H + 3, W + 2, 1, 2, sp())
+    want = np.zeros((B, H + 3, W + 2, C), F32)
+    want[:, 1:1 + H, 2:2 + W] = x.reshape(B, H, W, C)
+    assert np.array_equal(host(y).reshape(want.shape), want)
+    y = torch.empty((B * H * 2 * W * 3, C), dtype=torch.float32, device="cuda")
+    kx.call("kx_upsample2d", dx.data_ptr(), y.data_ptr(), B, H, W, C, 2 * H, 3 * W, 2, 3, sp())
+    want = x.reshape(B, H, W, C).repeat(2, axis=1).repeat(3, axis=2)
+    assert np.array_equal(host(y).reshape(want.shape), want)
+
+
+def test_depthwise_embedding_fma_relu(kx):
+    rng = np.random.default_rng(12)
+    B, H, W, C, mult = 2, 6, 5, 4, 2
+    x = rng.standard_normal((B * H * W, C)).astype(F32)
+    w = rng.standard_normal((9, C * mult)).astype(F32)
+    b = rng.standard_normal(C * mult).astype(F32)
+    y = torch.empty((B * H * W, C * mult), dtype=torch.float32, device="cuda")
+    kx.call("kx_conv_depthwise", dev(x).data_ptr(), dev(w).data_ptr(), dev(b).data_ptr(), y.data_ptr(), B, H, W, C, C * mult,
+            H, W, 3, 3, 1, 1, 1, 1, 1, 1, 0, 0.0, sp())
+    st = dict(groups=C, kh=3, kw=3, sh=1, sw=1, dh=1, dw=1, pt=1, pb=1, pl=1, pr=1, w=("f32", w), bias=b, act=0, alpha=0.0)
+    assert rel_err(host(y), ko.conv(st, ko._val([H, W, C]), ko._val([H, W, C * mult]), x)) <= 1e-6
+    table = rng.standard_normal((10, 6)).astype(F32)
+    ids = np.array([0, 3, 9, 10, -1, 2.5, 7], F32)
+    y = torch.empty((7, 6), dtype=torch.float32, device="cuda")
+    kx.call("kx_embedding", dev(ids).data_ptr(), 7, dev(table).data_ptr(), 10, 6, y.data_ptr(), sp())
+    got = host(y)
+    assert np.array_equal(got[[0, 1, 2, 6]], table[[0, 3, 9, 7]]) and np.all(np.isnan(got[[3, 4, 5]]))
+    n = 1000003
+    a, xx, bb = (rng.standard_normal(n).astype(F32) for _ in range(3))
+    y = torch.empty(n, dtype=torch.float32, device="cuda")
+    kx.call("kx_fma_relu", dev(a).data_ptr(), dev(xx).data_ptr(), dev(bb).data_ptr(), y.data_ptr(), n, sp())
+    want = np.maximum((a.astype(np.float64) * xx + bb), 0).astype(F32)
+    assert rel_err(host(y), want) <= 1e-7
+
+
+@pytest.mark.parametrize("Rq,S,H,dk,dv,causal", [(128, 128, 8, 64, 64, False), (10, 10, 4, 4, 4, True), (5, 17, 2, 32, 48, False)])
+def test_attention_core(kx, Rq, S, H, dk, dv, causal):
+    rng = np.random.default_rng(Rq + S + dk)
+    B = 3
+    q = rng.standard_normal((B * Rq, H * dk)).astype(F32)
+    k = rng.standard_normal((B * S, H * dk)).astype(F32)
+    v = rng.standard_normal((B * S, H * dv)).astype(F32)
+    ctx = torch.empty((B * Rq, H * dv), dtype=torch.float32, device="cuda")
+    kx.call("kx_attention", dev(q).data_ptr(), H * dk, dev(k).data_ptr(), H * dk, dev(v).data_ptr(), H * dv, ctx.data_ptr(),
+            H * dv, B, Rq, S, H, dk, dv, int(causal), sp())
+    Q = q.reshape(B, Rq, H, dk).transpose(0, 2, 1, 3).astype(np.float64)
+    K = k.reshape(B, S, H, dk).transpose(0, 2, 1, 3).astype(np.float64)
+    V = v.reshape(B, S, H, dv).transpose(0, 2, 1, 3).astype(np.float64)
+    P = Q @ K.transpose(0, 1, 3, 2) / np.sqrt(dk)
+    if causal:
+        P = np.where(np.triu(np.ones((Rq, S), bool), 1), -np.inf, P)
+    P = np.exp(P - P.max(-1, keepdims=True))
+    P /= P.sum(-1, keepdims=True)
+    want = (P @ V).transpose(0, 2, 1, 3).reshape(B * Rq, H * dv)
+    assert rel_err(host(ctx), want) <= 1e-5

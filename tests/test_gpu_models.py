@@ -1,0 +1,185 @@
+"""GPU parity of whole .knx models through the public API (the Model binding over kernix_capi_*), against the
+numpy oracle on the same seeded inputs, plus the reference runtime's own behavioural contract
+(test/model_test.c: chunking invariance, buffer reuse, trim, zero batch, bad inputs rejected)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import rel_err
+from oracle import knx_oracle as ko
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+F32 = np.float32
+
+
+@pytest.fixture(scope="module")
+def Model(libkx):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from kernix_b200 import Model
+    return Model
+
+
+def cfg_path(name, model_dir):
+    from kernix_b200 import configs
+    return configs.model_path(name, model_dir)
+
+
+# tolerances of the north star: max-abs relative to the output scale
+TOL = dict(c1=1e-5, c3=1e-4, c4=1e-4)
+
+
+@pytest.mark.parametrize("cfg,batch", [("c1", 256), ("c3", 4), ("c4", 2)])
+def test_config_matches_oracle(Model, model_dir, cfg, batch):
+    from kernix_b200 import configs
+    p = cfg_path(cfg, model_dir)
+    m = Model(p)
+    x = configs.inputs(cfg, batch)
+    got = m(x.reshape(-1, m.in_dim))
+    want = ko.forward(ko.load(p), x)
+    assert rel_err(got.reshape(want.shape), want) <= TOL[cfg]
+
+
+def test_c2_int8_end_to_end(Model, model_dir):
+    """int8 MLP end to end: within 1e-4 of the output scale; requantisation flips after GELU (device expf vs
+    glibc expf moving a value across a rounding tie) are allowed and counted."""
+    from kernix_b200 import configs
+    p = cfg_path("c2", model_dir)
+    m = Model(p)
+    x = configs.inputs("c2", 64)
+    got = m(x)
+    want = ko.forward(ko.load(p), x)
+    err = rel_err(got, want)
+    flips = int((np.abs(got - want) > 1e-6 * np.abs(want).max()).sum())
+    print(f"c2 e2e max rel err {err:.2e}, elements off by more than 1e-6: {flips} of {got.size}")
+    assert err <= 1e-4
+
+
+def test_c2_int8_per_layer_accumulators_bitexact(libkx):
+    """Teacher-forced layers of c2's shapes: same fp32 layer input on both sides -> identical int32 accumulators,
+    checked via the dequantised output with no activation (same IEEE ops, bit-exact)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from kernix_b200 import knx_writer
+    import tempfile, os
+    rng = np.random.default_rng(21)
+    for k, n in [(1024, 4096), (4096, 4096), (4096, 1024)]:
+        w = (rng.standard_normal((k, n)) * 0.02).astype(F32)
+        b = rng.uniform(-0.03, 0.03, n).astype(F32)
+        with tempfile.TemporaryDirectory() as d:
+            p = os.path.join(d, "l.knx")
+            knx_writer.Sequential(int8=True).linear(w, b).write(p)
+            from kernix_b200 import Model
+            m = Model(p)
+            x = (rng.standard_normal((40, k)) * rng.uniform(0.1, 3, (40, 1))).astype(F32)
+            got = m(x)
+            mod = ko.load(p)
+            st = mod["steps"][0]
+            want = ko.qlinear(x, st["w"][1], st["w"][2], st["bias"])
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"layer {k}x{n} differs"
+
+
+def test_full_batch_rows_equal_small_batch_rows(Model, model_dir):
+    """Size-independent property at the benchmark size: samples are independent, so every row of a batch-4096
+    forward equals the same row computed alone in a small batch (bitwise), and sampled rows match the oracle."""
+    from kernix_b200 import configs
+    p = cfg_path("c2", model_dir)
+    m = Model(p)
+    x = configs.inputs("c2", 4096)
+    full = m(x)
+    idx = np.array([0, 1, 127, 128, 1000, 2047, 4095])
+    part = m(x[idx])
+    assert np.array_equal(full[idx].view(np.uint32), part.view(np.uint32))
+    want = ko.forward(ko.load(p), x[idx])
+    assert rel_err(full[idx], want) <= 1e-4
+
+
+def test_chunked_equals_unchunked_and_trim(Model, model_dir):
+    """reference test/model_test.c:296-360: any workspace limit gives the same result; trim then re-run."""
+    from kernix_b200 import configs
+    p = cfg_path("c4", model_dir)
+    m = Model(p, workspace_mb=0)
+    x = configs.inputs("c4", 5)
+    want = m(x)
+    for mb in (1, 70, 1000):  # 1 MB -> one sample per chunk
+        m2 = Model(p, workspace_mb=mb)
+        assert np.array_equal(m2(x), want)
+        m2.close()
+    m.trim()
+    assert np.array_equal(m(x), want)
+    assert np.array_equal(m(x[: 3 * 128]), want[:3])
+
+
+def test_device_forward_matches_host_forward(Model, model_dir, libkx):
+    from kernix_b200 import configs
+    p = cfg_path("c1", model_dir)
+    m = Model(p)
+    x = configs.inputs("c1", 300)
+    want = m(x)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((300, 10), dtype=torch.float32, device="cuda")
+    libkx.kernix_model_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    libkx.kernix_model_forward_device.restype = ctypes.c_int
+    libkx.kernix_model_check.argtypes = [ctypes.c_void_p]
+    libkx.kernix_model_check.restype = ctypes.c_int
+    rc = libkx.kernix_model_forward_device(m._h, dx.data_ptr(), 300, dy.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert libkx.kernix_model_check(m._h) == 0
+    assert np.array_equal(dy.cpu().numpy(), want)
+
+
+class FloatTensor(ctypes.Structure):
+    _fields_ = [("row", ctypes.c_int), ("col", ctypes.c_int), ("tensor", ctypes.POINTER(ctypes.c_float))]
+
+
+def test_model_api_contract(libkx, model_dir):
+    """kernix_model_forward: zero batch -> 0 x out_dim, bad shapes and NULLs -> NULL, own output rejected,
+    same batch reuses the same output buffer, input never modified (reference test/model_test.c:144-194)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    L = libkx
+    L.kernix_model_load.restype = ctypes.c_void_p
+    L.kernix_model_load.argtypes = [ctypes.c_char_p]
+    L.kernix_model_forward.restype = ctypes.POINTER(FloatTensor)
+    L.kernix_model_forward.argtypes = [ctypes.c_void_p, ctypes.POINTER(FloatTensor)]
+    L.kernix_model_free.argtypes = [ctypes.c_void_p]
+    p = cfg_path("c1", model_dir)
+    m = L.kernix_model_load(p.encode())
+    assert m
+    x = np.random.default_rng(1).random((37, 784), dtype=F32)
+    x0 = x.copy()
+    t = FloatTensor(37, 784, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    y1 = L.kernix_model_forward(m, ctypes.byref(t))
+    assert y1 and y1.contents.row == 37 and y1.contents.col == 10
+    p1 = ctypes.addressof(y1.contents.tensor.contents)
+    out1 = np.ctypeslib.as_array(y1.contents.tensor, (37, 10)).copy()
+    y2 = L.kernix_model_forward(m, ctypes.byref(t))
+    assert ctypes.addressof(y2.contents.tensor.contents) == p1
+    assert np.array_equal(np.ctypeslib.as_array(y2.contents.tensor, (37, 10)), out1)
+    assert np.array_equal(x, x0)
+    t0 = FloatTensor(0, 784, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    y0 = L.kernix_model_forward(m, ctypes.byref(t0))
+    assert y0 and y0.contents.row == 0 and y0.contents.col == 10
+    bad = FloatTensor(2, 783, x.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    assert not L.kernix_model_forward(m, ctypes.byref(bad))
+    assert not L.kernix_model_forward(m, None)
+    assert not L.kernix_model_forward(None, ctypes.byref(t))
+    own = FloatTensor(3, 10, y2.contents.tensor)  # not 784 columns anyway; make a 10-column identity model below
+    del own
+    L.kernix_model_free(m)
+    L.kernix_model_free(None)
+    # an identity Linear(4,4): feeding its own output back is rejected
+    from kernix_b200 import knx_writer
+    q = model_dir + "/eye.knx"
+    knx_writer.Sequential().linear(np.eye(4, dtype=F32)).write(q)
+    m = L.kernix_model_load(q.encode())
+    x4 = np.arange(8, dtype=F32).reshape(2, 4)
+    t4 = FloatTensor(2, 4, x4.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    y = L.kernix_model_forward(m, ctypes.byref(t4))
+    assert y and np.array_equal(np.ctypeslib.as_array(y.contents.tensor, (2, 4)), x4)
+    assert not L.kernix_model_forward(m, y)
+    L.kernix_model_free(m)
