@@ -141,9 +141,12 @@ class Clocks:
         self.proc = None
 
     def __enter__(self):
+        import tempfile
+        self.path = tempfile.mktemp(prefix="kx_clocks_", suffix=".csv")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
         except OSError:
             self.proc = None
         return self
@@ -151,13 +154,17 @@ class Clocks:
     def __exit__(self, *a):
         self.lines = []
         if self.proc is not None:
+            time.sleep(0.25)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            try:
+                self.lines = [ln for ln in open(self.path).read().splitlines() if ln.strip()]
+                os.remove(self.path)
+            except OSError:
+                pass
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
@@ -224,7 +231,8 @@ def run_kernix(args):
     x_dev = x_pin.cuda()
     y_dev = torch.empty((BATCH, DIMS[-1]), dtype=torch.float32, device="cuda")
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # every launch and event of the timed regions goes on this one stream
+    torch.cuda.set_stream(stream)
 
     def fwd_device():
         if L.kernix_model_forward_device(m._h, x_dev.data_ptr(), BATCH, y_dev.data_ptr(), stream.cuda_stream) != 0:

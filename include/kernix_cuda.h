@@ -16,7 +16,7 @@ extern "C" {
 #endif
 
 /* d_x: rows x in_dim device floats (rows a positive multiple of seq_len), d_out: (rows/seq_len) x out_dim device
- * floats, stream: cudaStream_t (NULL = the model's own stream). Both buffers must be on the model's device.
+ * floats, stream: cudaStream_t the work is ordered on (0 = the legacy default stream). Both buffers must be on the model's device.
  * Returns 0 when all work was enqueued, -1 on bad arguments or a launch failure. Wait on the stream, then call
  * kernix_model_check to learn whether a kernel reported a failure. */
 KERNIX_API int kernix_model_forward_device(kernix_model* m, const float* d_x, int rows, float* d_out, void* stream);

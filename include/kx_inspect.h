@@ -21,6 +21,17 @@ extern "C" {
 KERNIX_API int kx_knx_inspect(const char* path, long* info, int* shapes, int* kinds, int* acts, int cap, char* err,
                               int errlen);
 
+/* Trace hook (no counterpart in the reference, whose intermediate values are host arrays): run the forward of
+ * `rows` host input rows as one chunk and, right after each step, copy its output value into outs[k] (host,
+ * (batch * r) x c floats for step k's output after activation fusion; NULL entries are skipped). Values are
+ * captured before the storage plan lets a later step reuse their buffer. Returns 0 or -1. */
+/* Storage plan of a .knx file without a GPU: st[v] = storage buffer of value v (-1 = the model input),
+ * last[v] = last step reading it. Returns the number of values or -1. */
+KERNIX_API int kx_knx_plan(const char* path, int* st, int* last, int cap);
+
+struct kernix_model;
+KERNIX_API int kx_model_forward_trace(struct kernix_model* m, const float* x, int rows, float** outs);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,14 @@ KERNIX_API int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* x
 KERNIX_API int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
                const float* bias, float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, void* stream);
 
+/* One int8 LINEAR step from fp32 activations, the whole of kernix_qmatmul plus the step's activation
+ * (include/kernix_model.h:99-182, :1854-1856): quantise x's rows into xq_scratch (rows x ldq int8, ldq =
+ * k rounded up to 16) and sx_scratch (rows floats), then y = act(((float)acc * sx) * scale + bias) with the
+ * int8 tcgen05 GEMM. The two scratch buffers are device memory supplied by the caller. */
+KERNIX_API int kx_linear_i8(const float* x, int ldx, int rows, int k, const int8_t* wq, int ldw, const float* scale,
+                            const float* bias, float* y, int ldy, int n, int act, float alpha, int8_t* xq_scratch,
+                            float* sx_scratch, int* status, void* stream);
+
 /* int32 accumulators only (acc[row][col], leading dimension ldacc): exposes the integer result for tests. */
 KERNIX_API int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
                    int* status, void* stream);

@@ -747,3 +747,16 @@ KERNIX_API int kx_knx_inspect(const char* path, long* info, int* shapes, int* ki
     kx_graph_free(g);
     return 0;
 }
+
+KERNIX_API int kx_knx_plan(const char* path, int* st, int* last, int cap) {
+    const char* e = NULL;
+    kx_graph* g = kx_graph_load(path, &e);
+    if (g == NULL) return -1;
+    for (int v = 0; v < g->n_vals && v < cap; v++) {
+        st[v] = g->vals[v].st;
+        last[v] = g->vals[v].last;
+    }
+    const int n = g->n_vals;
+    kx_graph_free(g);
+    return n;
+}

@@ -18,6 +18,7 @@
 
 #include "kernix_capi.h"
 #include "kernix_cuda.h"
+#include "kx_inspect.h"
 #include "kernix_model.h"
 #include "kx_internal.h"
 #include "kx_kernels.h"
@@ -56,24 +57,27 @@ static void dev_guard_leave(const kernix_model* m, int prev) {
 static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 /* ------------------------------------------------------------------------------- weight upload */
-static int upload(void** dst, const void* src, size_t bytes) {
+/* Every copy and preparation kernel of the load goes on the model's stream: a legacy-stream cudaMemcpy from
+ * pageable memory may return before its DMA has landed, and the model's non-blocking stream is not ordered
+ * after the legacy stream, so mixing the two lets a preparation kernel read a half-copied buffer. */
+static int upload(void** dst, const void* src, size_t bytes, cudaStream_t st) {
     if (cudaMalloc(dst, bytes ? bytes : 4) != cudaSuccess) return -1;
-    if (bytes && cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return -1;
+    if (bytes && cudaMemcpyAsync(*dst, src, bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) return -1;
     return 0;
 }
 
-static int upload_f(float** dst, const float* src, size_t n) {
+static int upload_f(float** dst, const float* src, size_t n, cudaStream_t st) {
     if (src == NULL) {
         *dst = NULL;
         return 0;
     }
-    return upload((void**)dst, src, n * sizeof(float));
+    return upload((void**)dst, src, n * sizeof(float), st);
 }
 
 /* float weight k x n -> tf32 split planes n x ldw at rows [row0, row0+n) of (hi, lo) */
 static int prep_f32_into(const kx_weight* w, float* hi, float* lo, int ldw, size_t row0, cudaStream_t st) {
     float* raw = NULL;
-    if (upload((void**)&raw, w->f, (size_t)w->k * w->n * sizeof(float)) != 0) {
+    if (upload((void**)&raw, w->f, (size_t)w->k * w->n * sizeof(float), st) != 0) {
         cudaFree(raw);
         return -1;
     }
@@ -94,7 +98,7 @@ static int prep_i8(kx_weight* w, cudaStream_t st) {
     w->ldw = (int)round_up((size_t)w->k, 16);
     int8_t* raw = NULL;
     if (cudaMalloc((void**)&w->d_q, (size_t)w->n * w->ldw) != cudaSuccess) return -1;
-    if (upload((void**)&raw, w->q, (size_t)w->k * w->n) != 0 || upload_f(&w->d_scale, w->scale_h, (size_t)w->n) != 0) {
+    if (upload((void**)&raw, w->q, (size_t)w->k * w->n, st) != 0 || upload_f(&w->d_scale, w->scale_h, (size_t)w->n, st) != 0) {
         cudaFree(raw);
         return -1;
     }
@@ -125,22 +129,22 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
     switch (s->kind) {
     case KERNIX_OP_LINEAR:
         if (s->w.int8 ? prep_i8(&s->w, st) : prep_f32(&s->w, st)) return -1;
-        return upload_f(&s->d_bias, s->bias, (size_t)s->out);
+        return upload_f(&s->d_bias, s->bias, (size_t)s->out, st);
     case KERNIX_OP_CONV:
         if (conv_depthwise(s)) {
-            if (upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n) != 0) return -1;
+            if (upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n, st) != 0) return -1;
         } else if (prep_f32(&s->w, st) != 0) {
             return -1;
         }
-        return upload_f(&s->d_bias, s->bias, (size_t)s->out);
+        return upload_f(&s->d_bias, s->bias, (size_t)s->out, st);
     case KERNIX_OP_LAYERNORM:
-        return upload_f(&s->d_gamma, s->gamma, (size_t)s->in) || upload_f(&s->d_beta, s->beta, (size_t)s->in) ? -1 : 0;
+        return upload_f(&s->d_gamma, s->gamma, (size_t)s->in, st) || upload_f(&s->d_beta, s->beta, (size_t)s->in, st) ? -1 : 0;
     case KERNIX_OP_AFFINE:
-        return upload_f(&s->d_gamma, s->gamma, (size_t)s->in) || upload_f(&s->d_beta, s->beta, (size_t)s->in) ? -1 : 0;
+        return upload_f(&s->d_gamma, s->gamma, (size_t)s->in, st) || upload_f(&s->d_beta, s->beta, (size_t)s->in, st) ? -1 : 0;
     case KERNIX_OP_ADD_CONST:
-        return upload_f(&s->d_cst, s->cst, (size_t)s->in);
+        return upload_f(&s->d_cst, s->cst, (size_t)s->in, st);
     case KERNIX_OP_EMBEDDING:
-        return upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n);
+        return upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n, st);
     case KERNIX_OP_ATTENTION: {
         const size_t hk = (size_t)s->heads * s->dk, hv = (size_t)s->heads * s->dv;
         s->qkv_fused = s->n_in == 1;
@@ -157,17 +161,17 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
                 return -1;
             if (s->bias) {
                 if (cudaMalloc((void**)&s->d_bqkv, (2 * hk + hv) * sizeof(float)) != cudaSuccess) return -1;
-                if (cudaMemcpy(s->d_bqkv, s->bias, hk * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-                    cudaMemcpy(s->d_bqkv + hk, s->bk, hk * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-                    cudaMemcpy(s->d_bqkv + 2 * hk, s->bv, hv * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                if (cudaMemcpyAsync(s->d_bqkv, s->bias, hk * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                    cudaMemcpyAsync(s->d_bqkv + hk, s->bk, hk * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                    cudaMemcpyAsync(s->d_bqkv + 2 * hk, s->bv, hv * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
                     return -1;
             }
         } else {
             if (prep_f32(&s->w, st) || prep_f32(&s->wk, st) || prep_f32(&s->wv, st)) return -1;
-            if (upload_f(&s->d_bias, s->bias, hk) || upload_f(&s->d_bk, s->bk, hk) || upload_f(&s->d_bv, s->bv, hv)) return -1;
+            if (upload_f(&s->d_bias, s->bias, hk, st) || upload_f(&s->d_bk, s->bk, hk, st) || upload_f(&s->d_bv, s->bv, hv, st)) return -1;
         }
         if (prep_f32(&s->wo, st) != 0) return -1;
-        return upload_f(&s->d_bo, s->bo, (size_t)s->out);
+        return upload_f(&s->d_bo, s->bo, (size_t)s->out, st);
     }
     default:
         (void)g;
@@ -261,7 +265,7 @@ static int model_alloc(kernix_model* m, int rows) {
     im->scratch = base + scr_off;
     im->status = (int*)(base + status_off);
     free(st_off);
-    if (cudaMemset(im->status, 0, sizeof(int)) != cudaSuccess) return -1;
+    if (cudaMemsetAsync(im->status, 0, sizeof(int), im->stream) != cudaSuccess) return -1;
     m->batch = rows;
     return 0;
 }
@@ -550,6 +554,7 @@ KERNIX_API kernix_model* kernix_model_load(const char* path) {
     else if (cudaHostAlloc((void**)&im->status_h, sizeof(int), cudaHostAllocDefault) != cudaSuccess) why = "cannot allocate host memory";
     for (int i = 0; why == NULL && i < g->n_steps; i++)
         if (step_upload(g, &g->steps[i], im->stream) != 0) why = "cannot copy the weights to the GPU";
+    if (why == NULL && cudaStreamSynchronize(im->stream) != cudaSuccess) why = "cannot copy the weights to the GPU";
     if (prev >= 0 && prev != im->device) cudaSetDevice(prev);
     if (why != NULL) {
         fprintf(stderr, "model load failed (%s): %s (%s)\n", path, why, cudaGetErrorString(cudaGetLastError()));
@@ -654,7 +659,7 @@ KERNIX_API int kernix_model_forward_device(kernix_model* m, const float* d_x, in
     int prev;
     if (dev_guard_enter(m, &prev) != 0) return -1;
     cudaStream_t own = im->stream;
-    if (stream != NULL) im->stream = (cudaStream_t)stream;
+    im->stream = (cudaStream_t)stream; /* as given: 0 is the legacy default stream */
     const int rc = forward_enqueue(m, d_x, rows, d_out, 1);
     im->stream = own;
     dev_guard_leave(m, prev);
@@ -669,6 +674,33 @@ KERNIX_API int kernix_model_check(kernix_model* m) {
     if (v != 0) cudaMemset(m->impl->status, 0, sizeof(int));
     dev_guard_leave(m, prev);
     return v == 0 ? 0 : -1;
+}
+
+/* --------------------------------------------------------------------------------- trace hook */
+KERNIX_API int kx_model_forward_trace(kernix_model* m, const float* x, int rows, float** outs) {
+    if (m == NULL || x == NULL || outs == NULL || rows <= 0 || rows % m->seq_len != 0) return -1;
+    struct kx_model_impl* im = m->impl;
+    const int B = rows / m->seq_len;
+    int prev;
+    if (dev_guard_enter(m, &prev) != 0) return -1;
+    int rc = -1;
+    if (rows != m->batch && model_alloc(m, rows) != 0) goto done;
+    cudaStream_t st = im->stream;
+    if (cudaMemcpyAsync(im->xin, x, (size_t)rows * m->in_dim * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        goto done;
+    for (int i = 0; i < im->g->n_steps; i++) {
+        if (step_run(m, i, B) != 0) goto done;
+        if (outs[i] != NULL) {
+            const kx_val* v = &im->g->vals[i + 1];
+            if (cudaMemcpyAsync(outs[i], val_ptr(im, i + 1), (size_t)B * v->r * v->c * sizeof(float), cudaMemcpyDeviceToHost,
+                                st) != cudaSuccess)
+                goto done;
+        }
+    }
+    rc = cudaStreamSynchronize(st) == cudaSuccess ? 0 : -1;
+done:
+    dev_guard_leave(m, prev);
+    return rc;
 }
 
 /* -------------------------------------------------------------------------------- C ABI (capi) */

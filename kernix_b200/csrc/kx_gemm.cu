@@ -50,9 +50,23 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// Epilogue activation: the configurations' activations (none, ReLU, GELU) are compiled into the kernel; the
+// other thirteen go through one out-of-line call, which keeps the unrolled epilogue small enough for the
+// instruction cache.
+constexpr int ACT_GENERIC = 99;
+__device__ __noinline__ float act_outline(int act, float v, float alpha) { return kx::act_apply(act, v, alpha); }
+template <int ACTC>
+__device__ __forceinline__ float epi_act(float v, int act, float alpha) {
+    if constexpr (ACTC == ACT_GENERIC) return act_outline(act, v, alpha);
+    else return kx::act_apply(ACTC, v, alpha);
+}
+inline int act_class(int act) { return act == -1 || act == 0 || act == 1 ? act : ACT_GENERIC; }
+
 struct SmemCtl {
     uint64_t full[8];
     uint64_t empty[8];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
     uint64_t accf;
     uint32_t tmem;
     int abort;
@@ -72,17 +86,33 @@ __device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], in
 }
 
 // ------------------------------------------------------------------------------------------ int8
+// Persistent kernel: each CTA walks output tiles t = blockIdx.x, +gridDim.x, ... (M-tile fastest so the CTAs
+// running at once share B tiles in L2). TMEM holds two 128 x BN int32 accumulators; the MMA warp fills one
+// while the 8 epilogue warps drain the other, so the epilogue of tile i overlaps the mainloop of tile i+1.
+// Epilogue: thread-per-row tcgen05.ld of 32 columns -> 128-byte-swizzled per-warp staging tile -> each lane
+// then owns 4 columns of 8 rows, applies ((float)acc*sx)*scale + bias and the activation, and the warp writes
+// four full 128-byte row segments per store instruction.
 template <int BN, int STAGES>
 struct I8Cfg {
     static constexpr int BK = 128;  // bytes of K per stage (one 128-byte swizzle row)
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
-    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + 1024 + static_cast<int>(sizeof(SmemCtl));
-    static constexpr uint32_t TMEM_COLS = BN;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int STAGE_EPI = EPI_WARPS * 32 * 32 * 4;  // per-warp 32 x 32 x 4-byte staging tiles
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + STAGE_EPI + 1024 + static_cast<int>(sizeof(SmemCtl));
+    static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
 };
 
-template <int BN, int STAGES, bool ACC_ONLY>
-__global__ void __launch_bounds__(192, 1)
+struct TileMap {  // tile t -> (m-tile, n-tile), M-tile fastest
+    int m_tiles, n_tiles;
+    __device__ __forceinline__ void at(int t, int& mt, int& nt) const {
+        nt = t / m_tiles;
+        mt = t - nt * m_tiles;
+    }
+};
+
+template <int BN, int STAGES, bool ACC_ONLY, int ACTC>
+__global__ void __launch_bounds__(320, 1)
 k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
           const float* __restrict__ sx, const float* __restrict__ scale, const float* __restrict__ bias,
           float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N, int K, int act, float alpha,
@@ -92,17 +122,23 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     uint8_t* smem = align1024(smem_raw);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
-    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(sB + STAGES * C::B_BYTES);
+    uint8_t* sE = sB + STAGES * C::B_BYTES;
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(sE + C::STAGE_EPI);
     volatile int* abort_flag = &ctl->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nk = (K + C::BK - 1) / C::BK;
+    const TileMap tm{(M + BM - 1) / BM, (N + BN - 1) / BN};
+    const int n_tiles = tm.m_tiles * tm.n_tiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             kx::mbar_init(&ctl->full[s], 1);
             kx::mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            kx::mbar_init(&ctl->acc_full[b], 1);
+            kx::mbar_init(&ctl->acc_empty[b], C::EPI_WARPS);
         }
         kx::mbar_init(&ctl->accf, 1);
         ctl->abort = 0;
@@ -122,67 +158,140 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         if (lane == 0) {
             kx::tma_prefetch_desc(&tmA);
             kx::tma_prefetch_desc(&tmB);
-            int issued = 0;
-            for (int kb = 0; kb < nk; kb++) {
-                const int s = kb % STAGES;
-                if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
-                kx::mbar_arrive_expect_tx(&ctl->full[s], C::A_BYTES + C::B_BYTES);
-                kx::tma_load_2d(sA + s * C::A_BYTES, &tmA, kb * C::BK, m0, &ctl->full[s]);
-                kx::tma_load_2d(sB + s * C::B_BYTES, &tmB, kb * C::BK, n0, &ctl->full[s]);
-                issued = kb + 1;
+            int it = 0;
+            for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+                int mt, nt;
+                tm.at(t, mt, nt);
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                    kx::mbar_arrive_expect_tx(&ctl->full[s], C::A_BYTES + C::B_BYTES);
+                    kx::tma_load_2d(sA + s * C::A_BYTES, &tmA, kb * C::BK, mt * BM, &ctl->full[s]);
+                    kx::tma_load_2d(sB + s * C::B_BYTES, &tmB, kb * C::BK, nt * BN, &ctl->full[s]);
+                }
             }
             if (*abort_flag)  // let copies already in flight land before the CTA's shared memory goes away
-                for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
-                    drain_wait(&ctl->full[kb % STAGES], (kb / STAGES) & 1);
+                for (int i = it > STAGES ? it - STAGES : 0; i < it; i++) drain_wait(&ctl->full[i % STAGES], (i / STAGES) & 1);
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = kx::idesc_i8(BM, BN);
-            for (int kb = 0; kb < nk; kb++) {
-                const int s = kb % STAGES;
-                if (!kx::mbar_wait(&ctl->full[s], (kb / STAGES) & 1, abort_flag, status)) break;
+            int it = 0, j = 0;
+            for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, j++) {
+                const int b = j & 1;
+                if (!kx::mbar_wait(&ctl->acc_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, status)) break;
                 kx::tc_fence_after();
-                const uint32_t a0 = kx::smem_u32(sA + s * C::A_BYTES), b0 = kx::smem_u32(sB + s * C::B_BYTES);
+                const uint32_t d = tmem + b * BN;
+                bool ok = true;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->full[s], (it / STAGES) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    kx::tc_fence_after();
+                    const uint32_t a0 = kx::smem_u32(sA + s * C::A_BYTES), b0 = kx::smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < C::BK / 32; kk++)
-                    kx::mma_i8(tmem, kx::desc_sw128_kmajor(a0 + kk * 32), kx::desc_sw128_kmajor(b0 + kk * 32), idesc,
-                               (kb | kk) != 0);
-                kx::mma_commit(&ctl->empty[s]);
+                    for (int kk = 0; kk < C::BK / 32; kk++)
+                        kx::mma_i8(d, kx::desc_sw128_kmajor(a0 + kk * 32), kx::desc_sw128_kmajor(b0 + kk * 32), idesc,
+                                   (kb | kk) != 0);
+                    kx::mma_commit(&ctl->empty[s]);
+                }
+                if (!ok) break;
+                kx::mma_commit(&ctl->acc_full[b]);
             }
-            kx::mma_commit(&ctl->accf);  // arrives once every MMA above has completed
+            kx::mma_commit(&ctl->accf);  // completes once every MMA issued above has finished
+            drain_wait(&ctl->accf, 0);
         }
         __syncwarp();
     } else {
-        const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
-        drain_wait(&ctl->accf, 0);
-        kx::tc_fence_after();
-        const bool ok = !*abort_flag;
-        const float sxr = (ok && row < M && !ACC_ONLY) ? sx[row] : 0.0f;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
-            kx::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
-            kx::tmem_ld_wait();
-            const int col = n0 + c0;
-            if (!ok || row >= M || col >= N) continue;
-            const int nv = N - col;
-            if (ACC_ONLY) {
-                int32_t* dst = acc_out + static_cast<size_t>(row) * ldy + col;
-                for (int j = 0; j < 32; j++)
-                    if (j < nv) dst[j] = static_cast<int32_t>(r[j]);
-            } else {
-                float v[32];
+        const int ew = warp - 2;           // 0..7
+        const int q = warp & 3;            // TMEM lane quarter this warp may read
+        const int c_lo = (ew >> 2) * (BN / 2);  // this warp's half of the tile's columns
+        float* stg = reinterpret_cast<float*>(sE + ew * 4096);
+        const int sub = lane >> 3, chunk = lane & 7;  // column phase: rows 4i + sub, columns 4*chunk .. +3
+        int j = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, j++) {
+            int mt, nt;
+            tm.at(t, mt, nt);
+            const int b = j & 1;
+            if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
+            kx::tc_fence_after();
+            const int r0 = mt * BM + q * 32;  // first row of this warp's 32
+            float sxr[8];
+            if (!ACC_ONLY) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int cc = col + (j < nv ? j : 0);
-                    float t = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sxr), __ldg(scale + cc));
-                    t = __fadd_rn(t, bias ? __ldg(bias + cc) : 0.0f);
-                    v[j] = kx::act_apply(act, t, alpha);
+                for (int i = 0; i < 8; i++) {
+                    const int gr = r0 + 4 * i + sub;
+                    sxr[i] = gr < M ? __ldg(sx + gr) : 0.0f;
                 }
-                float* dst = y + static_cast<size_t>(row) * ldy + col;
-                store_row32(dst, v, nv, ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0));
             }
+#pragma unroll 1
+            for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
+                uint32_t r[32];
+                kx::tmem_ld32(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16) + c, r);
+                kx::tmem_ld_wait();
+                // row phase: this thread's row -> staging (16-byte chunk k of row `lane` at chunk k ^ (lane & 7))
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    *reinterpret_cast<uint4*>(stg + lane * 32 + ((k ^ (lane & 7)) << 2)) =
+                        make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+                __syncwarp();
+                const int gc = nt * BN + c + 4 * chunk;
+                float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f), bi4 = sc4;
+                if (!ACC_ONLY && gc < N) {
+                    if (gc + 3 < N) {
+                        sc4 = *reinterpret_cast<const float4*>(scale + gc);  // scale/bias: 16-byte aligned, padded
+                        if (bias) bi4 = *reinterpret_cast<const float4*>(bias + gc);
+                    } else {
+                        sc4.x = scale[gc];
+                        if (gc + 1 < N) sc4.y = scale[gc + 1];
+                        if (gc + 2 < N) sc4.z = scale[gc + 2];
+                        if (bias) {
+                            bi4.x = bias[gc];
+                            if (gc + 1 < N) bi4.y = bias[gc + 1];
+                            if (gc + 2 < N) bi4.z = bias[gc + 2];
+                        }
+                    }
+                }
+                const bool vec = (gc + 3 < N) && ((ldy & 3) == 0);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int rr = 4 * i + sub;
+                    const int gr = r0 + rr;
+                    const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 32 + ((chunk ^ (rr & 7)) << 2));
+                    if (gr >= M || gc >= N) continue;
+                    if (ACC_ONLY) {
+                        int32_t* dst = acc_out + static_cast<size_t>(gr) * ldy + gc;
+                        const int32_t e[4] = {static_cast<int32_t>(v.x), static_cast<int32_t>(v.y), static_cast<int32_t>(v.z),
+                                              static_cast<int32_t>(v.w)};
+                        for (int e2 = 0; e2 < 4; e2++)
+                            if (gc + e2 < N) dst[e2] = e[e2];
+                    } else {
+                        const float s = sxr[i];
+                        float o[4];
+                        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+                        const float scv[4] = {sc4.x, sc4.y, sc4.z, sc4.w}, biv[4] = {bi4.x, bi4.y, bi4.z, bi4.w};
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; e2++) {
+                            float tv = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(vv[e2])), s), scv[e2]);
+                            tv = __fadd_rn(tv, biv[e2]);
+                            o[e2] = epi_act<ACTC>(tv, act, alpha);
+                        }
+                        float* dst = y + static_cast<size_t>(gr) * ldy + gc;
+                        if (vec) {
+                            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                        } else {
+                            for (int e2 = 0; e2 < 4; e2++)
+                                if (gc + e2 < N) dst[e2] = o[e2];
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            kx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[b]);
         }
     }
     kx::tc_fence_before();
@@ -223,7 +332,7 @@ struct ConvGeom {
     int H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog;
 };
 
-template <int BN, int STAGES, bool CONV>
+template <int BN, int STAGES, bool CONV, int ACTC>
 __global__ void __launch_bounds__(320, 1)
 k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
               const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
@@ -326,7 +435,7 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
                 const int cc = col + (j < nv ? j : 0);
                 float t = __uint_as_float(r[j]);
                 if (bias) t = __fadd_rn(t, __ldg(bias + cc));
-                v[j] = kx::act_apply(act, t, alpha);
+                v[j] = epi_act<ACTC>(t, act, alpha);
             }
             store_row32(y + static_cast<size_t>(row) * ldy + col, v, nv,
                         ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0));
@@ -491,21 +600,39 @@ int make_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint
     return 0;
 }
 
-// raise the dynamic shared-memory limit of a kernel once per device (the attribute is per device context)
-template <typename Kern>
-int set_smem_once(Kern k, int bytes) {
-    static uint64_t done = 0;  // bit d: done on device d
+// raise the dynamic shared-memory limit of a kernel once per (kernel, device); the attribute is per device context
+int set_smem_once(const void* kern, int bytes) {
+    struct Done {
+        const void* k;
+        uint64_t devs;
+    };
+    static Done done[32];
+    static int n_done = 0;
     static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return -1;
     std::lock_guard<std::mutex> g(mu);
-    if (dev < 64 && (done >> dev) & 1) return 0;
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -1;
-    if (dev < 64) done |= uint64_t(1) << dev;
+    int i = 0;
+    while (i < n_done && done[i].k != kern) i++;
+    if (i < n_done && dev < 64 && ((done[i].devs >> dev) & 1)) return 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return -1;
+    if (i == n_done && n_done < 32) done[n_done++] = Done{kern, 0};
+    if (i < n_done && dev < 64) done[i].devs |= uint64_t(1) << dev;
     return 0;
 }
 
-template <int BN, bool ACC_ONLY>
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev < 64 && cached[dev]) return cached[dev];
+    int n = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (dev < 64) cached[dev] = n;
+    return n;
+}
+
+template <int BN, bool ACC_ONLY, int ACTC>
 int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
               const float* bias, float* y, int32_t* acc, int ldy, int m, int n, int k, int act, float alpha, int* status,
               cudaStream_t st) {
@@ -517,14 +644,15 @@ int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int 
         make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, static_cast<uint64_t>(ldw), static_cast<uint64_t>(n),
                     static_cast<uint64_t>(ldw), C::BK, BN) != 0)
         return -1;
-    auto kern = k_gemm_i8<BN, STAGES, ACC_ONLY>;
-    if (set_smem_once(kern, C::SMEM) != 0) return -1;
-    dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
-    kern<<<grid, 192, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
+    auto kern = k_gemm_i8<BN, STAGES, ACC_ONLY, ACTC>;
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+    const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    kern<<<grid, 320, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-template <int BN, bool CONV>
+template <int BN, bool CONV, int ACTC>
 int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
                int groups) {
@@ -536,8 +664,8 @@ int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int 
         make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
                     static_cast<uint64_t>(ldw) * 4, C::BK, BN) != 0)
         return -1;
-    auto kern = k_gemm_tf32x3<BN, STAGES, CONV>;
-    if (set_smem_once(kern, C::SMEM) != 0) return -1;
+    auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC>;
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
     kern<<<grid, 320, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
@@ -580,6 +708,32 @@ __global__ void k_prep_f32(const float* __restrict__ w, int k, int n, float* __r
     }
 }
 
+template <int BN>
+int dispatch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale, const float* bias,
+                float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st) {
+    switch (act_class(act)) {
+    case -1: return launch_i8<BN, false, -1>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+    case 0: return launch_i8<BN, false, 0>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+    case 1: return launch_i8<BN, false, 1>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+    default:
+        return launch_i8<BN, false, ACT_GENERIC>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+    }
+}
+
+template <int BN, bool CONV>
+int dispatch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
+                 int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
+                 int groups) {
+    switch (act_class(act)) {
+    case -1: return launch_f32<BN, CONV, -1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
+    case 0: return launch_f32<BN, CONV, 0>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
+    case 1: return launch_f32<BN, CONV, 1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
+    default:
+        return launch_f32<BN, CONV, ACT_GENERIC>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv,
+                                                 groups);
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -590,17 +744,26 @@ int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int
     if (m <= 0 || n <= 0) return 0;
     if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15)) return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (n <= 128)
-        return launch_i8<128, false>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
-    return launch_i8<256, false>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+    if (n <= 128) return dispatch_i8<128>(xq, ldq, sx, wq, ldw, scale, bias, y, ldy, m, n, k, act, alpha, status, st);
+    return dispatch_i8<256>(xq, ldq, sx, wq, ldw, scale, bias, y, ldy, m, n, k, act, alpha, status, st);
+}
+
+int kx_linear_i8(const float* x, int ldx, int rows, int k, const int8_t* wq, int ldw, const float* scale, const float* bias,
+                 float* y, int ldy, int n, int act, float alpha, int8_t* xq_scratch, float* sx_scratch, int* status,
+                 void* stream) {
+    if (rows <= 0 || n <= 0) return 0;
+    if (xq_scratch == nullptr || sx_scratch == nullptr) return -1;
+    const int ldq = (k + 15) / 16 * 16;
+    if (kx_quant_rows(x, ldx, rows, k, xq_scratch, ldq, sx_scratch, stream) != 0) return -1;
+    return kx_gemm_i8(xq_scratch, ldq, sx_scratch, wq, ldw, scale, bias, y, ldy, rows, n, k, act, alpha, status, stream);
 }
 
 int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
                    int* status, void* stream) {
     if (m <= 0 || n <= 0) return 0;
     if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15)) return -1;
-    return launch_i8<256, true>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, acc, ldacc, m, n, k, -1, 0.0f,
-                                status, static_cast<cudaStream_t>(stream));
+    return launch_i8<256, true, -1>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, acc, ldacc, m, n, k, -1, 0.0f,
+                                    status, static_cast<cudaStream_t>(stream));
 }
 
 int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
@@ -609,8 +772,8 @@ int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, i
     if (k <= 0 || k > ldx || k > ldw || (ldw & 3)) return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const ConvGeom cv{};
-    if (n <= 128) return launch_f32<128, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
-    return launch_f32<256, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
+    if (n <= 128) return dispatch_f32<128, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
+    return dispatch_f32<256, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
 }
 
 int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y, int B, int H,
@@ -624,10 +787,10 @@ int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, c
     const ConvGeom cv{H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (cog <= 128)
-        return launch_f32<128, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status, st,
-                                     cv, groups);
-    return launch_f32<256, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status, st,
-                                 cv, groups);
+        return dispatch_f32<128, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status,
+                                       st, cv, groups);
+    return dispatch_f32<256, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status, st,
+                                   cv, groups);
 }
 
 int kx_prep_i8_weight(const int8_t* q_kn, int k, int n, int8_t* wq, int ldw, void* stream) {

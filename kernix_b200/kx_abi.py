@@ -10,6 +10,7 @@ _vp, _i, _l, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_long, ctypes.c_fl
 SIGNATURES = {
     "kx_quant_rows": [_vp, _i, _i, _i, _vp, _i, _vp, _vp],
     "kx_gemm_i8": [_vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp],
+    "kx_linear_i8": [_vp, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _f, _vp, _vp, _vp, _vp],
     "kx_gemm_i8_acc": [_vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp],
     "kx_prep_i8_weight": [_vp, _i, _i, _vp, _i, _vp],
     "kx_gemm_f32": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp],
@@ -27,10 +28,11 @@ SIGNATURES = {
     "kx_pad2d": [_vp, _vp] + [_i] * 8 + [_vp],
     "kx_upsample2d": [_vp, _vp] + [_i] * 8 + [_vp],
     "kx_embedding": [_vp, _l, _vp, _i, _i, _vp, _vp],
-    "kx_conv_depthwise": [_vp, _vp, _vp, _vp] + [_i] * 16 + [_i, _f, _vp],
-    "kx_conv_f32": [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 16 + [_i, _i, _f, _vp, _vp],
+    "kx_conv_depthwise": [_vp, _vp, _vp, _vp] + [_i] * 15 + [_i, _f, _vp],
+    "kx_conv_f32": [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 16 + [_i, _f, _vp, _vp],
     "kx_attention": [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "kx_fma_relu": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "kx_knx_plan": [ctypes.c_char_p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i],
     "kx_knx_inspect": [ctypes.c_char_p, ctypes.POINTER(_l), ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i), _i,
                        ctypes.c_char_p, _i],
 }
@@ -71,3 +73,13 @@ def inspect(path):
     return dict(n_steps=n, in_dim=info[1], out_dim=info[2], seq_len=info[3], layout=info[4],
                 in_shape=list(shapes[:info[5]]), out_shape=list(shapes[4:4 + info[6]]), n_storage=info[7],
                 version=info[8], storage_per_sample=info[9], steps=list(zip(kinds[:n], acts[:n])))
+
+
+def plan(path):
+    """(storage id per value, last reader per value) of the runtime's storage plan."""
+    st = (ctypes.c_int * 2048)()
+    last = (ctypes.c_int * 2048)()
+    n = lib().kx_knx_plan(path.encode() if isinstance(path, str) else path, st, last, 2048)
+    if n < 0:
+        raise ValueError("rejected")
+    return list(st[:n]), list(last[:n])

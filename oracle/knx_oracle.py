@@ -400,25 +400,30 @@ def load(path_or_bytes):
         vals[0] = _val([seq, in_dim] if seq else [in_dim])
     for s in steps:
         vals.append(_infer(s, vals))
-    # ACT fusion count (:1530-1555): an ACT whose input is a LINEAR/CONV output read only by it
+    # ACT fusion (:1530-1555): an ACT whose input is a LINEAR/CONV output read only by it merges into that step.
+    # fused_map[v] = value id of original value v in the fused graph (the runtime's numbering).
     cons = [0] * (n_ops + 1)
     for s in steps:
         for i in s["inp"]:
             cons[i] += 1
     cons[n_ops] += 1
-    fused_act = {}
-    fused = 0
+    fmap = [0] * (n_ops + 1)
+    kept = []  # (kind, act) of fused steps
     for i, s in enumerate(steps):
-        src = s["inp"][0]
-        if s["kind"] == OP["ACT"] and src > 0 and cons[src] == 1:
-            p = steps[src - 1]
-            if p["kind"] in (OP["LINEAR"], OP["CONV"]) and fused_act.get(src - 1, ACT_NONE) == ACT_NONE and \
-                    p["act"] == ACT_NONE and (src - 1) not in fused_act:
-                fused_act[src - 1] = s["act"]
-                fused += 1
+        inp = [fmap[v] for v in s["inp"]]
+        if s["kind"] == OP["ACT"] and inp[0] > 0 and cons[s["inp"][0]] == 1:
+            pk, pa = kept[inp[0] - 1]
+            if pk in (OP["LINEAR"], OP["CONV"]) and pa == ACT_NONE:
+                kept[inp[0] - 1] = (pk, s["act"])
+                fmap[i + 1] = inp[0]
+                continue
+        kept.append((s["kind"], s["act"]))
+        fmap[i + 1] = len(kept)
+    fused = n_ops - len(kept)
     vin, vout = vals[0], vals[n_ops]
     return dict(ver=ver, layout=layout, steps=steps, vals=vals, in_shape=vin["d"], out_shape=vout["d"],
-                in_dim=vin["c"], seq_len=vin["r"], out_dim=vout["r"] * vout["c"], n_fused_steps=n_ops - fused)
+                in_dim=vin["c"], seq_len=vin["r"], out_dim=vout["r"] * vout["c"], n_fused_steps=n_ops - fused,
+                fused_map=fmap, fused_steps=kept)
 
 
 # ------------------------------------------------------------------------------------------ arithmetic
@@ -681,8 +686,9 @@ def attention(s, q2, vq, k2, v2, vv):
     return dense(ctx, _wf(s["wo"]), s["bo"], ACT_NONE, 0)
 
 
-def forward(model, x):
-    """kernix_model_forward on (rows, in_dim) float32, rows a multiple of seq_len. Returns (B, out_dim)."""
+def forward(model, x, trace=None):
+    """kernix_model_forward on (rows, in_dim) float32, rows a multiple of seq_len. Returns (B, out_dim).
+    trace: optional list that receives every value (index = original value id, (B*r) x c arrays)."""
     vals = model["vals"]
     x = np.ascontiguousarray(x, F32).reshape(-1, model["in_dim"])
     B = x.shape[0] // model["seq_len"]
@@ -757,6 +763,8 @@ def forward(model, x):
         else:
             raise NotImplementedError(f"{OP_NAMES[k]} is outside the GPU path")
         views.append(np.ascontiguousarray(y, F32).reshape(B * vo["r"], vo["c"]))
+    if trace is not None:
+        trace.extend(views)
     return views[-1].reshape(B, -1)
 
 

@@ -32,3 +32,10 @@ KX_REF_API int kx_ref_model_steps(const kernix_model* m, int* kind, int* act, in
     for (int i = 0; i < m->n_steps && i < cap; i++) { kind[i] = m->steps[i].kind; act[i] = m->steps[i].act; }
     return m->n_steps;
 }
+
+/* storage buffer of every value after planning (-1 = caller input), for comparing buffer plans */
+KX_REF_API int kx_ref_model_plan(const kernix_model* m, int* st, int* last, int cap)
+{
+    for (int v = 0; v < m->n_vals && v < cap; v++) { st[v] = m->vals[v].st; last[v] = m->vals[v].last; }
+    return m->n_vals;
+}

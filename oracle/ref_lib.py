@@ -45,6 +45,8 @@ def lib():
         L.kx_ref_model_info.restype = None
         L.kx_ref_model_steps.argtypes = [vp, ip, ip, ctypes.c_int]
         L.kx_ref_model_steps.restype = ctypes.c_int
+        L.kx_ref_model_plan.argtypes = [vp, ip, ip, ctypes.c_int]
+        L.kx_ref_model_plan.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -74,6 +76,12 @@ class RefModel:
         act = (ctypes.c_int * 1024)()
         n = lib().kx_ref_model_steps(self.h, kind, act, 1024)
         return list(zip(kind[:n], act[:n]))
+
+    def plan(self):
+        st = (ctypes.c_int * 2048)()
+        last = (ctypes.c_int * 2048)()
+        n = lib().kx_ref_model_plan(self.h, st, last, 2048)
+        return list(st[:n]), list(last[:n])
 
     def set_workspace_limit(self, nbytes):
         lib().kernix_capi_set_workspace_limit(self.h, int(nbytes))
