@@ -42,6 +42,18 @@ KERNIX_API int kx_linear_i8(const float* x, int ldx, int rows, int k, const int8
                             const float* bias, float* y, int ldy, int n, int act, float alpha, int8_t* xq_scratch,
                             float* sx_scratch, int* status, void* stream);
 
+/* kx_linear_i8 for callers that cannot allocate device memory (latency-critical code that cannot take cudaMalloc's
+ * device-wide synchronisation, or hosts whose allocator forbids extra device allocations). No counterpart in the
+ * reference. Same arguments and result as kx_linear_i8 minus the two scratch buffers: they come from one
+ * KX_NOALLOC_SCRATCH_BYTES array compiled into the library (held on every GPU that loads it until exit), so
+ * rows * (k rounded up to 16) + 4 * rows (+ alignment) must fit, else it returns -1 with a message. The first call on
+ * a device looks the array up (cudaGetSymbolAddress); make it before any stream capture. Calls share the array:
+ * calls whose work overlaps on the GPU race, so order them on one stream. Allocates nothing. */
+#define KX_NOALLOC_SCRATCH_BYTES (16 << 20)
+KERNIX_API int kx_linear_i8_noalloc(const float* x, int ldx, int rows, int k, const int8_t* wq, int ldw, const float* scale,
+                                    const float* bias, float* y, int ldy, int n, int act, float alpha, int* status,
+                                    void* stream);
+
 /* int32 accumulators only (acc[row][col], leading dimension ldacc): exposes the integer result for tests. */
 KERNIX_API int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
                    int* status, void* stream);
