@@ -34,6 +34,9 @@ DIMS = [1024, 4096, 4096, 1024]
 METRIC = "samples/s, int8 MLP 1024-4096-4096-1024 (config c2), batch 4096 per GPU"
 WORKLOAD = "c2: int8-quantised MLP 1024-4096-4096-1024, GELU hidden, I8_COL per-output-channel weights, batch 4096"
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) per int8-GEMM op from the ncu capture in profiles/k_gemm_i8_8192x4096x4096_full.md:
+# 156.3 MB for 274.9 GOP; the roofline's traffic per launch is this ratio times the launch's ops.
+GEMM_DRAM_BYTES_PER_OP = 156.3e6 / 274.9e9
 
 
 def parse():
@@ -42,8 +45,35 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kernix", "reference"], default="kernix")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="time box of the CPU-baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="time box of the CPU-baseline sample (0: none)")
+    ap.add_argument("--kernel-case", type=int, default=0, metavar="M",
+                    help="profiling case: only run the int8 GEMM of c2's 4096x4096 layer with M rows, 3 launches, then exit")
     return ap.parse_args()
+
+
+def kernel_case(m_rows):
+    """Three launches of k_gemm_i8 (GELU epilogue) on an M x 4096 x 4096 problem -- for an ncu capture of one kernel
+    on a case larger than L2 (M = 8192: 32 MB A + 16 MB B + 128 MB C)."""
+    import numpy as np
+    import torch
+
+    from kernix_b200 import build, kx_abi
+    build.build()
+    L = kx_abi.lib()
+    k = n = 4096
+    rng = np.random.default_rng(0)
+    xq = torch.from_numpy(rng.integers(-127, 128, (m_rows, k), dtype=np.int8)).cuda()
+    wq = torch.from_numpy(rng.integers(-127, 128, (n, k), dtype=np.int8)).cuda()
+    sx = torch.full((m_rows,), 0.01, device="cuda")
+    sc = torch.full((n,), 0.001, device="cuda")
+    b = torch.zeros(n, device="cuda")
+    y = torch.empty((m_rows, n), device="cuda")
+    for _ in range(3):
+        if L.kx_gemm_i8(xq.data_ptr(), k, sx.data_ptr(), wq.data_ptr(), k, sc.data_ptr(), b.data_ptr(), y.data_ptr(), n, m_rows,
+                        n, k, 1, 0.0, None, None) != 0:
+            raise RuntimeError("kx_gemm_i8 failed")
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": "k_gemm_i8", "m": m_rows, "n": n, "k": k, "launches": 3}))
 
 
 def model_file(rank):
@@ -287,7 +317,7 @@ def run_kernix(args):
 
     # ---- CPU baseline: the reference's own forward on this host (rank 0 at N = 1 only)
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
         from oracle import ref_lib
         if ref_lib.available():
             v, thr, n, dt = reference_throughput(path, args.cpu_seconds)
@@ -370,13 +400,16 @@ def gemm_roofline(L, torch, np, steps, flush):
         basis = "2 x fallback dense bf16 1.59 PFLOP/s"
     return {"kernel": "k_gemm_i8 (tcgen05 kind::i8, 128x256 tiles)", "bound": "tensor", "achieved": achieved, "peak": peak,
             "unit": "TOP/s (int8, 2 ops per MAC)", "frac": achieved / peak, "peak_basis": basis,
-            "traffic": None, "per_layer": per,
+            "traffic": GEMM_DRAM_BYTES_PER_OP * tot_ops / len(per),
+            "traffic_note": "bytes per launch, scaled by ops from the ncu capture of M=8192 (profiles/)", "per_layer": per,
             "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
 
 
 if __name__ == "__main__":
     a = parse()
-    if a.impl == "reference":
+    if a.kernel_case:
+        kernel_case(a.kernel_case)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_kernix(a)
