@@ -24,15 +24,28 @@
 #include "kx_kernels.h"
 
 #define KX_ALIGN 256
+#define KX_PIPE_MAX 8             /* pieces a chunk of host rows is split into, at most */
+#define KX_PIPE_MIN_BYTES (1 << 20) /* input bytes of one piece, at least */
 
 struct kx_model_impl {
     kx_graph* g;
     int device;
-    cudaStream_t stream;
+    cudaStream_t stream;  /* kernels */
+    cudaStream_t s_in;    /* host -> device copies of the host-memory forward */
+    cudaStream_t s_out;   /* device -> host copies of the host-memory forward */
+    /* per piece: start / end of its input copy, kernels and output copy (timed, to choose the piece count) */
+    cudaEvent_t ev_is[KX_PIPE_MAX], ev_in[KX_PIPE_MAX], ev_cs[KX_PIPE_MAX], ev_comp[KX_PIPE_MAX];
+    cudaEvent_t ev_os[KX_PIPE_MAX], ev_out[KX_PIPE_MAX];
+    int pipe;             /* pieces per chunk when pipelining ($KERNIX_PIPELINE; default 4) */
+    int pipe_fixed;       /* 1: $KERNIX_PIPELINE was given, use it as is */
+    int pipe_now;         /* pieces per chunk for the current chunk size (decided after two timed calls) */
+    int tune_calls;       /* timed calls at the current chunk size */
+    int last_pieces;      /* pieces of the last chunk of the last call (whose events hold its timings) */
     /* workspace (one arena) */
     void* arena;
     size_t arena_bytes;
-    float** st;           /* device storage buffers */
+    float** st;           /* device storage buffers as the running steps see them (a piece's rows) */
+    float** st_base;      /* the same buffers from their first sample */
     float* xin;           /* device input rows */
     uint8_t* scratch;     /* per-step scratch: int8 activations, attention Q/K/V/context */
     int* status;          /* device status word of bounded waits */
@@ -55,6 +68,15 @@ static void dev_guard_leave(const kernix_model* m, int prev) {
 }
 
 static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+/* wait for the model's three streams; the first error seen, or cudaSuccess */
+static cudaError_t sync_all(struct kx_model_impl* im) {
+    cudaError_t e = cudaSuccess, f;
+    cudaStream_t ss[3] = {im->s_in, im->stream, im->s_out};
+    for (int i = 0; i < 3; i++)
+        if (ss[i] && (f = cudaStreamSynchronize(ss[i])) != cudaSuccess && e == cudaSuccess) e = f;
+    return e;
+}
 
 /* ------------------------------------------------------------------------------- weight upload */
 /* Every copy and preparation kernel of the load goes on the model's stream: a legacy-stream cudaMemcpy from
@@ -213,6 +235,8 @@ static void model_release(kernix_model* m) {
     im->arena_bytes = 0;
     free(im->st);
     im->st = NULL;
+    free(im->st_base);
+    im->st_base = NULL;
     im->xin = NULL;
     im->scratch = NULL;
     im->status = NULL;
@@ -238,7 +262,8 @@ static int model_alloc(kernix_model* m, int rows) {
     size_t off = 0;
     size_t* st_off = calloc((size_t)g->n_st + 1, sizeof(size_t));
     im->st = calloc((size_t)g->n_st + 1, sizeof(float*));
-    if (st_off == NULL || im->st == NULL) {
+    im->st_base = calloc((size_t)g->n_st + 1, sizeof(float*));
+    if (st_off == NULL || im->st == NULL || im->st_base == NULL) {
         free(st_off);
         return -1;
     }
@@ -260,13 +285,15 @@ static int model_alloc(kernix_model* m, int rows) {
     }
     im->arena_bytes = off;
     uint8_t* base = (uint8_t*)im->arena;
-    for (int k = 0; k < g->n_st; k++) im->st[k] = (float*)(base + st_off[k]);
+    for (int k = 0; k < g->n_st; k++) im->st[k] = im->st_base[k] = (float*)(base + st_off[k]);
     im->xin = (float*)(base + xin_off);
     im->scratch = base + scr_off;
     im->status = (int*)(base + status_off);
     free(st_off);
     if (cudaMemsetAsync(im->status, 0, sizeof(int), im->stream) != cudaSuccess) return -1;
     m->batch = rows;
+    im->pipe_now = im->pipe;
+    im->tune_calls = 0;
     return 0;
 }
 
@@ -428,12 +455,8 @@ static int chunk_run(kernix_model* m, int B) {
     return 0;
 }
 
-/* Enqueue the forward of rows of x into out (samples x out_dim) on im->stream. x / out are host memory
- * (copied per chunk) or, with on_device, device memory (the first chunk's input is read in place). */
-static int forward_enqueue(kernix_model* m, const float* x, int rows, float* out, int on_device) {
-    struct kx_model_impl* im = m->impl;
-    const int samples = rows / m->seq_len;
-    if (samples == 0) return 0;
+/* samples per chunk under the workspace limit (the reference's rule, include/kernix_model.h:2040-2050) */
+static int chunk_samples(const kernix_model* m, int samples) {
     int chunk = samples;
     if (m->ws_limit > 0 && m->ws_per_sample > 0) {
         const size_t fixed = m->ws_fixed * sizeof(float), avail = m->ws_limit > fixed ? m->ws_limit - fixed : 0;
@@ -441,46 +464,127 @@ static int forward_enqueue(kernix_model* m, const float* x, int rows, float* out
         if (c < 1) c = 1;
         if (c < (size_t)samples) chunk = (int)c;
     }
+    return chunk;
+}
+
+/* Point the running steps at samples [a, a + n) of the chunk arena: the input rows and every storage buffer are
+ * offset by a samples (a buffer holds st_cap floats per sample), so pieces of one chunk use disjoint memory and
+ * can be in flight together. The per-step scratch is shared: pieces run one after another on the kernel stream. */
+static void piece_view(struct kx_model_impl* im, float* xin_base, int a, size_t in_per_sample) {
+    im->xin = xin_base + (size_t)a * in_per_sample;
+    for (int k = 0; k < im->g->n_st; k++) im->st[k] = im->st_base[k] + (size_t)a * im->g->st_cap[k];
+}
+
+/* Enqueue the forward of device rows d_x into d_out (samples x out_dim) on im->stream, chunk by chunk. The model
+ * input is never written (the plan keeps it read-only), so each chunk reads it in place. */
+static int forward_enqueue_device(kernix_model* m, const float* x, int rows, float* out) {
+    struct kx_model_impl* im = m->impl;
+    const int samples = rows / m->seq_len;
+    if (samples == 0) return 0;
+    const int chunk = chunk_samples(m, samples);
     const int crow = chunk * m->seq_len;
     if (crow != m->batch && model_alloc(m, crow) != 0) return -1;
-    cudaStream_t st = im->stream;
-    const float* yv = val_ptr(im, im->g->out_v);
-    const enum cudaMemcpyKind h2d = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    const enum cudaMemcpyKind d2h = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
     float* const xin_own = im->xin;
     for (int s0 = 0; s0 < samples; s0 += chunk) {
         const int n = samples - s0 < chunk ? samples - s0 : chunk;
-        const size_t in_floats = (size_t)n * m->seq_len * m->in_dim;
-        const float* src = x + (size_t)s0 * m->seq_len * m->in_dim;
-        int rc;
-        const float* yc = yv;
-        if (on_device) { /* the model input is never written (the plan keeps it read-only): read it in place */
-            im->xin = (float*)src;
-            rc = chunk_run(m, n);
-            yc = val_ptr(im, im->g->out_v); /* the input itself when the graph is only views of it */
-            im->xin = xin_own;
-        } else {
-            if (cudaMemcpyAsync(im->xin, src, in_floats * sizeof(float), h2d, st) != cudaSuccess) return -1;
-            rc = chunk_run(m, n);
-        }
+        im->xin = (float*)(x + (size_t)s0 * m->seq_len * m->in_dim);
+        const int rc = chunk_run(m, n);
+        const float* yc = val_ptr(im, im->g->out_v); /* the input itself when the graph is only views of it */
+        im->xin = xin_own;
         if (rc != 0) return -1;
-        if (cudaMemcpyAsync(out + (size_t)s0 * m->out_dim, yc, (size_t)n * m->out_dim * sizeof(float), d2h, st) !=
-            cudaSuccess)
+        if (cudaMemcpyAsync(out + (size_t)s0 * m->out_dim, yc, (size_t)n * m->out_dim * sizeof(float),
+                            cudaMemcpyDeviceToDevice, im->stream) != cudaSuccess)
             return -1;
     }
     return 0;
 }
 
-/* host-memory forward: enqueue, then wait and check the status word */
+/* Enqueue the forward of host rows x into host out. Each chunk is cut into up to im->pipe_now pieces; piece p's
+ * host -> device copy (stream s_in), kernels (stream) and device -> host copy (s_out) are ordered by events, so
+ * the copies of one piece overlap the kernels of its neighbours and the two copy directions overlap each other.
+ * Piece p of every chunk reuses arena region p: its input copy waits until the last user of region p has been
+ * computed and copied out, and its kernels wait for that copy-out too. Rows never mix across pieces, so the
+ * result is the same for any cut (the chunking invariance of include/kernix_model.h:1691-1694). The copies of a
+ * chunk's outputs are issued after all of its kernels, so a copy into pageable memory (which returns only when
+ * done) does not hold back the next piece's launches. */
+static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float* out) {
+    struct kx_model_impl* im = m->impl;
+    const int samples = rows / m->seq_len;
+    if (samples == 0) return 0;
+    const int chunk = chunk_samples(m, samples);
+    const int crow = chunk * m->seq_len;
+    if (crow != m->batch && model_alloc(m, crow) != 0) return -1;
+    const size_t in_ps = (size_t)m->seq_len * m->in_dim; /* input floats per sample */
+    const kx_val* vo = &im->g->vals[im->g->out_v];
+    const int out_st = vo->st;
+    float* const xin_own = im->xin;
+    int rc = 0;
+    for (int s0 = 0; s0 < samples && rc == 0; s0 += chunk) {
+        const int n = samples - s0 < chunk ? samples - s0 : chunk;
+        int P = im->pipe_now < n ? im->pipe_now : n;
+        while (P > 1 && (size_t)(n / P) * in_ps * sizeof(float) < KX_PIPE_MIN_BYTES) P--;
+        const int q = (n + P - 1) / P;
+        P = (n + q - 1) / q;
+        for (int p = 0; p < P && rc == 0; p++) {
+            const int a = p * q, np = n - a < q ? n - a : q;
+            float* xr = xin_own + (size_t)a * in_ps;
+            rc |= cudaStreamWaitEvent(im->s_in, im->ev_comp[p], 0) != cudaSuccess;
+            rc |= cudaStreamWaitEvent(im->s_in, im->ev_out[p], 0) != cudaSuccess;
+            rc |= cudaEventRecord(im->ev_is[p], im->s_in) != cudaSuccess;
+            rc |= cudaMemcpyAsync(xr, x + (size_t)(s0 + a) * in_ps, (size_t)np * in_ps * sizeof(float),
+                                  cudaMemcpyHostToDevice, im->s_in) != cudaSuccess;
+            rc |= cudaEventRecord(im->ev_in[p], im->s_in) != cudaSuccess;
+            rc |= cudaStreamWaitEvent(im->stream, im->ev_in[p], 0) != cudaSuccess;
+            rc |= cudaStreamWaitEvent(im->stream, im->ev_out[p], 0) != cudaSuccess;
+            rc |= cudaEventRecord(im->ev_cs[p], im->stream) != cudaSuccess;
+            if (rc) break;
+            piece_view(im, xin_own, a, in_ps);
+            rc |= chunk_run(m, np) != 0;
+            rc |= cudaEventRecord(im->ev_comp[p], im->stream) != cudaSuccess;
+        }
+        for (int p = 0; p < P && rc == 0; p++) {
+            const int a = p * q, np = n - a < q ? n - a : q;
+            /* the output value of piece p: in its storage buffer at the piece's offset, or (a graph of views
+             * only) in the piece's input rows */
+            const float* yp = out_st < 0 ? xin_own + (size_t)a * in_ps : im->st_base[out_st] + (size_t)a * im->g->st_cap[out_st];
+            rc |= cudaStreamWaitEvent(im->s_out, im->ev_comp[p], 0) != cudaSuccess;
+            rc |= cudaEventRecord(im->ev_os[p], im->s_out) != cudaSuccess;
+            rc |= cudaMemcpyAsync(out + (size_t)(s0 + a) * m->out_dim, yp, (size_t)np * m->out_dim * sizeof(float),
+                                  cudaMemcpyDeviceToHost, im->s_out) != cudaSuccess;
+            rc |= cudaEventRecord(im->ev_out[p], im->s_out) != cudaSuccess;
+        }
+        im->last_pieces = P;
+    }
+    piece_view(im, xin_own, 0, in_ps);
+    return rc ? -1 : 0;
+}
+
+/* Choose the piece count from the timings of the last call's last chunk: cutting pays when the copies are a
+ * sizeable part of the work; when the kernels take more than 3x as long as either copy direction, smaller
+ * pieces only make the kernels less efficient, so the chunk runs whole. Decided once per chunk size, after the
+ * second call (the first one also pays for loading the kernels). */
+static void pipe_tune(struct kx_model_impl* im) {
+    if (im->pipe_fixed || im->tune_calls >= 2 || ++im->tune_calls < 2) return;
+    float t_in = 0.f, t_cmp = 0.f, t_out = 0.f, v;
+    for (int p = 0; p < im->last_pieces; p++) {
+        if (cudaEventElapsedTime(&v, im->ev_is[p], im->ev_in[p]) == cudaSuccess) t_in += v;
+        if (cudaEventElapsedTime(&v, im->ev_cs[p], im->ev_comp[p]) == cudaSuccess) t_cmp += v;
+        if (cudaEventElapsedTime(&v, im->ev_os[p], im->ev_out[p]) == cudaSuccess) t_out += v;
+    }
+    cudaGetLastError();
+    im->pipe_now = t_cmp > 3.0f * (t_in > t_out ? t_in : t_out) ? 1 : im->pipe;
+}
+
+/* host-memory forward: enqueue, then wait for every stream and check the status word */
 static int forward_into(kernix_model* m, const float* x, int rows, float* out) {
     struct kx_model_impl* im = m->impl;
     if (rows / m->seq_len == 0) return 0;
     cudaStream_t st = im->stream;
     if (m->batch > 0 && cudaMemsetAsync(im->status, 0, sizeof(int), st) != cudaSuccess) return -1;
-    if (forward_enqueue(m, x, rows, out, 0) != 0) return -1;
-    if (m->batch <= 0) return -1;
-    cudaMemcpyAsync(im->status_h, im->status, sizeof(int), cudaMemcpyDeviceToHost, st);
-    const cudaError_t e = cudaStreamSynchronize(st);
+    const int rc = forward_enqueue_host(m, x, rows, out);
+    if (rc == 0 && m->batch > 0) cudaMemcpyAsync(im->status_h, im->status, sizeof(int), cudaMemcpyDeviceToHost, st);
+    const cudaError_t e = sync_all(im); /* also on failure: no copy may still be reading x or writing out */
+    if (rc != 0 || m->batch <= 0) return -1;
     if (e != cudaSuccess) {
         fprintf(stderr, "forward: CUDA error %s\n", cudaGetErrorString(e));
         return -1;
@@ -490,6 +594,7 @@ static int forward_into(kernix_model* m, const float* x, int rows, float* out) {
         cudaMemsetAsync(im->status, 0, sizeof(int), st);
         return -1;
     }
+    pipe_tune(im);
     return 0;
 }
 
@@ -550,8 +655,23 @@ KERNIX_API kernix_model* kernix_model_load(const char* path) {
     im->device = env && *env ? atoi(env) : (prev >= 0 ? prev : 0);
     const char* why = NULL;
     if (cudaSetDevice(im->device) != cudaSuccess) why = "no CUDA device";
-    else if (cudaStreamCreateWithFlags(&im->stream, cudaStreamNonBlocking) != cudaSuccess) why = "cannot create a CUDA stream";
-    else if (cudaHostAlloc((void**)&im->status_h, sizeof(int), cudaHostAllocDefault) != cudaSuccess) why = "cannot allocate host memory";
+    else if (cudaStreamCreateWithFlags(&im->stream, cudaStreamNonBlocking) != cudaSuccess ||
+             cudaStreamCreateWithFlags(&im->s_in, cudaStreamNonBlocking) != cudaSuccess ||
+             cudaStreamCreateWithFlags(&im->s_out, cudaStreamNonBlocking) != cudaSuccess)
+        why = "cannot create a CUDA stream";
+    for (int i = 0; why == NULL && i < KX_PIPE_MAX; i++)
+        if (cudaEventCreate(&im->ev_is[i]) != cudaSuccess || cudaEventCreate(&im->ev_in[i]) != cudaSuccess ||
+            cudaEventCreate(&im->ev_cs[i]) != cudaSuccess || cudaEventCreate(&im->ev_comp[i]) != cudaSuccess ||
+            cudaEventCreate(&im->ev_os[i]) != cudaSuccess || cudaEventCreate(&im->ev_out[i]) != cudaSuccess)
+            why = "cannot create a CUDA event";
+    if (why == NULL && cudaHostAlloc((void**)&im->status_h, sizeof(int), cudaHostAllocDefault) != cudaSuccess)
+        why = "cannot allocate host memory";
+    const char* pe = getenv("KERNIX_PIPELINE");
+    im->pipe_fixed = pe && *pe;
+    im->pipe = im->pipe_fixed ? atoi(pe) : 4;
+    if (im->pipe < 1) im->pipe = 1;
+    if (im->pipe > KX_PIPE_MAX) im->pipe = KX_PIPE_MAX;
+    im->pipe_now = im->pipe;
     for (int i = 0; why == NULL && i < g->n_steps; i++)
         if (step_upload(g, &g->steps[i], im->stream) != 0) why = "cannot copy the weights to the GPU";
     if (why == NULL && cudaStreamSynchronize(im->stream) != cudaSuccess) why = "cannot copy the weights to the GPU";
@@ -584,11 +704,18 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
         int prev = -1;
         cudaGetDevice(&prev);
         cudaSetDevice(im->device);
-        if (im->stream) cudaStreamSynchronize(im->stream);
+        sync_all(im);
         model_release(m);
         if (im->g != NULL)
             for (int i = 0; i < im->g->n_steps; i++) step_dev_free(&im->g->steps[i]);
         if (im->status_h) cudaFreeHost(im->status_h);
+        for (int i = 0; i < KX_PIPE_MAX; i++) {
+            cudaEvent_t* evs[6] = {im->ev_is, im->ev_in, im->ev_cs, im->ev_comp, im->ev_os, im->ev_out};
+            for (int k = 0; k < 6; k++)
+                if (evs[k][i]) cudaEventDestroy(evs[k][i]);
+        }
+        if (im->s_in) cudaStreamDestroy(im->s_in);
+        if (im->s_out) cudaStreamDestroy(im->s_out);
         if (im->stream) cudaStreamDestroy(im->stream);
         kx_graph_free(im->g);
         if (prev >= 0) cudaSetDevice(prev);
@@ -601,7 +728,7 @@ KERNIX_API void kernix_model_trim(kernix_model* m) {
     if (m == NULL) return;
     int prev;
     if (dev_guard_enter(m, &prev) != 0) return;
-    cudaStreamSynchronize(m->impl->stream);
+    sync_all(m->impl);
     model_release(m);
     dev_guard_leave(m, prev);
 }
@@ -660,7 +787,7 @@ KERNIX_API int kernix_model_forward_device(kernix_model* m, const float* d_x, in
     if (dev_guard_enter(m, &prev) != 0) return -1;
     cudaStream_t own = im->stream;
     im->stream = (cudaStream_t)stream; /* as given: 0 is the legacy default stream */
-    const int rc = forward_enqueue(m, d_x, rows, d_out, 1);
+    const int rc = forward_enqueue_device(m, d_x, rows, d_out);
     im->stream = own;
     dev_guard_leave(m, prev);
     return rc;

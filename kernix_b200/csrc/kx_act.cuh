@@ -22,7 +22,7 @@ __device__ __forceinline__ float gelu_as(float x) {
     const float z = __fmul_rn(x, 0.70710678f);
     const float t = expf(__fmul_rn(-z, z));
     const float za = __fmul_rn(fabsf(x), 0.70710678f);
-    const float k = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(0.3275911f, za)));
+    const float k = __frcp_rn(__fadd_rn(1.0f, __fmul_rn(0.3275911f, za)));  // == 1 / d, correctly rounded
     float p = __fadd_rn(-1.453152027f, __fmul_rn(k, 1.061405429f));
     p = __fadd_rn(1.421413741f, __fmul_rn(k, p));
     p = __fadd_rn(-0.284496736f, __fmul_rn(k, p));
@@ -33,7 +33,7 @@ __device__ __forceinline__ float gelu_as(float x) {
 }
 
 __device__ __forceinline__ float sigmoidf_ref(float x) {
-    return __fdiv_rn(1.0f, __fadd_rn(expf(-x), 1.0f));
+    return __frcp_rn(__fadd_rn(expf(-x), 1.0f));  // == 1 / d, correctly rounded
 }
 
 __device__ __forceinline__ float act_apply(int act, float x, float alpha) {

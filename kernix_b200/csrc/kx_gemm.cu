@@ -88,17 +88,21 @@ __device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], in
 // ------------------------------------------------------------------------------------------ int8
 // Persistent kernel: each CTA walks output tiles t = blockIdx.x, +gridDim.x, ... (M-tile fastest so the CTAs
 // running at once share B tiles in L2). TMEM holds two 128 x BN int32 accumulators; the MMA warp fills one
-// while the 8 epilogue warps drain the other, so the epilogue of tile i overlaps the mainloop of tile i+1.
-// Epilogue: thread-per-row tcgen05.ld of 32 columns -> 128-byte-swizzled per-warp staging tile -> each lane
-// then owns 4 columns of 8 rows, applies ((float)acc*sx)*scale + bias and the activation, and the warp writes
-// four full 128-byte row segments per store instruction.
+// while the 16 epilogue warps drain the other, so the epilogue of tile i overlaps the mainloop of tile i+1.
+// Epilogue (4 warps per TMEM lane quarter, each owning a quarter of the tile's columns -- four warps per
+// scheduler hide the latency of the activation math): thread-per-row tcgen05.ld of 16 columns (the next
+// chunk's load is in flight while this one is processed) -> 64-byte-row swizzled per-warp staging tile -> each
+// lane then owns 4 columns of 4 rows, applies ((float)acc*sx)*scale + bias and the activation, and the warp
+// writes eight full 64-byte row segments per store instruction.
 template <int BN, int STAGES>
 struct I8Cfg {
     static constexpr int BK = 128;  // bytes of K per stage (one 128-byte swizzle row)
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
-    static constexpr int EPI_WARPS = 8;
-    static constexpr int STAGE_EPI = EPI_WARPS * 32 * 32 * 4;  // per-warp 32 x 32 x 4-byte staging tiles
+    static constexpr int EPI_WARPS = 16;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int EPI_COLS = BN / 4;                     // columns of the tile per epilogue warp
+    static constexpr int STAGE_EPI = EPI_WARPS * 32 * 16 * 4;  // per-warp 32 x 16 x 4-byte staging tiles
     static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + STAGE_EPI + 1024 + static_cast<int>(sizeof(SmemCtl));
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
 };
@@ -111,8 +115,95 @@ struct TileMap {  // tile t -> (m-tile, n-tile), M-tile fastest
     }
 };
 
+// Epilogue of one 128 x BN accumulator tile for one warp: its 32 TMEM lanes (tile rows r0 .. r0+31, TMEM address
+// tbase = lane quarter base) and columns [c_lo, c_lo + BN/4) of the tile, whose first global column is n0.
+// Thread-per-row tcgen05.ld of 16 columns (the next chunk's load is in flight while this one is processed) ->
+// 64-byte-row swizzled staging tile (16-byte chunk k of row i at chunk k ^ ((i >> 1) & 3): conflict-free both
+// ways) -> each lane owns 4 columns of 4 rows, applies ((float)acc * sx) * scale + bias and the activation, and
+// the warp writes eight full 64-byte row segments per store instruction. ACC_ONLY writes the raw int32 sums.
+template <int BN, bool ACC_ONLY, int ACTC>
+__device__ __forceinline__ void epi_tile_i8(uint32_t tbase, int r0, int n0, int c_lo, float* stg, int lane,
+                                            const float* __restrict__ sx, const float* __restrict__ scale,
+                                            const float* __restrict__ bias, float* __restrict__ y,
+                                            int32_t* __restrict__ acc_out, int ldy, int M, int N, int act, float alpha) {
+    constexpr int EPI_COLS = BN / 4;
+    const int sub = lane >> 2, chunk = lane & 3;  // column phase: rows 8i + sub, columns 4*chunk .. +3
+    float sxr[4];
+    if (!ACC_ONLY) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int gr = r0 + 8 * i + sub;
+            sxr[i] = gr < M ? __ldg(sx + gr) : 0.0f;
+        }
+    }
+    uint32_t r[16];
+    kx::tmem_ld16(tbase + c_lo, r);
+#pragma unroll 1
+    for (int c = c_lo; c < c_lo + EPI_COLS; c += 16) {
+        kx::tmem_ld16_wait(r);
+        // row phase: this thread's row -> staging (16-byte chunk k of row `lane` at chunk k ^ ((lane>>1)&3))
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            *reinterpret_cast<uint4*>(stg + lane * 16 + ((k ^ ((lane >> 1) & 3)) << 2)) =
+                make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+        if (c + 16 < c_lo + EPI_COLS) kx::tmem_ld16(tbase + c + 16, r);
+        __syncwarp();
+        const int gc = n0 + c + 4 * chunk;
+        float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f), bi4 = sc4;
+        if (!ACC_ONLY && gc < N) {
+            if (gc + 3 < N) {
+                sc4 = *reinterpret_cast<const float4*>(scale + gc);  // scale/bias: 16-byte aligned, padded
+                if (bias) bi4 = *reinterpret_cast<const float4*>(bias + gc);
+            } else {
+                sc4.x = scale[gc];
+                if (gc + 1 < N) sc4.y = scale[gc + 1];
+                if (gc + 2 < N) sc4.z = scale[gc + 2];
+                if (bias) {
+                    bi4.x = bias[gc];
+                    if (gc + 1 < N) bi4.y = bias[gc + 1];
+                    if (gc + 2 < N) bi4.z = bias[gc + 2];
+                }
+            }
+        }
+        const bool vec = (gc + 3 < N) && ((ldy & 3) == 0);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int rr = 8 * i + sub;
+            const int gr = r0 + rr;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 16 + ((chunk ^ ((rr >> 1) & 3)) << 2));
+            if (gr >= M || gc >= N) continue;
+            if (ACC_ONLY) {
+                int32_t* dst = acc_out + static_cast<size_t>(gr) * ldy + gc;
+                const int32_t e[4] = {static_cast<int32_t>(v.x), static_cast<int32_t>(v.y), static_cast<int32_t>(v.z),
+                                      static_cast<int32_t>(v.w)};
+                for (int e2 = 0; e2 < 4; e2++)
+                    if (gc + e2 < N) dst[e2] = e[e2];
+            } else {
+                const float s = sxr[i];
+                float o[4];
+                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+                const float scv[4] = {sc4.x, sc4.y, sc4.z, sc4.w}, biv[4] = {bi4.x, bi4.y, bi4.z, bi4.w};
+#pragma unroll
+                for (int e2 = 0; e2 < 4; e2++) {
+                    float tv = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(vv[e2])), s), scv[e2]);
+                    tv = __fadd_rn(tv, biv[e2]);
+                    o[e2] = epi_act<ACTC>(tv, act, alpha);
+                }
+                float* dst = y + static_cast<size_t>(gr) * ldy + gc;
+                if (vec) {
+                    *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+                    for (int e2 = 0; e2 < 4; e2++)
+                        if (gc + e2 < N) dst[e2] = o[e2];
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
 template <int BN, int STAGES, bool ACC_ONLY, int ACTC>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(I8Cfg<BN, STAGES>::THREADS, 1)
 k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
           const float* __restrict__ sx, const float* __restrict__ scale, const float* __restrict__ bias,
           float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N, int K, int act, float alpha,
@@ -205,11 +296,10 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         }
         __syncwarp();
     } else {
-        const int ew = warp - 2;           // 0..7
-        const int q = warp & 3;            // TMEM lane quarter this warp may read
-        const int c_lo = (ew >> 2) * (BN / 2);  // this warp's half of the tile's columns
-        float* stg = reinterpret_cast<float*>(sE + ew * 4096);
-        const int sub = lane >> 3, chunk = lane & 7;  // column phase: rows 4i + sub, columns 4*chunk .. +3
+        const int ew = warp - 2;                    // 0..15
+        const int q = warp & 3;                     // TMEM lane quarter this warp may read
+        const int c_lo = (ew >> 2) * C::EPI_COLS;   // this warp's quarter of the tile's columns
+        float* stg = reinterpret_cast<float*>(sE + ew * 2048);
         int j = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, j++) {
             int mt, nt;
@@ -217,78 +307,8 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             const int b = j & 1;
             if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
             kx::tc_fence_after();
-            const int r0 = mt * BM + q * 32;  // first row of this warp's 32
-            float sxr[8];
-            if (!ACC_ONLY) {
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int gr = r0 + 4 * i + sub;
-                    sxr[i] = gr < M ? __ldg(sx + gr) : 0.0f;
-                }
-            }
-#pragma unroll 1
-            for (int c = c_lo; c < c_lo + BN / 2; c += 32) {
-                uint32_t r[32];
-                kx::tmem_ld32(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16) + c, r);
-                kx::tmem_ld_wait();
-                // row phase: this thread's row -> staging (16-byte chunk k of row `lane` at chunk k ^ (lane & 7))
-#pragma unroll
-                for (int k = 0; k < 8; k++)
-                    *reinterpret_cast<uint4*>(stg + lane * 32 + ((k ^ (lane & 7)) << 2)) =
-                        make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
-                __syncwarp();
-                const int gc = nt * BN + c + 4 * chunk;
-                float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f), bi4 = sc4;
-                if (!ACC_ONLY && gc < N) {
-                    if (gc + 3 < N) {
-                        sc4 = *reinterpret_cast<const float4*>(scale + gc);  // scale/bias: 16-byte aligned, padded
-                        if (bias) bi4 = *reinterpret_cast<const float4*>(bias + gc);
-                    } else {
-                        sc4.x = scale[gc];
-                        if (gc + 1 < N) sc4.y = scale[gc + 1];
-                        if (gc + 2 < N) sc4.z = scale[gc + 2];
-                        if (bias) {
-                            bi4.x = bias[gc];
-                            if (gc + 1 < N) bi4.y = bias[gc + 1];
-                            if (gc + 2 < N) bi4.z = bias[gc + 2];
-                        }
-                    }
-                }
-                const bool vec = (gc + 3 < N) && ((ldy & 3) == 0);
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int rr = 4 * i + sub;
-                    const int gr = r0 + rr;
-                    const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 32 + ((chunk ^ (rr & 7)) << 2));
-                    if (gr >= M || gc >= N) continue;
-                    if (ACC_ONLY) {
-                        int32_t* dst = acc_out + static_cast<size_t>(gr) * ldy + gc;
-                        const int32_t e[4] = {static_cast<int32_t>(v.x), static_cast<int32_t>(v.y), static_cast<int32_t>(v.z),
-                                              static_cast<int32_t>(v.w)};
-                        for (int e2 = 0; e2 < 4; e2++)
-                            if (gc + e2 < N) dst[e2] = e[e2];
-                    } else {
-                        const float s = sxr[i];
-                        float o[4];
-                        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-                        const float scv[4] = {sc4.x, sc4.y, sc4.z, sc4.w}, biv[4] = {bi4.x, bi4.y, bi4.z, bi4.w};
-#pragma unroll
-                        for (int e2 = 0; e2 < 4; e2++) {
-                            float tv = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(vv[e2])), s), scv[e2]);
-                            tv = __fadd_rn(tv, biv[e2]);
-                            o[e2] = epi_act<ACTC>(tv, act, alpha);
-                        }
-                        float* dst = y + static_cast<size_t>(gr) * ldy + gc;
-                        if (vec) {
-                            *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-                        } else {
-                            for (int e2 = 0; e2 < 4; e2++)
-                                if (gc + e2 < N) dst[e2] = o[e2];
-                        }
-                    }
-                }
-                __syncwarp();
-            }
+            epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), mt * BM + q * 32, nt * BN,
+                                            c_lo, stg, lane, sx, scale, bias, y, acc_out, ldy, M, N, act, alpha);
             kx::tc_fence_before();
             __syncwarp();
             if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[b]);
@@ -299,6 +319,162 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     if (warp == 1) {
         kx::tc_fence_after();
         kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------ int8, CTA pairs
+// The same persistent GEMM on 256 x 256 output tiles computed by a cluster of two CTAs with one M = 256
+// tcgen05.mma (cta_group::2). CTA rank r of the pair stages A rows [m0 + 128 r, +128) and B rows
+// [n0 + 128 r, +128) of each K block in its own shared memory; the MMA, issued by rank 0, reads both CTAs'
+// halves and leaves rows [m0 + 128 r, +128) x 256 columns in rank r's TMEM, which rank r's 16 epilogue warps
+// drain exactly as in the one-CTA kernel. Per SM a K block moves 32 KB of operands for 128 x 256 x 128 MACs
+// (the one-CTA 128 x 256 tile moves 48 KB), so six stages fit where the one-CTA kernel holds four.
+// Synchronisation: both CTAs' TMA loads complete on rank 0's full[s] (rank 0 alone arms it with the bytes of
+// both); rank 0's MMA thread commits every stage to empty[s] and every tile to acc_full[b] of BOTH CTAs (one
+// commit per CTA, no multicast); each epilogue warp of either CTA arrives on rank 0's acc_empty[b] (32 arrivals).
+// Every wait is bounded. On a timeout rank 0 waits (bounded) for the stages it armed, which cover the peer's
+// copies of the same stages; the peer's producer can run at most STAGES K blocks ahead of rank 0's MMA, and
+// those copies land within microseconds, long before any timeout expires.
+template <int STAGES>
+struct I8PairCfg {
+    static constexpr int BN = 256;                 // columns per tile (the MMA's N)
+    static constexpr int BK = 128;                 // bytes of K per stage
+    static constexpr int A_BYTES = BM * BK;        // this CTA's 128 rows of A
+    static constexpr int B_BYTES = (BN / 2) * BK;  // this CTA's 128 rows of B
+    static constexpr int EPI_WARPS = 16;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int STAGE_EPI = EPI_WARPS * 32 * 16 * 4;
+    static constexpr int SMEM = STAGES * (A_BYTES + B_BYTES) + STAGE_EPI + 1024 + static_cast<int>(sizeof(SmemCtl));
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+template <int STAGES, bool ACC_ONLY, int ACTC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(I8PairCfg<STAGES>::THREADS, 1)
+k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const float* __restrict__ sx, const float* __restrict__ scale, const float* __restrict__ bias,
+               float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N, int K, int act, float alpha,
+               int* status) {
+    using C = I8PairCfg<STAGES>;
+    constexpr int BN = C::BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);  // the same offset in both CTAs (same kernel, same static layout)
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint8_t* sE = sB + STAGES * C::B_BYTES;
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(sE + C::STAGE_EPI);
+    volatile int* abort_flag = &ctl->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = kx::cluster_ctarank();
+    const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    const int nk = (K + C::BK - 1) / C::BK;
+    const TileMap tm{(M + 2 * BM - 1) / (2 * BM), (N + BN - 1) / BN};  // pair tiles: 256 rows x 256 columns
+    const int n_tiles = tm.m_tiles * tm.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1);
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            kx::mbar_init(&ctl->acc_full[b], 1);
+            kx::mbar_init(&ctl->acc_empty[b], 2 * C::EPI_WARPS);
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {  // warp 1 of both CTAs, same destination offset
+        kx::tmem_alloc_pair(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish_pair();
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmA);
+            kx::tma_prefetch_desc(&tmB);
+            int it = 0;
+            for (int t = cluster; t < n_tiles && !*abort_flag; t += n_clusters) {
+                int mt, nt;
+                tm.at(t, mt, nt);
+                const int arow = mt * 2 * BM + static_cast<int>(rank) * BM, brow = nt * BN + static_cast<int>(rank) * (BN / 2);
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                    if (rank == 0) kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * (C::A_BYTES + C::B_BYTES));
+                    const uint32_t full0 = kx::mapa(kx::smem_u32(&ctl->full[s]), 0);
+                    kx::tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, kb * C::BK, arow, full0);
+                    kx::tma_load_2d_pair(sB + s * C::B_BYTES, &tmB, kb * C::BK, brow, full0);
+                }
+            }
+            if (*abort_flag && rank == 0)  // the stages armed here also carry the peer's copies
+                for (int i = it > STAGES ? it - STAGES : 0; i < it; i++) drain_wait(&ctl->full[i % STAGES], (i / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = kx::idesc_i8(2 * BM, BN);
+            int it = 0, j = 0;
+            for (int t = cluster; t < n_tiles && !*abort_flag; t += n_clusters, j++) {
+                const int b = j & 1;
+                if (!kx::mbar_wait(&ctl->acc_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                bool ok = true;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->full[s], (it / STAGES) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    kx::tc_fence_after();
+                    const uint32_t a0 = kx::smem_u32(sA + s * C::A_BYTES), b0 = kx::smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 32; kk++)
+                        kx::mma_i8_pair(d, kx::desc_sw128_kmajor(a0 + kk * 32), kx::desc_sw128_kmajor(b0 + kk * 32), idesc,
+                                        (kb | kk) != 0);
+                    const uint32_t e = kx::smem_u32(&ctl->empty[s]);
+                    kx::mma_commit_pair(e);
+                    kx::mma_commit_pair(kx::mapa(e, 1));
+                }
+                if (!ok) break;
+                const uint32_t f = kx::smem_u32(&ctl->acc_full[b]);
+                kx::mma_commit_pair(f);
+                kx::mma_commit_pair(kx::mapa(f, 1));
+            }
+            kx::mma_commit_pair(kx::smem_u32(&ctl->accf));  // completes once every MMA issued above has finished
+            drain_wait(&ctl->accf, 0);
+        }
+        __syncwarp();
+    } else {
+        const int ew = warp - 2;                 // 0..15
+        const int q = warp & 3;                  // TMEM lane quarter this warp may read
+        const int c_lo = (ew >> 2) * (BN / 4);   // this warp's quarter of the tile's columns
+        float* stg = reinterpret_cast<float*>(sE + ew * 2048);
+        int j = 0;
+        for (int t = cluster; t < n_tiles; t += n_clusters, j++) {
+            int mt, nt;
+            tm.at(t, mt, nt);
+            const int b = j & 1;
+            if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
+            kx::tc_fence_after();
+            epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16),
+                                            mt * 2 * BM + static_cast<int>(rank) * BM + q * 32, nt * BN, c_lo, stg, lane, sx,
+                                            scale, bias, y, acc_out, ldy, M, N, act, alpha);
+            kx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) kx::mbar_arrive_cluster(kx::mapa(kx::smem_u32(&ctl->acc_empty[b]), 0));
+        }
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc_pair(tmem, C::TMEM_COLS);
     }
 }
 
@@ -648,7 +824,64 @@ int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int 
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    kern<<<grid, 320, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// clusters of the pair kernel that can be resident at once (per kernel and device; 0 if the query fails)
+int max_pair_clusters(const void* kern, int threads, int smem) {
+    static std::mutex mu;
+    static const void* keys[64];
+    static int devs[64], vals[64], n = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    for (int i = 0; i < n; i++)
+        if (keys[i] == kern && devs[i] == dev) return vals[i];
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * 148, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        c = 0;
+    }
+    if (n < 64) {
+        keys[n] = kern;
+        devs[n] = dev;
+        vals[n] = c;
+        n++;
+    }
+    return c;
+}
+
+template <bool ACC_ONLY, int ACTC>
+int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
+                   const float* bias, float* y, int32_t* acc, int ldy, int m, int n, int k, int act, float alpha, int* status,
+                   cudaStream_t st) {
+    constexpr int STAGES = 6;
+    using C = I8PairCfg<STAGES>;
+    CUtensorMap ta, tb;
+    if (make_map_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, static_cast<uint64_t>(ldq), static_cast<uint64_t>(m),
+                    static_cast<uint64_t>(ldq), C::BK, BM) != 0 ||
+        make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, static_cast<uint64_t>(ldw), static_cast<uint64_t>(n),
+                    static_cast<uint64_t>(ldw), C::BK, C::BN / 2) != 0)
+        return -1;
+    auto kern = k_gemm_i8_pair<STAGES, ACC_ONLY, ACTC>;
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + C::BN - 1) / C::BN);
+    int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
+    if (clusters <= 0) clusters = sm_count() / 2;
+    if (clusters > tiles) clusters = tiles;
+    kern<<<2 * clusters, C::THREADS, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -711,6 +944,16 @@ __global__ void k_prep_f32(const float* __restrict__ w, int k, int n, float* __r
 template <int BN>
 int dispatch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale, const float* bias,
                 float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st) {
+    if (BN == 256) {  // 256 x 256 tiles on CTA pairs
+        switch (act_class(act)) {
+        case -1: return launch_i8_pair<false, -1>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+        case 0: return launch_i8_pair<false, 0>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+        case 1: return launch_i8_pair<false, 1>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
+        default:
+            return launch_i8_pair<false, ACT_GENERIC>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha,
+                                                      status, st);
+        }
+    }
     switch (act_class(act)) {
     case -1: return launch_i8<BN, false, -1>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
     case 0: return launch_i8<BN, false, 0>(xq, ldq, sx, wq, ldw, scale, bias, y, nullptr, ldy, m, n, k, act, alpha, status, st);
@@ -762,8 +1005,10 @@ int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t
                    int* status, void* stream) {
     if (m <= 0 || n <= 0) return 0;
     if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15)) return -1;
-    return launch_i8<256, true, -1>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, acc, ldacc, m, n, k, -1, 0.0f,
-                                    status, static_cast<cudaStream_t>(stream));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n <= 128)
+        return launch_i8<128, true, -1>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, acc, ldacc, m, n, k, -1, 0.0f, status, st);
+    return launch_i8_pair<true, -1>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, acc, ldacc, m, n, k, -1, 0.0f, status, st);
 }
 
 int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,

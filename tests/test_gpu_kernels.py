@@ -91,8 +91,11 @@ def _prep_i8(kx, q):
     return wq, ldw
 
 
-@pytest.mark.parametrize("m,k,n", [(300, 1000, 520), (128, 256, 256), (5, 55, 31), (1, 16, 16), (130, 4096, 384)])
+@pytest.mark.parametrize("m,k,n", [(300, 1000, 520), (128, 256, 256), (5, 55, 31), (1, 16, 16), (130, 4096, 384),
+                                   (2100, 1024, 4100), (1500, 4096, 4096)])
 def test_gemm_i8_accumulators_bitexact(kx, m, k, n):
+    """int32 sums bit-exact; N > 128 runs on CTA pairs (256 x 256 tiles): ragged pair tiles whose second CTA's rows
+    or columns lie wholly outside the matrix, and several tiles per cluster (both accumulator buffers reused)."""
     rng = np.random.default_rng(m + k + n)
     xq = rng.integers(-127, 128, (m, k), dtype=np.int8)
     q = rng.integers(-127, 128, (k, n), dtype=np.int8)

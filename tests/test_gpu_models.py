@@ -132,6 +132,37 @@ def test_device_forward_matches_host_forward(Model, model_dir, libkx):
     assert np.array_equal(dy.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("cfg,batch,ws_mb", [("c2", 1000, 0), ("c2", 1000, 40), ("c3", 37, 0), ("c4", 9, 0)])
+def test_pipelined_host_forward_is_cut_invariant(Model, model_dir, monkeypatch, cfg, batch, ws_mb):
+    """The host-memory forward cuts each chunk into pieces whose copies overlap the kernels of their neighbours:
+    any number of pieces, with or without workspace chunking, gives bitwise the same rows as one piece."""
+    from kernix_b200 import configs
+    p = cfg_path(cfg, model_dir)
+    x = configs.inputs(cfg, batch)
+    outs = []
+    for pieces in ("1", "3", "8"):
+        monkeypatch.setenv("KERNIX_PIPELINE", pieces)
+        m = Model(p, workspace_mb=ws_mb)
+        got = m(x)
+        outs.append(got)
+        assert np.array_equal(m(x), got)  # second call into the same arena
+        m.close()
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+
+
+def test_pipelined_forward_of_a_view_only_graph(Model, model_dir, monkeypatch):
+    """A graph that is only a RESHAPE of its input: the output rows are read from the pieces' input rows."""
+    from kernix_b200 import knx_writer
+    q = model_dir + "/view_only.knx"
+    g = knx_writer.Graph((4, 8))
+    g.reshape(0, (32,))
+    g.write(q)
+    monkeypatch.setenv("KERNIX_PIPELINE", "8")
+    m = Model(q)
+    x = np.random.default_rng(5).standard_normal((4 * 40000, 8), dtype=F32)  # 5 MB: several pieces
+    assert np.array_equal(m(x), x.reshape(40000, 32))
+
+
 class FloatTensor(ctypes.Structure):
     _fields_ = [("row", ctypes.c_int), ("col", ctypes.c_int), ("tensor", ctypes.POINTER(ctypes.c_float))]
 
