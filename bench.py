@@ -48,19 +48,21 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="time box of the CPU-baseline sample (0: none)")
     ap.add_argument("--kernel-case", type=int, default=0, metavar="M",
                     help="profiling case: only run the int8 GEMM of c2's 4096x4096 layer with M rows, 3 launches, then exit")
+    ap.add_argument("--kernel-k", type=int, default=4096, help="K of the profiling case (1024: c2's first layer)")
+    ap.add_argument("--kernel-act", type=int, default=1, help="activation of the profiling case (1 GELU, -1 none)")
     return ap.parse_args()
 
 
-def kernel_case(m_rows):
-    """Three launches of k_gemm_i8 (GELU epilogue) on an M x 4096 x 4096 problem -- for an ncu capture of one kernel
-    on a case larger than L2 (M = 8192: 32 MB A + 16 MB B + 128 MB C)."""
+def kernel_case(m_rows, k=4096, act=1):
+    """Three launches of the int8 GEMM (GELU epilogue by default) on an M x K x 4096 problem -- for an ncu capture
+    of one kernel on a case larger than L2 (M = 8192, K = 4096: 32 MB A + 16 MB B + 128 MB C)."""
     import numpy as np
     import torch
 
     from kernix_b200 import build, kx_abi
     build.build()
     L = kx_abi.lib()
-    k = n = 4096
+    n = 4096
     rng = np.random.default_rng(0)
     xq = torch.from_numpy(rng.integers(-127, 128, (m_rows, k), dtype=np.int8)).cuda()
     wq = torch.from_numpy(rng.integers(-127, 128, (n, k), dtype=np.int8)).cuda()
@@ -70,10 +72,10 @@ def kernel_case(m_rows):
     y = torch.empty((m_rows, n), device="cuda")
     for _ in range(3):
         if L.kx_gemm_i8(xq.data_ptr(), k, sx.data_ptr(), wq.data_ptr(), k, sc.data_ptr(), b.data_ptr(), y.data_ptr(), n, m_rows,
-                        n, k, 1, 0.0, None, None) != 0:
+                        n, k, act, 0.0, None, None) != 0:
             raise RuntimeError("kx_gemm_i8 failed")
     torch.cuda.synchronize()
-    print(json.dumps({"kernel_case": "k_gemm_i8", "m": m_rows, "n": n, "k": k, "launches": 3}))
+    print(json.dumps({"kernel_case": "k_gemm_i8", "m": m_rows, "n": n, "k": k, "act": act, "launches": 3}))
 
 
 def model_file(rank):
@@ -408,7 +410,7 @@ def gemm_roofline(L, torch, np, steps, flush):
 if __name__ == "__main__":
     a = parse()
     if a.kernel_case:
-        kernel_case(a.kernel_case)
+        kernel_case(a.kernel_case, a.kernel_k, a.kernel_act)
     elif a.impl == "reference":
         run_reference(a)
     else:

@@ -60,6 +60,12 @@ __device__ __forceinline__ float epi_act(float v, int act, float alpha) {
     if constexpr (ACTC == ACT_GENERIC) return act_outline(act, v, alpha);
     else return kx::act_apply(ACTC, v, alpha);
 }
+// the epilogue activation on two values (packed f32x2 arithmetic for GELU; per component otherwise)
+template <int ACTC>
+__device__ __forceinline__ float2 epi_act2(float2 v, int act, float alpha) {
+    if constexpr (ACTC == 1) return kx::gelu_as2(v);
+    else return make_float2(epi_act<ACTC>(v.x, act, alpha), epi_act<ACTC>(v.y, act, alpha));
+}
 inline int act_class(int act) { return act == -1 || act == 0 || act == 1 ? act : ACT_GENERIC; }
 
 struct SmemCtl {
@@ -115,90 +121,111 @@ struct TileMap {  // tile t -> (m-tile, n-tile), M-tile fastest
     }
 };
 
-// Epilogue of one 128 x BN accumulator tile for one warp: its 32 TMEM lanes (tile rows r0 .. r0+31, TMEM address
-// tbase = lane quarter base) and columns [c_lo, c_lo + BN/4) of the tile, whose first global column is n0.
-// Thread-per-row tcgen05.ld of 16 columns (the next chunk's load is in flight while this one is processed) ->
-// 64-byte-row swizzled staging tile (16-byte chunk k of row i at chunk k ^ ((i >> 1) & 3): conflict-free both
-// ways) -> each lane owns 4 columns of 4 rows, applies ((float)acc * sx) * scale + bias and the activation, and
-// the warp writes eight full 64-byte row segments per store instruction. ACC_ONLY writes the raw int32 sums.
-template <int BN, bool ACC_ONLY, int ACTC>
-__device__ __forceinline__ void epi_tile_i8(uint32_t tbase, int r0, int n0, int c_lo, float* stg, int lane,
-                                            const float* __restrict__ sx, const float* __restrict__ scale,
-                                            const float* __restrict__ bias, float* __restrict__ y,
-                                            int32_t* __restrict__ acc_out, int ldy, int M, int N, int act, float alpha) {
-    constexpr int EPI_COLS = BN / 4;
-    const int sub = lane >> 2, chunk = lane & 3;  // column phase: rows 8i + sub, columns 4*chunk .. +3
-    float sxr[4];
-    if (!ACC_ONLY) {
+// Per-warp dequantisation factors of one tile, loaded one tile ahead so that their global-load latency hides
+// behind the wait for the accumulator: sx of the thread's four rows (r0 + 16h + 8e + lane/4 -> sx[2h + e]) and,
+// spread over the warp (two columns per lane), scale and bias of the warp's 64 columns starting at col0.
+struct EpiPre {
+    float sx[4];
+    float2 sc, bi;
+};
+__device__ __forceinline__ void epi_prefetch(EpiPre& p, int r0, int col0, int lane, int M, int N, const float* __restrict__ sx,
+                                             const float* __restrict__ scale, const float* __restrict__ bias) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int gr = r0 + 8 * i + sub;
-            sxr[i] = gr < M ? __ldg(sx + gr) : 0.0f;
-        }
+    for (int i = 0; i < 4; i++) {
+        const int gr = r0 + 16 * (i >> 1) + 8 * (i & 1) + (lane >> 2);
+        p.sx[i] = gr < M ? __ldg(sx + gr) : 0.0f;
     }
-    uint32_t r[16];
-    kx::tmem_ld16(tbase + c_lo, r);
-#pragma unroll 1
-    for (int c = c_lo; c < c_lo + EPI_COLS; c += 16) {
-        kx::tmem_ld16_wait(r);
-        // row phase: this thread's row -> staging (16-byte chunk k of row `lane` at chunk k ^ ((lane>>1)&3))
+    const int c = col0 + 2 * lane;
+    p.sc.x = c < N ? __ldg(scale + c) : 0.0f;
+    p.sc.y = c + 1 < N ? __ldg(scale + c + 1) : 0.0f;
+    p.bi.x = bias && c < N ? __ldg(bias + c) : 0.0f;
+    p.bi.y = bias && c + 1 < N ? __ldg(bias + c + 1) : 0.0f;
+}
+
+// Dequantise, activate and store one 16x256b.x4 block: rows ra and ra + 8, columns gc, gc + 1 (per k block).
+template <bool ACC_ONLY, int ACTC>
+__device__ __forceinline__ void epi_block(const uint32_t (&r)[16], int ra, int gc0, float sxa, float sxb,
+                                          const float2* __restrict__ scs, const float2* __restrict__ bis,
+                                          float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N,
+                                          bool vec, int act, float alpha) {
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            *reinterpret_cast<uint4*>(stg + lane * 16 + ((k ^ ((lane >> 1) & 3)) << 2)) =
-                make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
-        if (c + 16 < c_lo + EPI_COLS) kx::tmem_ld16(tbase + c + 16, r);
-        __syncwarp();
-        const int gc = n0 + c + 4 * chunk;
-        float4 sc4 = make_float4(0.f, 0.f, 0.f, 0.f), bi4 = sc4;
-        if (!ACC_ONLY && gc < N) {
-            if (gc + 3 < N) {
-                sc4 = *reinterpret_cast<const float4*>(scale + gc);  // scale/bias: 16-byte aligned, padded
-                if (bias) bi4 = *reinterpret_cast<const float4*>(bias + gc);
-            } else {
-                sc4.x = scale[gc];
-                if (gc + 1 < N) sc4.y = scale[gc + 1];
-                if (gc + 2 < N) sc4.z = scale[gc + 2];
-                if (bias) {
-                    bi4.x = bias[gc];
-                    if (gc + 1 < N) bi4.y = bias[gc + 1];
-                    if (gc + 2 < N) bi4.z = bias[gc + 2];
-                }
-            }
-        }
-        const bool vec = (gc + 3 < N) && ((ldy & 3) == 0);
+    for (int k = 0; k < 4; k++) {
+        const int gc = gc0 + 8 * k;
+        if (gc >= N) continue;
+        const float2 sc = scs[4 * k], bi = bis[4 * k];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int rr = 8 * i + sub;
-            const int gr = r0 + rr;
-            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 16 + ((chunk ^ ((rr >> 1) & 3)) << 2));
-            if (gr >= M || gc >= N) continue;
+        for (int e = 0; e < 2; e++) {
+            const int gr = ra + 8 * e;
+            if (gr >= M) continue;
+            const uint32_t v0 = r[4 * k + 2 * e], v1 = r[4 * k + 2 * e + 1];
             if (ACC_ONLY) {
                 int32_t* dst = acc_out + static_cast<size_t>(gr) * ldy + gc;
-                const int32_t e[4] = {static_cast<int32_t>(v.x), static_cast<int32_t>(v.y), static_cast<int32_t>(v.z),
-                                      static_cast<int32_t>(v.w)};
-                for (int e2 = 0; e2 < 4; e2++)
-                    if (gc + e2 < N) dst[e2] = e[e2];
+                dst[0] = static_cast<int32_t>(v0);
+                if (gc + 1 < N) dst[1] = static_cast<int32_t>(v1);
             } else {
-                const float s = sxr[i];
-                float o[4];
-                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-                const float scv[4] = {sc4.x, sc4.y, sc4.z, sc4.w}, biv[4] = {bi4.x, bi4.y, bi4.z, bi4.w};
-#pragma unroll
-                for (int e2 = 0; e2 < 4; e2++) {
-                    float tv = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(vv[e2])), s), scv[e2]);
-                    tv = __fadd_rn(tv, biv[e2]);
-                    o[e2] = epi_act<ACTC>(tv, act, alpha);
-                }
+                const float s = e ? sxb : sxa;
+                // ((float)acc * sx) * scale + bias in scalar IEEE steps (the compiler may contract packed
+                // mul + add chains into fma, which would change the bits), the activation on the pair
+                const float d0 = __fadd_rn(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v0)), s), sc.x), bi.x);
+                const float d1 = __fadd_rn(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v1)), s), sc.y), bi.y);
+                const float2 o = epi_act2<ACTC>(make_float2(d0, d1), act, alpha);
+                const float o0 = o.x, o1 = o.y;
                 float* dst = y + static_cast<size_t>(gr) * ldy + gc;
-                if (vec) {
-                    *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+                if (vec && gc + 1 < N) {
+                    *reinterpret_cast<float2*>(dst) = make_float2(o0, o1);
                 } else {
-                    for (int e2 = 0; e2 < 4; e2++)
-                        if (gc + e2 < N) dst[e2] = o[e2];
+                    dst[0] = o0;
+                    if (gc + 1 < N) dst[1] = o1;
                 }
             }
         }
+    }
+}
+
+// Epilogue of one 128 x BN accumulator tile for one warp: its 32 TMEM lanes (tile rows r0 .. r0+31, TMEM address
+// tbase = lane quarter base) and columns [c_lo, c_lo + BN/4) of the tile, whose first global column is n0.
+// tcgen05.ld 16x256b: four consecutive threads hold 8 consecutive columns of one row, so every store writes
+// whole 32-byte sectors straight from registers (no shared-memory transpose); the loads are double-buffered so
+// each block's load is in flight while the previous block is processed. The warp's column factors sit in
+// its shared-memory slot (written from the prefetched registers) and are read as broadcasts.
+// ACC_ONLY writes the raw int32 sums.
+template <int BN, bool ACC_ONLY, int ACTC>
+__device__ __forceinline__ void epi_tile_i8(uint32_t tbase, int r0, int n0, int c_lo, float* slot, int lane, const EpiPre& f,
+                                            float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N,
+                                            int act, float alpha) {
+    constexpr int EPI_COLS = BN / 4;  // 64 or 32 columns: 2 or 1 column halves of 32
+    constexpr int NB = 2 * (EPI_COLS / 32);  // 16x256b.x4 blocks per warp: (row half, column half)
+    float2* scs = reinterpret_cast<float2*>(slot);
+    float2* bis = scs + 32;
+    if (!ACC_ONLY) {
         __syncwarp();
+        scs[lane] = f.sc;  // columns c_lo + 2 lane, +1
+        bis[lane] = f.bi;
+        __syncwarp();
+    }
+    const int t4 = lane & 3, row = lane >> 2;
+    const bool vec = (ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(y) & 7) == 0;
+    uint32_t ra[16], rb[16];
+    // block i: row half h = i % 2, column half cc = i / 2
+    auto taddr = [&](int i) { return tbase + (static_cast<uint32_t>(16 * (i & 1)) << 16) + c_lo + 32 * (i >> 1); };
+    auto run = [&](const uint32_t (&r)[16], int i) {
+        const int h = i & 1, cc = i >> 1;
+        epi_block<ACC_ONLY, ACTC>(r, r0 + 16 * h + row, n0 + c_lo + 32 * cc + 2 * t4, f.sx[2 * h], f.sx[2 * h + 1],
+                                  scs + 16 * cc + t4, bis + 16 * cc + t4, y, acc_out, ldy, M, N, vec, act, alpha);
+    };
+    kx::tmem_ld16x256b_x4(taddr(0), ra);
+    kx::tmem_ld16_wait(ra);
+    kx::tmem_ld16x256b_x4(taddr(1), rb);
+    run(ra, 0);
+    kx::tmem_ld16_wait(rb);
+    if (NB > 2) kx::tmem_ld16x256b_x4(taddr(2), ra);
+    run(rb, 1);
+    if (NB > 2) {
+        kx::tmem_ld16_wait(ra);
+        kx::tmem_ld16x256b_x4(taddr(3), rb);
+        run(ra, 2);
+        kx::tmem_ld16_wait(rb);
+        run(rb, 3);
     }
 }
 
@@ -300,15 +327,27 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         const int q = warp & 3;                     // TMEM lane quarter this warp may read
         const int c_lo = (ew >> 2) * C::EPI_COLS;   // this warp's quarter of the tile's columns
         float* stg = reinterpret_cast<float*>(sE + ew * 2048);
+        EpiPre cur{}, nxt{};
+        if (!ACC_ONLY && blockIdx.x < n_tiles) {
+            int mt, nt;
+            tm.at(blockIdx.x, mt, nt);
+            epi_prefetch(cur, mt * BM + q * 32, nt * BN + c_lo, lane, M, N, sx, scale, bias);
+        }
         int j = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, j++) {
             int mt, nt;
             tm.at(t, mt, nt);
             const int b = j & 1;
+            if (!ACC_ONLY && t + static_cast<int>(gridDim.x) < n_tiles) {
+                int mt2, nt2;
+                tm.at(t + gridDim.x, mt2, nt2);
+                epi_prefetch(nxt, mt2 * BM + q * 32, nt2 * BN + c_lo, lane, M, N, sx, scale, bias);
+            }
             if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
             kx::tc_fence_after();
             epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), mt * BM + q * 32, nt * BN,
-                                            c_lo, stg, lane, sx, scale, bias, y, acc_out, ldy, M, N, act, alpha);
+                                            c_lo, stg, lane, cur, y, acc_out, ldy, M, N, act, alpha);
+            cur = nxt;
             kx::tc_fence_before();
             __syncwarp();
             if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[b]);
@@ -455,19 +494,32 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3;                  // TMEM lane quarter this warp may read
         const int c_lo = (ew >> 2) * (BN / 4);   // this warp's quarter of the tile's columns
         float* stg = reinterpret_cast<float*>(sE + ew * 2048);
+        const int row_off = static_cast<int>(rank) * BM + q * 32;  // this warp's rows within a pair tile
+        EpiPre cur{}, nxt{};
+        if (!ACC_ONLY && cluster < n_tiles) {
+            int mt, nt;
+            tm.at(cluster, mt, nt);
+            epi_prefetch(cur, mt * 2 * BM + row_off, nt * BN + c_lo, lane, M, N, sx, scale, bias);
+        }
+        const uint32_t acc_empty0 = kx::mapa(kx::smem_u32(&ctl->acc_empty[0]), 0);
         int j = 0;
         for (int t = cluster; t < n_tiles; t += n_clusters, j++) {
             int mt, nt;
             tm.at(t, mt, nt);
             const int b = j & 1;
+            if (!ACC_ONLY && t + n_clusters < n_tiles) {
+                int mt2, nt2;
+                tm.at(t + n_clusters, mt2, nt2);
+                epi_prefetch(nxt, mt2 * 2 * BM + row_off, nt2 * BN + c_lo, lane, M, N, sx, scale, bias);
+            }
             if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
             kx::tc_fence_after();
-            epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16),
-                                            mt * 2 * BM + static_cast<int>(rank) * BM + q * 32, nt * BN, c_lo, stg, lane, sx,
-                                            scale, bias, y, acc_out, ldy, M, N, act, alpha);
+            epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), mt * 2 * BM + row_off,
+                                            nt * BN, c_lo, stg, lane, cur, y, acc_out, ldy, M, N, act, alpha);
+            cur = nxt;
             kx::tc_fence_before();
             __syncwarp();
-            if (lane == 0) kx::mbar_arrive_cluster(kx::mapa(kx::smem_u32(&ctl->acc_empty[b]), 0));
+            if (lane == 0) kx::mbar_arrive_remote(acc_empty0 + b * static_cast<uint32_t>(sizeof(uint64_t)));
         }
     }
     kx::tc_fence_before();
@@ -736,7 +788,7 @@ struct MapKey {
     const void* base;
     uint64_t inner, outer, row_bytes;
     uint32_t box_inner, box_outer;
-    int dt;
+    int dt, swz;
 };
 
 struct MapEntry {
@@ -750,11 +802,12 @@ thread_local MapEntry t_maps[64];
 bool same_key(const MapKey& a, const MapKey& b) { return std::memcmp(&a, &b, sizeof(MapKey)) == 0; }
 
 int make_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
-                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     MapKey k;
     std::memset(&k, 0, sizeof k);
     k.base = base; k.inner = inner; k.outer = outer; k.row_bytes = row_bytes;
-    k.box_inner = box_inner; k.box_outer = box_outer; k.dt = static_cast<int>(dt);
+    k.box_inner = box_inner; k.box_outer = box_outer; k.dt = static_cast<int>(dt); k.swz = static_cast<int>(swz);
     const size_t h = (reinterpret_cast<uintptr_t>(base) >> 8 ^ inner * 31 ^ outer * 131 ^ box_outer) & 63;
     if (t_maps[h].used && same_key(t_maps[h].key, k)) {
         *out = t_maps[h].map;
@@ -768,7 +821,7 @@ int make_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t es[2] = {1, 1};
     if (enc(out, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return -1;
     t_maps[h].key = k;
     t_maps[h].map = *out;
