@@ -531,14 +531,22 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ------------------------------------------------------------------------------------------ 3xTF32
-template <int BN, int STAGES>
+// DRAIN: for long reductions the MMA accumulates chunks of KC_BLOCKS K blocks (256 K) into two alternating TMEM
+// buffers, and the epilogue warps add every chunk into an fp32 running sum kept in a third TMEM region with
+// round-to-nearest adds (sum = ((P0 + P1) + P2) + ..., a fixed order). The tensor core's accumulation truncates,
+// which costs about 2e-9 * (accumulation length) relative error; draining bounds that length by 256, so K = 16384
+// stays near 1e-6 instead of 3e-5.
+constexpr int KC_BLOCKS = 8;
+constexpr int DRAIN_MIN_K = 2048;  // reductions longer than this drain
+template <int BN, int STAGES, bool DRAIN = false>
 struct F32Cfg {
     static constexpr int BK = 32;  // fp32 elements of K per stage (128 bytes per row)
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // A hi, A lo, B hi, B lo
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + static_cast<int>(sizeof(SmemCtl));
-    static constexpr uint32_t TMEM_COLS = BN;
+    static constexpr uint32_t TMEM_COLS = DRAIN ? 512 : BN;  // DRAIN: two chunk buffers + the running sum (3 BN)
+    static_assert(!DRAIN || 3 * BN <= 512, "drain needs three accumulator regions");
 };
 
 // split v into hi (v rounded to tf32: 10 explicit mantissa bits, ties away from zero) and lo = v - hi (exact)
@@ -560,12 +568,12 @@ struct ConvGeom {
     int H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog;
 };
 
-template <int BN, int STAGES, bool CONV, int ACTC>
+template <int BN, int STAGES, bool CONV, int ACTC, bool DRAIN>
 __global__ void __launch_bounds__(320, 1)
 k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
               const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
               int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv) {
-    using C = F32Cfg<BN, STAGES>;
+    using C = F32Cfg<BN, STAGES, DRAIN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + STAGES * C::STAGE_BYTES);
@@ -590,6 +598,10 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         for (int s = 0; s < STAGES; s++) {
             kx::mbar_init(&ctl->full[s], 1 + 4);  // TMA producer + 4 converter warps
             kx::mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {  // DRAIN: chunk buffer b holds a finished chunk / has been added in
+            kx::mbar_init(&ctl->acc_full[b], 1);
+            kx::mbar_init(&ctl->acc_empty[b], 4);
         }
         kx::mbar_init(&ctl->accf, 1);
         ctl->abort = 0;
@@ -627,6 +639,12 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
             constexpr uint32_t idesc = kx::idesc_tf32(BM, BN);
             for (int kb = 0; kb < nk; kb++) {
                 const int s = kb % STAGES;
+                const int c = DRAIN ? kb / KC_BLOCKS : 0, kc = DRAIN ? kb % KC_BLOCKS : kb;  // chunk, block in chunk
+                const uint32_t d = tmem + (DRAIN ? (c & 1) * BN : 0);
+                if (DRAIN && kc == 0) {  // chunk buffer free: the epilogue has added chunk c - 2 in
+                    if (!kx::mbar_wait(&ctl->acc_empty[c & 1], ((c >> 1) & 1) ^ 1, abort_flag, status)) break;
+                    kx::tc_fence_after();
+                }
                 if (!kx::mbar_wait(&ctl->full[s], (kb / STAGES) & 1, abort_flag, status)) break;
                 kx::tc_fence_after();
                 const uint32_t ah = kx::smem_u32(sAhi(s)), al = kx::smem_u32(sAlo(s));
@@ -634,11 +652,12 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
 #pragma unroll
                 for (int kk = 0; kk < C::BK / 8; kk++) {
                     const uint32_t o = kk * 32;  // 8 tf32 = 32 bytes of K per MMA
-                    kx::mma_tf32(tmem, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
-                    kx::mma_tf32(tmem, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
-                    kx::mma_tf32(tmem, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
+                    kx::mma_tf32(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
+                    kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                    kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
                 }
                 kx::mma_commit(&ctl->empty[s]);
+                if (DRAIN && (kc == KC_BLOCKS - 1 || kb == nk - 1)) kx::mma_commit(&ctl->acc_full[c & 1]);
             }
             kx::mma_commit(&ctl->accf);
         }
@@ -646,13 +665,39 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
     } else if (warp < 6) {
         const int q = warp & 3;
         const int row = m0 + q * 32 + lane;
+        const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        uint32_t sum_col = 0;  // TMEM column of the finished sums
+        if (DRAIN) {  // add each chunk into the running sum at columns 2 BN .. 3 BN
+            const int nchunks = (nk + KC_BLOCKS - 1) / KC_BLOCKS;
+            for (int c = 0; c < nchunks; c++) {
+                if (!kx::mbar_wait(&ctl->acc_full[c & 1], (c >> 1) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t p[32], t[32];
+                    kx::tmem_ld32(tmem + lanes + (c & 1) * BN + c0, p);
+                    if (c > 0) kx::tmem_ld32(tmem + lanes + 2 * BN + c0, t);
+                    kx::tmem_ld_wait();
+                    if (c > 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++) p[j] = __float_as_uint(__fadd_rn(__uint_as_float(t[j]), __uint_as_float(p[j])));
+                    }
+                    kx::tmem_st32(tmem + lanes + 2 * BN + c0, p);
+                }
+                kx::tmem_st_wait();
+                kx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[c & 1]);
+            }
+            sum_col = 2 * BN;
+        }
         drain_wait(&ctl->accf, 0);
         kx::tc_fence_after();
         const bool ok = !*abort_flag;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
             uint32_t r[32];
-            kx::tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, r);
+            kx::tmem_ld32(tmem + lanes + sum_col + c0, r);
             kx::tmem_ld_wait();
             const int col = n0 + c0;
             if (!ok || row >= M || col >= N) continue;
@@ -938,19 +983,19 @@ int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq,
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-template <int BN, bool CONV, int ACTC>
+template <int BN, bool CONV, int ACTC, bool DRAIN>
 int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
                int groups) {
     constexpr int STAGES = BN == 256 ? 2 : 3;
-    using C = F32Cfg<BN, STAGES>;
+    using C = F32Cfg<BN, STAGES, DRAIN>;
     CUtensorMap th, tl;
     if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
                     static_cast<uint64_t>(ldw) * 4, C::BK, BN) != 0 ||
         make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
                     static_cast<uint64_t>(ldw) * 4, C::BK, BN) != 0)
         return -1;
-    auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC>;
+    auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
     kern<<<grid, 320, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
@@ -1016,17 +1061,20 @@ int dispatch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, in
     }
 }
 
-template <int BN, bool CONV>
+template <int BN, bool CONV, bool DRAIN = false>
 int dispatch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
                  int groups) {
+    if (!DRAIN && k > DRAIN_MIN_K)  // long reductions: 128-column tiles with chunk draining
+        return dispatch_f32<128, CONV, true>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv,
+                                             groups);
     switch (act_class(act)) {
-    case -1: return launch_f32<BN, CONV, -1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
-    case 0: return launch_f32<BN, CONV, 0>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
-    case 1: return launch_f32<BN, CONV, 1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
+    case -1: return launch_f32<BN, CONV, -1, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
+    case 0: return launch_f32<BN, CONV, 0, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
+    case 1: return launch_f32<BN, CONV, 1, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
     default:
-        return launch_f32<BN, CONV, ACT_GENERIC>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv,
-                                                 groups);
+        return launch_f32<BN, CONV, ACT_GENERIC, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st,
+                                                        cv, groups);
     }
 }
 

@@ -10,9 +10,9 @@ from conftest import ROOT, rel_err
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(ROOT, "tests", "golden")
-# wide's last layer has K = 9000: tcgen05's truncating fp32 accumulation puts it at ~2e-5; the reference's own bound
-# for this model is 1e-4 (test/model_test.c:127-142)
-TOL = dict(small=1e-5, wide=1e-4, inplace_first=1e-5, small_int8=1e-4, q8_s=1e-4, cnn_s=1e-4, tfm_s=1e-4, g_cnn=1e-5,
+# wide's last layer has K = 9000: it drains its partial sums every 256 (the GEMM's long-reduction mode), which keeps
+# it at the dense-MLP bound 1e-5; the reference's own bound for this model is 1e-4 (test/model_test.c:127-142)
+TOL = dict(small=1e-5, wide=1e-5, inplace_first=1e-5, small_int8=1e-4, q8_s=1e-4, cnn_s=1e-4, tfm_s=1e-4, g_cnn=1e-5,
            g_attn=1e-5)
 
 
