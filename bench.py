@@ -219,6 +219,23 @@ class Clocks:
 
 
 # --------------------------------------------------------------------------------------- GPU bench
+def reduce_max(dist, v, device):
+    """The maximum of v over all ranks (v itself without a process group): every rank's timed region is
+    reported as the slowest rank's."""
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rank_batch(rank):
+    """The seeded synthetic input rows of one rank: every rank runs its own BATCH samples (weak scaling)."""
+    from kernix_b200 import configs
+    return configs.inputs(CFG, BATCH, seed=100 + rank)
+
+
 def run_kernix(args):
     import numpy as np
     import torch
@@ -240,11 +257,7 @@ def run_kernix(args):
         torch.cuda.synchronize()
 
     def max_over_ranks(v):
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return reduce_max(dist, v, "cuda")
 
     from kernix_b200 import Model, build, configs, kx_abi
     build.build()
@@ -257,7 +270,7 @@ def run_kernix(args):
     os.environ["KERNIX_DEVICE"] = str(local)
     path = model_file(rank)
     m = Model(path)
-    x_np = configs.inputs(CFG, BATCH, seed=100 + rank)
+    x_np = rank_batch(rank)
     x_pin = torch.from_numpy(x_np).pin_memory()
     out_pin = torch.empty((BATCH, DIMS[-1]), dtype=torch.float32).pin_memory()
     x_dev = x_pin.cuda()

@@ -25,6 +25,29 @@ KERNIX_API int kernix_model_forward_device(kernix_model* m, const float* d_x, in
  * finished normally, -1 if one gave up on a bounded wait (the output is then invalid). Resets the flag. */
 KERNIX_API int kernix_model_check(kernix_model* m);
 
+/* ------------------------------------------------------------------ output-column sharding across GPUs
+ * (extension; no counterpart in the reference, whose GPU/CPU row split of one sgemm, src/kernix_metal.m:161-265,
+ * becomes a split of wide dense layers across the GPUs of one node).
+ *
+ * One process per GPU loads the same .knx with its rank. Every fp32 LINEAR step with at least
+ * KERNIX_SHARD_MIN_COLS outputs, divisible by world, keeps only its slice of weight and bias columns
+ * [out * rank / world, out * (rank + 1) / world); the forward computes that slice of the layer's output, then the
+ * caller-supplied all-gather assembles every rank's slice (rank-major: [world][rows][out / world]) and a kernel
+ * re-interleaves it into the full rows for the next step. All other steps run whole on every rank, so every rank
+ * returns the full output. The collective order is the step order, the same on every rank; the host-memory
+ * forward of a sharded model runs each chunk in one piece for that reason. */
+#define KERNIX_SHARD_MIN_COLS 1024
+
+/* All-gather of `count` floats per rank: every rank's `send` (device) lands in `recv` (device, world * count
+ * floats, rank r at offset r * count), ordered on `stream` (a cudaStream_t) after the work already on it, and
+ * later work on the stream waits for it. Returns 0 on success. */
+typedef int (*kernix_allgather_fn)(void* ctx, const float* send, float* recv, size_t count, void* stream);
+
+/* kernix_model_load for rank `rank` of `world` processes (0 <= rank < world); `gather` is called with `ctx` at
+ * every sharded step. world = 1 loads the whole model (gather unused). NULL on failure, as kernix_model_load. */
+KERNIX_API kernix_model* kernix_model_load_sharded(const char* path, int rank, int world, kernix_allgather_fn gather,
+                                                   void* ctx);
+
 #ifdef __cplusplus
 }
 #endif

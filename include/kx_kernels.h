@@ -143,6 +143,11 @@ KERNIX_API int kx_attention(const float* q, int ldq, const float* k, int ldk, co
 /* y = max(a*x + b, 0), fused multiply-add then max (src/kernix_metal.m:331-338; include/kernix.h:990) */
 KERNIX_API int kx_fma_relu(const float* a, const float* x, const float* b, float* y, size_t n, void* stream);
 
+/* Re-interleave an all-gathered column-sharded output: src = [world][rows][slice] -> y rows x (world * slice)
+ * with row pitch ldy: y[r][g * slice + j] = src[(g * rows + r) * slice + j]. (Extension; the reference has no
+ * sharding.) */
+KERNIX_API int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y, int ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -51,6 +51,10 @@ struct kx_model_impl {
     int* status;          /* device status word of bounded waits */
     int* status_h;        /* pinned host copy */
     size_t scratch_per_row_max;
+    /* output-column sharding (kernix_model_load_sharded) */
+    int rank, world;
+    kernix_allgather_fn gather;
+    void* gather_ctx;
     /* host output owned by the model (pinned) */
     float* out_host;
     size_t out_host_floats;
@@ -109,6 +113,21 @@ static int prep_f32_into(const kx_weight* w, float* hi, float* lo, int ldw, size
     return rc;
 }
 
+/* columns [c0, c0 + n) of a float weight k x N -> tf32 split planes n x ldw (the weight of one output slice) */
+static int prep_f32_cols(kx_weight* w, int c0, int n, cudaStream_t st) {
+    w->ldw = (int)round_up((size_t)w->k, 32);
+    const size_t bytes = (size_t)n * w->ldw * sizeof(float);
+    if (cudaMalloc((void**)&w->d_hi, bytes) != cudaSuccess || cudaMalloc((void**)&w->d_lo, bytes) != cudaSuccess) return -1;
+    float* raw = NULL;
+    if (cudaMalloc((void**)&raw, (size_t)w->k * n * sizeof(float)) != cudaSuccess) return -1;
+    int rc = cudaMemcpy2DAsync(raw, (size_t)n * sizeof(float), w->f + c0, (size_t)w->n * sizeof(float), (size_t)n * sizeof(float),
+                               (size_t)w->k, cudaMemcpyHostToDevice, st) == cudaSuccess ? 0 : -1;
+    if (rc == 0) rc = kx_prep_f32_weight(raw, w->k, n, w->d_hi, w->d_lo, w->ldw, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) rc = -1;
+    cudaFree(raw);
+    return rc;
+}
+
 static int prep_f32(kx_weight* w, cudaStream_t st) {
     w->ldw = (int)round_up((size_t)w->k, 32);
     const size_t bytes = (size_t)w->n * w->ldw * sizeof(float);
@@ -150,6 +169,10 @@ static int conv_depthwise(const kx_step* s) { return s->groups > 1 && s->in / s-
 static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
     switch (s->kind) {
     case KERNIX_OP_LINEAR:
+        if (s->shard_n > 0) { /* this rank's output columns only */
+            if (prep_f32_cols(&s->w, s->shard_c0, s->shard_n, st)) return -1;
+            return upload_f(&s->d_bias, s->bias ? s->bias + s->shard_c0 : NULL, (size_t)s->shard_n, st);
+        }
         if (s->w.int8 ? prep_i8(&s->w, st) : prep_f32(&s->w, st)) return -1;
         return upload_f(&s->d_bias, s->bias, (size_t)s->out, st);
     case KERNIX_OP_CONV:
@@ -216,7 +239,9 @@ static void step_dev_free(kx_step* s) {
 static size_t step_scratch(const kx_graph* g, const kx_step* s, size_t* per_sample) {
     *per_sample = 0;
     const kx_val* vi = &g->vals[s->inp[0]];
-    if (s->kind == KERNIX_OP_LINEAR && s->w.int8) {
+    if (s->kind == KERNIX_OP_LINEAR && s->shard_n > 0) { /* local slice, then the gathered [world][rows][slice] */
+        *per_sample = (size_t)vi->r * ((size_t)s->shard_n + (size_t)s->out) * sizeof(float) + 2 * KX_ALIGN;
+    } else if (s->kind == KERNIX_OP_LINEAR && s->w.int8) {
         const size_t ldq = round_up((size_t)s->in, 16);
         *per_sample = (size_t)vi->r * (round_up(ldq, 16) + 4 * 4);
     } else if (s->kind == KERNIX_OP_ATTENTION) {
@@ -325,6 +350,18 @@ static int step_run(kernix_model* m, int i, int B) {
             if (kx_quant_rows(a, s->in, (int)rin, s->in, xq, ldq, sx, st) != 0) return -1;
             return kx_gemm_i8(xq, ldq, sx, s->w.d_q, s->w.ldw, s->w.d_scale, s->d_bias, y, s->out, (int)rin, s->out, s->in,
                               s->act, s->alpha, im->status, st);
+        }
+        if (s->shard_n > 0) { /* this rank's columns, all-gather across ranks, re-interleave into full rows */
+            float* yl = (float*)align_ptr(im->scratch);
+            float* yg = (float*)align_ptr(yl + (size_t)rin * s->shard_n);
+            if (kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, yl, s->shard_n, (int)rin, s->shard_n, s->in,
+                            s->act, s->alpha, im->status, st) != 0)
+                return -1;
+            if (im->gather(im->gather_ctx, yl, yg, (size_t)rin * s->shard_n, st) != 0) {
+                fprintf(stderr, "forward: the all-gather of step %d failed\n", i);
+                return -1;
+            }
+            return kx_unshard_cols(yg, im->world, rin, s->shard_n, y, s->out, st);
         }
         return kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act,
                            s->alpha, im->status, st);
@@ -615,13 +652,25 @@ static size_t ws_count(kernix_model* m) {
 }
 
 /* ------------------------------------------------------------------------------------ public API */
-KERNIX_API kernix_model* kernix_model_load(const char* path) {
+static kernix_model* model_load(const char* path, int rank, int world, kernix_allgather_fn gather, void* ctx) {
     const char* err = NULL;
+    if (world < 1 || rank < 0 || rank >= world || (world > 1 && gather == NULL)) {
+        fprintf(stderr, "model load failed (%s): bad shard arguments (rank %d of %d)\n", path ? path : "NULL", rank, world);
+        return NULL;
+    }
     kx_graph* g = kx_graph_load(path, &err);
     if (g == NULL) {
         fprintf(stderr, "model load failed (%s): %s\n", path ? path : "NULL", err);
         return NULL;
     }
+    if (world > 1) /* wide fp32 LINEAR steps keep one output slice per rank */
+        for (int i = 0; i < g->n_steps; i++) {
+            kx_step* s = &g->steps[i];
+            if (s->kind == KERNIX_OP_LINEAR && !s->w.int8 && s->out >= KERNIX_SHARD_MIN_COLS && s->out % world == 0) {
+                s->shard_n = s->out / world;
+                s->shard_c0 = s->shard_n * rank;
+            }
+        }
     kernix_model* m = calloc(1, sizeof *m);
     struct kx_model_impl* im = calloc(1, sizeof *im);
     if (m == NULL || im == NULL) {
@@ -633,6 +682,10 @@ KERNIX_API kernix_model* kernix_model_load(const char* path) {
     }
     m->impl = im;
     im->g = g;
+    im->rank = rank;
+    im->world = world;
+    im->gather = gather;
+    im->gather_ctx = ctx;
     m->batch = -1;
     const kx_val* vin = &g->vals[0];
     const kx_val* vout = &g->vals[g->out_v];
@@ -667,8 +720,8 @@ KERNIX_API kernix_model* kernix_model_load(const char* path) {
     if (why == NULL && cudaHostAlloc((void**)&im->status_h, sizeof(int), cudaHostAllocDefault) != cudaSuccess)
         why = "cannot allocate host memory";
     const char* pe = getenv("KERNIX_PIPELINE");
-    im->pipe_fixed = pe && *pe;
-    im->pipe = im->pipe_fixed ? atoi(pe) : 4;
+    im->pipe_fixed = (pe && *pe) || world > 1; /* sharded: the same pieces (collectives) on every rank */
+    im->pipe = pe && *pe ? atoi(pe) : (world > 1 ? 1 : 4);
     if (im->pipe < 1) im->pipe = 1;
     if (im->pipe > KX_PIPE_MAX) im->pipe = KX_PIPE_MAX;
     im->pipe_now = im->pipe;
@@ -695,6 +748,13 @@ KERNIX_API kernix_model* kernix_model_load(const char* path) {
         s->bias = s->bk = s->bv = s->bo = s->gamma = s->beta = s->cst = NULL;
     }
     return m;
+}
+
+KERNIX_API kernix_model* kernix_model_load(const char* path) { return model_load(path, 0, 1, NULL, NULL); }
+
+KERNIX_API kernix_model* kernix_model_load_sharded(const char* path, int rank, int world, kernix_allgather_fn gather,
+                                                   void* ctx) {
+    return model_load(path, rank, world, gather, ctx);
 }
 
 KERNIX_API void kernix_model_free(kernix_model* m) {

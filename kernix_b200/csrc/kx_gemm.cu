@@ -531,13 +531,16 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ------------------------------------------------------------------------------------------ 3xTF32
-// DRAIN: for long reductions the MMA accumulates chunks of KC_BLOCKS K blocks (256 K) into two alternating TMEM
-// buffers, and the epilogue warps add every chunk into an fp32 running sum kept in a third TMEM region with
-// round-to-nearest adds (sum = ((P0 + P1) + P2) + ..., a fixed order). The tensor core's accumulation truncates,
-// which costs about 2e-9 * (accumulation length) relative error; draining bounds that length by 256, so K = 16384
-// stays near 1e-6 instead of 3e-5.
+// Accuracy of the 3xTF32 product A.B = Ah.Bh + (Al.Bh + Ah.Bl): the tensor core adds each MMA's result into the
+// fp32 accumulator with truncation, which shrinks the sum's magnitude by about 1.6e-8 per accumulated MMA
+// (measured). So the two small cross terms accumulate in their own TMEM region (their truncation is 2^-11
+// smaller), and the large Ah.Bh sum sees one MMA per 8 K. DRAIN, for long reductions: Ah.Bh accumulates chunks of
+// KC_BLOCKS K blocks (256 K) into two alternating TMEM buffers, and the epilogue warps add every chunk into an fp32
+// running sum in a third region with round-to-nearest adds (((P0 + P1) + P2) + ..., a fixed order), which bounds
+// the truncated accumulation length by 32 MMAs: about 5e-7 per layer at any K. The result is running sum (or
+// Ah.Bh sum) + cross terms, rounded to nearest.
 constexpr int KC_BLOCKS = 8;
-constexpr int DRAIN_MIN_K = 2048;  // reductions longer than this drain
+constexpr int DRAIN_MIN_K = 1024;  // reductions longer than this drain
 template <int BN, int STAGES, bool DRAIN = false>
 struct F32Cfg {
     static constexpr int BK = 32;  // fp32 elements of K per stage (128 bytes per row)
@@ -545,8 +548,10 @@ struct F32Cfg {
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // A hi, A lo, B hi, B lo
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + static_cast<int>(sizeof(SmemCtl));
-    static constexpr uint32_t TMEM_COLS = DRAIN ? 512 : BN;  // DRAIN: two chunk buffers + the running sum (3 BN)
-    static_assert(!DRAIN || 3 * BN <= 512, "drain needs three accumulator regions");
+    // TMEM: [Ah.Bh | cross] or, draining, [Ah.Bh chunk 0 | Ah.Bh chunk 1 | cross | running sum]
+    static constexpr uint32_t MAIN0 = 0, CROSS = DRAIN ? 2 * BN : BN, RUN = 3 * BN;
+    static constexpr uint32_t TMEM_COLS = DRAIN ? 512 : 2 * BN;
+    static_assert((DRAIN ? 4 : 2) * BN <= 512, "accumulator regions exceed TMEM");
 };
 
 // split v into hi (v rounded to tf32: 10 explicit mantissa bits, ties away from zero) and lo = v - hi (exact)
@@ -640,7 +645,7 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
             for (int kb = 0; kb < nk; kb++) {
                 const int s = kb % STAGES;
                 const int c = DRAIN ? kb / KC_BLOCKS : 0, kc = DRAIN ? kb % KC_BLOCKS : kb;  // chunk, block in chunk
-                const uint32_t d = tmem + (DRAIN ? (c & 1) * BN : 0);
+                const uint32_t d = tmem + (DRAIN ? (c & 1) * BN : C::MAIN0), dx = tmem + C::CROSS;
                 if (DRAIN && kc == 0) {  // chunk buffer free: the epilogue has added chunk c - 2 in
                     if (!kx::mbar_wait(&ctl->acc_empty[c & 1], ((c >> 1) & 1) ^ 1, abort_flag, status)) break;
                     kx::tc_fence_after();
@@ -652,9 +657,9 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
 #pragma unroll
                 for (int kk = 0; kk < C::BK / 8; kk++) {
                     const uint32_t o = kk * 32;  // 8 tf32 = 32 bytes of K per MMA
-                    kx::mma_tf32(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
-                    kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
-                    kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
+                    kx::mma_tf32(dx, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
+                    kx::mma_tf32(dx, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                    kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
                 }
                 kx::mma_commit(&ctl->empty[s]);
                 if (DRAIN && (kc == KC_BLOCKS - 1 || kb == nk - 1)) kx::mma_commit(&ctl->acc_full[c & 1]);
@@ -666,8 +671,8 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         const int q = warp & 3;
         const int row = m0 + q * 32 + lane;
         const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
-        uint32_t sum_col = 0;  // TMEM column of the finished sums
-        if (DRAIN) {  // add each chunk into the running sum at columns 2 BN .. 3 BN
+        uint32_t sum_col = C::MAIN0;  // TMEM column of the finished Ah.Bh sums
+        if (DRAIN) {  // add each chunk into the running sum
             const int nchunks = (nk + KC_BLOCKS - 1) / KC_BLOCKS;
             for (int c = 0; c < nchunks; c++) {
                 if (!kx::mbar_wait(&ctl->acc_full[c & 1], (c >> 1) & 1, abort_flag, status)) break;
@@ -676,29 +681,32 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     uint32_t p[32], t[32];
                     kx::tmem_ld32(tmem + lanes + (c & 1) * BN + c0, p);
-                    if (c > 0) kx::tmem_ld32(tmem + lanes + 2 * BN + c0, t);
+                    if (c > 0) kx::tmem_ld32(tmem + lanes + C::RUN + c0, t);
                     kx::tmem_ld_wait();
                     if (c > 0) {
 #pragma unroll
                         for (int j = 0; j < 32; j++) p[j] = __float_as_uint(__fadd_rn(__uint_as_float(t[j]), __uint_as_float(p[j])));
                     }
-                    kx::tmem_st32(tmem + lanes + 2 * BN + c0, p);
+                    kx::tmem_st32(tmem + lanes + C::RUN + c0, p);
                 }
                 kx::tmem_st_wait();
                 kx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[c & 1]);
             }
-            sum_col = 2 * BN;
+            sum_col = C::RUN;
         }
         drain_wait(&ctl->accf, 0);
         kx::tc_fence_after();
         const bool ok = !*abort_flag;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32];
+            uint32_t r[32], x[32];
             kx::tmem_ld32(tmem + lanes + sum_col + c0, r);
+            kx::tmem_ld32(tmem + lanes + C::CROSS + c0, x);
             kx::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(x[j])));
             const int col = n0 + c0;
             if (!ok || row >= M || col >= N) continue;
             const int nv = N - col;

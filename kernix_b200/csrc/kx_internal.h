@@ -58,6 +58,7 @@ typedef struct {
     kx_weight wqkv;
     float* d_bqkv;
     size_t scratch_per_row; /* bytes of scratch per input row this step needs */
+    int shard_c0, shard_n;  /* sharded LINEAR: this rank keeps output columns [shard_c0, shard_c0 + shard_n); 0 = whole */
 } kx_step;
 
 /* Parsed graph (host side), the output of kx_graph_load */

@@ -564,9 +564,37 @@ __global__ void k_fma_relu(const float* __restrict__ a, const float* __restrict_
         y[i] = fmaxf(__fmaf_rn(a[i], x[i], b[i]), 0.0f);
 }
 
+// [world][rows][slice] -> rows x (world * slice), one float4 (slice % 4 == 0) or one float per thread
+template <int V>
+__global__ void k_unshard_cols(const float* __restrict__ src, int world, long rows, int slice, float* __restrict__ y, int ldy) {
+    const long per_row = static_cast<long>(world) * slice / V;
+    const long n = rows * per_row;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const long r = i / per_row;
+        const int c = static_cast<int>(i - r * per_row) * V;
+        const int g = c / slice, j = c - g * slice;
+        const float* s = src + (static_cast<long>(g) * rows + r) * slice + j;
+        float* d = y + r * ldy + c;
+        if (V == 4) *reinterpret_cast<float4*>(d) = __ldg(reinterpret_cast<const float4*>(s));
+        else *d = __ldg(s);
+    }
+}
+
 }  // namespace
 
 extern "C" {
+
+int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y, int ldy, void* stream) {
+    if (rows <= 0 || world <= 0 || slice <= 0) return 0;
+    if (ldy < world * slice) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool vec = (slice % 4 == 0) && (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(y)) % 16 == 0);
+    const long n = rows * world * slice;
+    if (vec) k_unshard_cols<4><<<grid_for(n / 4, 256), 256, 0, st>>>(src, world, rows, slice, y, ldy);
+    else k_unshard_cols<1><<<grid_for(n, 256), 256, 0, st>>>(src, world, rows, slice, y, ldy);
+    return launch_ok();
+}
+
 
 int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream) {
     if (rows <= 0) return 0;

@@ -51,18 +51,43 @@ def lib():
         L.kernix_capi_ane_info.restype = None
         L.kernix_capi_ane_dump.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_char_p]
         L.kernix_capi_ane_dump.restype = ctypes.c_int
+        L.kernix_model_load_sharded.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, vp, vp]
+        L.kernix_model_load_sharded.restype = vp
         _lib = L
     return _lib
 
 
+# int gather(void* ctx, const float* send, float* recv, size_t count, void* stream)
+GATHER_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p)
+
+
 class Model:
-    def __init__(self, path, workspace_mb=None, ane=False):
+    def __init__(self, path, workspace_mb=None, ane=False, shard=None):
         """workspace_mb: bound of the forward workspace (device memory) in MB; larger batches run in chunks with
         identical results. None = library default, 0 = unlimited. ane: there is no Apple Neural Engine on a
-        B200 host, so ane=True warns and runs on the GPU."""
+        B200 host, so ane=True warns and runs on the GPU.
+        shard: (rank, world, gather) to split the wide fp32 dense layers by output columns across `world`
+        processes (kernix_model_load_sharded); gather(send_ptr, recv_ptr, count, stream) all-gathers `count`
+        device floats per rank on the CUDA stream (see kernix_b200.shard.torch_allgather)."""
         self._lock = threading.Lock()
         L = lib()
-        self._h = L.kernix_capi_load(os.fsencode(path))
+        self._gather_cb = None
+        if shard is None:
+            self._h = L.kernix_capi_load(os.fsencode(path))
+        else:
+            rank, world, gather = shard
+
+            def _cb(ctx, send, recv, count, stream):
+                try:
+                    gather(send or 0, recv or 0, int(count), stream or 0)
+                    return 0
+                except Exception as e:  # noqa: BLE001  (reported to the runtime as a failed step)
+                    warnings.warn(f"KERNIX all-gather failed: {e!r}", RuntimeWarning, stacklevel=1)
+                    return -1
+
+            self._gather_cb = GATHER_FN(_cb)  # kept alive as long as the model
+            self._h = L.kernix_model_load_sharded(os.fsencode(path), int(rank), int(world),
+                                                  ctypes.cast(self._gather_cb, ctypes.c_void_p), None)
         if not self._h:
             raise ValueError(f"cannot load KERNIX model: {path}")
         if workspace_mb is not None:

@@ -33,6 +33,7 @@ SIGNATURES = {
     "kx_conv_f32": [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 16 + [_i, _f, _vp, _vp],
     "kx_attention": [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "kx_fma_relu": [_vp, _vp, _vp, _vp, _sz, _vp],
+    "kx_unshard_cols": [_vp, _i, _l, _i, _vp, _i, _vp],
     "kx_knx_plan": [ctypes.c_char_p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i],
     "kx_knx_inspect": [ctypes.c_char_p, ctypes.POINTER(_l), ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i), _i,
                        ctypes.c_char_p, _i],
