@@ -550,6 +550,177 @@ __global__ void k_attention(const float* __restrict__ q, int ldq, const float* _
     }
 }
 
+// Attention for short key sequences (S <= ATT_SMAX, head dims <= 64), register-tiled on the CUDA cores: one block of
+// 128 threads per (sample, head, tile of 64 query rows). Q^T (d x 64), K^T (d x SP) and V (SP x 64) are staged in
+// shared memory; thread (ty, tx) owns queries 8 ty .. 8 ty + 7 and, per 128-key chunk, keys 8 tx .. 8 tx + 7, so each
+// step of the score loop reads two float4 of Q^T (a broadcast within the half-warp) and two of K^T (contiguous
+// across the half-warp) for 64 fmas. s = (q . k) * scale (fma over d, then the scale, as alpha * (Q K^T)); the 16
+// threads of a row reduce its max and sum with shuffles; P^T = exp(s - max) * (1 / sum) (keys x queries) replaces
+// K^T in shared memory; thread (ty, tx) then owns ctx rows 8 ty .. +7 x columns 4 tx .. +3 (one float4 of V and two
+// of P^T per key for 32 fmas).
+constexpr int ATT_TQ = 64, ATT_D = 64, ATT_SMAX = 256, ATT_KC = 128;
+__host__ __device__ constexpr int att_smem_floats(int SP) {
+    return SP * ATT_D + ATT_D * ATT_TQ + (ATT_D > ATT_TQ ? ATT_D : ATT_TQ) * SP;
+}
+__global__ void __launch_bounds__(128) k_attention_tiled(const float* __restrict__ q, int ldq, const float* __restrict__ k,
+                                                         int ldk, const float* __restrict__ v, int ldv, float* __restrict__ ctx,
+                                                         int ldc, int Rq, int S, int dk, int dv, int causal, float scale) {
+    extern __shared__ __align__(16) float sm[];
+    const int SP = (S + 15) / 16 * 16;  // keys padded to a multiple of 16
+    float* vs = sm;                      // SP x ATT_D
+    float* qT = vs + SP * ATT_D;         // ATT_D x ATT_TQ
+    float* kT = qT + ATT_D * ATT_TQ;     // ATT_D x SP, then P^T: SP x ATT_TQ
+    float* pT = kT;
+    const int h = blockIdx.y, b = blockIdx.z, r0 = blockIdx.x * ATT_TQ;
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const float* qb = q + static_cast<long>(b) * Rq * ldq + h * dk;
+    const float* kb = k + static_cast<long>(b) * S * ldk + h * dk;
+    const float* vb = v + static_cast<long>(b) * S * ldv + h * dv;
+    const bool v4 = ((ldq | ldk | ldv | dk | dv) & 3) == 0 &&
+                    ((reinterpret_cast<uintptr_t>(qb) | reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15) == 0;
+    auto load4 = [&](const float* src, int d, int dmax, bool live) -> float4 {
+        if (!live || d >= dmax) return make_float4(0.f, 0.f, 0.f, 0.f);
+        if (v4) return __ldg(reinterpret_cast<const float4*>(src + d));
+        return make_float4(src[d], d + 1 < dmax ? src[d + 1] : 0.f, d + 2 < dmax ? src[d + 2] : 0.f, d + 3 < dmax ? src[d + 3] : 0.f);
+    };
+    // staging, 4 consecutive d of one row per float4; loads are issued U at a time before their stores so that
+    // their latencies overlap
+    constexpr int U = 8;
+    for (int t0 = 0; t0 < ATT_TQ * ATT_D / 4; t0 += 128 * U) {
+        float4 x[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int t = t0 + u * 128 + tid, row = t / (ATT_D / 4), d = 4 * (t - row * (ATT_D / 4));
+            x[u] = load4(qb + static_cast<long>(r0 + row) * ldq, d, dk, t < ATT_TQ * ATT_D / 4 && r0 + row < Rq);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int t = t0 + u * 128 + tid, row = t / (ATT_D / 4), d = 4 * (t - row * (ATT_D / 4));
+            if (t < ATT_TQ * ATT_D / 4)
+                qT[d * ATT_TQ + row] = x[u].x, qT[(d + 1) * ATT_TQ + row] = x[u].y, qT[(d + 2) * ATT_TQ + row] = x[u].z,
+                qT[(d + 3) * ATT_TQ + row] = x[u].w;
+        }
+    }
+    for (int t0 = 0; t0 < SP * ATT_D / 4; t0 += 128 * U) {
+        float4 x[U], y[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int t = t0 + u * 128 + tid, j = t / (ATT_D / 4), d = 4 * (t - j * (ATT_D / 4));
+            const bool live = t < SP * ATT_D / 4 && j < S;
+            x[u] = load4(kb + static_cast<long>(j) * ldk, d, dk, live);
+            y[u] = load4(vb + static_cast<long>(j) * ldv, d, dv, live);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int t = t0 + u * 128 + tid, j = t / (ATT_D / 4), d = 4 * (t - j * (ATT_D / 4));
+            if (t < SP * ATT_D / 4) {
+                kT[d * SP + j] = x[u].x, kT[(d + 1) * SP + j] = x[u].y, kT[(d + 2) * SP + j] = x[u].z, kT[(d + 3) * SP + j] = x[u].w;
+                *reinterpret_cast<float4*>(vs + j * ATT_D + d) = y[u];
+            }
+        }
+    }
+    __syncthreads();
+    // scores of rows 8 ty + i: key chunks of 128, keys 8 tx + c of each
+    constexpr int NCH = ATT_SMAX / ATT_KC;
+    float sc[NCH][8][8];
+    const int nch = (SP + ATT_KC - 1) / ATT_KC;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ch++) {
+        if (ch >= nch) break;
+        const int j0 = ch * ATT_KC + 8 * tx;
+        const bool kin = j0 < SP;  // keys of this thread's group exist in the padded range
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int c = 0; c < 8; c++) sc[ch][i][c] = 0.0f;
+        if (kin)
+            for (int d = 0; d < dk; d++) {
+                const float4 qa = *reinterpret_cast<const float4*>(qT + d * ATT_TQ + 8 * ty);
+                const float4 qc = *reinterpret_cast<const float4*>(qT + d * ATT_TQ + 8 * ty + 4);
+                const float4 ka = *reinterpret_cast<const float4*>(kT + d * SP + j0);
+                const float4 kc = *reinterpret_cast<const float4*>(kT + d * SP + j0 + 4);
+                const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qc.x, qc.y, qc.z, qc.w};
+                const float kv[8] = {ka.x, ka.y, ka.z, ka.w, kc.x, kc.y, kc.z, kc.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int c = 0; c < 8; c++) sc[ch][i][c] = __fmaf_rn(qv[i], kv[c], sc[ch][i][c]);
+            }
+    }
+    __syncthreads();  // every thread is done reading K^T before P^T overwrites it
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int row = r0 + 8 * ty + i;
+        float m = -INFINITY;
+#pragma unroll
+        for (int ch = 0; ch < NCH; ch++) {
+            if (ch >= nch) break;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const int j = ch * ATT_KC + 8 * tx + c;
+                float s = __fmul_rn(sc[ch][i][c], scale);
+                if (j >= S || (causal && j > row)) s = -INFINITY;
+                sc[ch][i][c] = s;
+                m = fmaxf(m, s);
+            }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float sum = 0.0f;
+#pragma unroll
+        for (int ch = 0; ch < NCH; ch++) {
+            if (ch >= nch) break;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const float e = expf(__fsub_rn(sc[ch][i][c], m));
+                sc[ch][i][c] = e;
+                sum = __fadd_rn(sum, e);
+            }
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+        const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+        for (int ch = 0; ch < NCH; ch++) {
+            if (ch >= nch) break;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const int j = ch * ATT_KC + 8 * tx + c;
+                if (j < SP) pT[j * ATT_TQ + 8 * ty + i] = __fmul_rn(sc[ch][i][c], inv);
+            }
+        }
+    }
+    __syncthreads();
+    // ctx rows 8 ty + i, columns 4 tx + e
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[i][e] = 0.0f;
+    for (int j = 0; j < S; j++) {
+        const float4 vv = *reinterpret_cast<const float4*>(vs + j * ATT_D + 4 * tx);
+        const float4 pa = *reinterpret_cast<const float4*>(pT + j * ATT_TQ + 8 * ty);
+        const float4 pc = *reinterpret_cast<const float4*>(pT + j * ATT_TQ + 8 * ty + 4);
+        const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pc.x, pc.y, pc.z, pc.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            acc[i][0] = __fmaf_rn(pv[i], vv.x, acc[i][0]);
+            acc[i][1] = __fmaf_rn(pv[i], vv.y, acc[i][1]);
+            acc[i][2] = __fmaf_rn(pv[i], vv.z, acc[i][2]);
+            acc[i][3] = __fmaf_rn(pv[i], vv.w, acc[i][3]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int row = r0 + 8 * ty + i;
+        if (row >= Rq) continue;
+        float* dst = ctx + (static_cast<long>(b) * Rq + row) * ldc + h * dv;
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            if (4 * tx + e < dv) dst[4 * tx + e] = acc[i][e];
+    }
+}
+
 __global__ void k_fma_relu(const float* __restrict__ a, const float* __restrict__ x, const float* __restrict__ b,
                            float* __restrict__ y, size_t n) {
     const size_t n4 = n >> 2;
@@ -740,6 +911,25 @@ int kx_attention(const float* q, int ldq, const float* k, int ldk, const float* 
                  int Rq, int S, int H, int dk, int dv, int causal, void* stream) {
     if (B <= 0 || Rq <= 0) return 0;
     if (S <= 0 || dk <= 0 || dv <= 0 || dk > 128 || dv > 128) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (S <= ATT_SMAX && dk <= ATT_D && dv <= ATT_D) {
+        const int SP = (S + 15) / 16 * 16;
+        const size_t smem = static_cast<size_t>(att_smem_floats(SP)) * sizeof(float);
+        static unsigned long long devs_set = 0;  // devices whose kernel attribute holds the largest size (S = ATT_SMAX)
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+        const unsigned long long bit = 1ull << (dev & 63);
+        if (!(__atomic_load_n(&devs_set, __ATOMIC_ACQUIRE) & bit)) {
+            if (cudaFuncSetAttribute(k_attention_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     att_smem_floats(ATT_SMAX) * 4) != cudaSuccess)
+                return -1;
+            __atomic_fetch_or(&devs_set, bit, __ATOMIC_RELEASE);
+        }
+        const float scale = 1.0f / sqrtf(static_cast<float>(dk));
+        dim3 grid((Rq + ATT_TQ - 1) / ATT_TQ, H, B);
+        k_attention_tiled<<<grid, 128, smem, st>>>(q, ldq, k, ldk, v, ldv, ctx, ldc, Rq, S, dk, dv, causal, scale);
+        return launch_ok();
+    }
     int T = 128;
     while (T > 32 && static_cast<size_t>(S) * T * 4 > 160 * 1024) T >>= 1;
     const int D = (dk <= 64 && dv <= 64) ? 64 : 128;
@@ -747,7 +937,6 @@ int kx_attention(const float* q, int ldq, const float* k, int ldk, const float* 
     if (smem > 220 * 1024) return -1;
     const float scale = 1.0f / sqrtf(static_cast<float>(dk)); /* IEEE on the host, as the reference's 1.0f / sqrtf */
     dim3 grid((Rq + T - 1) / T, H, B);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (D == 64) {
         if (cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
             return -1;

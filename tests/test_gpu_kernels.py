@@ -362,9 +362,13 @@ def test_depthwise_embedding_fma_relu(kx):
 
 
 @pytest.mark.parametrize("Rq,S,H,dk,dv,causal,packed", [(128, 128, 8, 64, 64, False, False), (10, 10, 4, 4, 4, True, False),
-                                                        (5, 17, 2, 32, 48, False, False), (128, 128, 8, 64, 64, False, True)])
+                                                        (5, 17, 2, 32, 48, False, False), (128, 128, 8, 64, 64, False, True),
+                                                        (200, 200, 4, 64, 64, True, False), (256, 256, 2, 16, 64, False, True),
+                                                        (70, 300, 2, 80, 96, True, False), (33, 257, 3, 64, 64, False, False)])
 def test_attention_core(kx, Rq, S, H, dk, dv, causal, packed):
-    """packed: Q, K, V are column blocks of one [Q | K | V] row buffer (the fused-projection layout)."""
+    """packed: Q, K, V are column blocks of one [Q | K | V] row buffer (the fused-projection layout). S <= 256 with
+    head dims <= 64 run the register-tiled kernel (ragged query tiles, causal masks); longer or wider heads the
+    one-row-per-thread kernel."""
     rng = np.random.default_rng(Rq + S + dk)
     B = 3
     q = rng.standard_normal((B * Rq, H * dk)).astype(F32)
