@@ -34,9 +34,9 @@ DIMS = [1024, 4096, 4096, 1024]
 METRIC = "samples/s, int8 MLP 1024-4096-4096-1024 (config c2), batch 4096 per GPU"
 WORKLOAD = "c2: int8-quantised MLP 1024-4096-4096-1024, GELU hidden, I8_COL per-output-channel weights, batch 4096"
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) per int8-GEMM op from the ncu capture in profiles/k_gemm_i8_8192x4096x4096_full.md:
-# 156.3 MB for 274.9 GOP; the roofline's traffic per launch is this ratio times the launch's ops.
-GEMM_DRAM_BYTES_PER_OP = 156.3e6 / 274.9e9
+# DRAM bytes (read + write) per int8-GEMM op from the ncu capture in profiles/k_gemm_i8_pair_8192x4096x4096_full.md:
+# 167.3 MB for 274.9 GOP; the roofline's traffic per launch is this ratio times the launch's ops.
+GEMM_DRAM_BYTES_PER_OP = 167.3e6 / 274.9e9
 
 
 def parse():
@@ -50,6 +50,10 @@ def parse():
                     help="profiling case: only run the int8 GEMM of c2's 4096x4096 layer with M rows, 3 launches, then exit")
     ap.add_argument("--kernel-k", type=int, default=4096, help="K of the profiling case (1024: c2's first layer)")
     ap.add_argument("--kernel-act", type=int, default=1, help="activation of the profiling case (1 GELU, -1 none)")
+    ap.add_argument("--workload", choices=["c2", "c5-rows"], default="c2",
+                    help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
+                         "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling)")
+    ap.add_argument("--batch", type=int, default=64, help="global batch of --workload c5-rows")
     return ap.parse_args()
 
 
@@ -413,17 +417,115 @@ def gemm_roofline(L, torch, np, steps, flush):
     except (OSError, ValueError, KeyError):
         peak = 2.0 * 1590.0
         basis = "2 x fallback dense bf16 1.59 PFLOP/s"
-    return {"kernel": "k_gemm_i8 (tcgen05 kind::i8, 128x256 tiles)", "bound": "tensor", "achieved": achieved, "peak": peak,
+    return {"kernel": "k_gemm_i8_pair (tcgen05 kind::i8, cta_group::2, 256x256 tiles)", "bound": "tensor", "achieved": achieved, "peak": peak,
             "unit": "TOP/s (int8, 2 ops per MAC)", "frac": achieved / peak, "peak_basis": basis,
             "traffic": GEMM_DRAM_BYTES_PER_OP * tot_ops / len(per),
             "traffic_note": "bytes per launch, scaled by ops from the ncu capture of M=8192 (profiles/)", "per_layer": per,
             "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
 
 
+def run_c5_rows(args):
+    """Config c5 (fp32 MLP 8192-16384-16384-8192, ReLU) at a small batch, its three layers split by output columns
+    over the ranks (kernix_model_load_sharded + NCCL all-gather on the model's stream). value: batch * steps / (max
+    over ranks of the CUDA-event time of the timed steps); the weights (2.15 GB, 1/N per rank) stream from HBM every
+    step, larger than L2, so no flush is needed. e2e: kernix_capi_forward with page-locked host buffers."""
+    import datetime
+
+    import numpy as np
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+    from kernix_b200 import Model, build, configs, kx_abi, shard
+    build.build()
+    L = kx_abi.lib()
+    L.kernix_model_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    L.kernix_model_forward_device.restype = ctypes.c_int
+    L.kernix_model_check.argtypes = [ctypes.c_void_p]
+    L.kernix_model_check.restype = ctypes.c_int
+    if rank == 0:
+        configs.model_path("c5")
+    if dist is not None:
+        dist.barrier()
+    path = configs.model_path("c5")
+    os.environ["KERNIX_DEVICE"] = str(local)
+    m = Model(path, workspace_mb=0, shard=(rank, world, shard.torch_allgather()) if world > 1 else None)
+    B = args.batch
+    x_pin = torch.from_numpy(configs.inputs("c5", B, seed=100)).pin_memory()
+    out_pin = torch.empty((B, 8192), dtype=torch.float32).pin_memory()
+    x_dev = x_pin.cuda()
+    y_dev = torch.empty((B, 8192), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+
+    def step():
+        if L.kernix_model_forward_device(m._h, x_dev.data_ptr(), B, y_dev.data_ptr(), stream.cuda_stream) != 0:
+            raise RuntimeError("forward_device failed")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if L.kernix_model_check(m._h) != 0:
+        raise RuntimeError("a kernel reported a failure")
+    t = reduce_max(dist, e0.elapsed_time(e1) / 1e3, "cuda")
+    value = B * args.steps / t
+    # e2e through the C ABI with page-locked host buffers
+    for _ in range(2):
+        L.kernix_capi_forward(m._h, x_pin.data_ptr(), B, out_pin.data_ptr())
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        if L.kernix_capi_forward(m._h, x_pin.data_ptr(), B, out_pin.data_ptr()) != 0:
+            raise RuntimeError("kernix_capi_forward failed")
+    t_e2e = reduce_max(dist, time.perf_counter() - t0, "cuda")
+    if not np.array_equal(out_pin.numpy(), y_dev.cpu().numpy()):
+        raise RuntimeError("host-memory and device-memory forward disagree")
+    if rank == 0:
+        flops = 2.0 * 536870912 * B  # 536,870,912 MACs per sample
+        line = {
+            "metric": f"samples/s, fp32 MLP 8192-16384-16384-8192 (config c5), batch {B}, layers split by output columns",
+            "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic: inputs U[-1,1) seed 100, weights N(0, sqrt(2/fan_in)), b = 0.01",
+            "config": {"workload": f"c5-rows: c5 at batch {B}, every layer's output columns split over {world} GPU(s)",
+                       "global_batch": B, "parallelism": f"column-parallel x{world}, NCCL all-gather per layer",
+                       "l2": "no flush: 2.15 GB of weights stream from HBM every step"},
+            "e2e": {"value": B * args.steps / t_e2e, "unit": "samples/s", "h2d_bytes_per_step": B * 8192 * 4,
+                    "d2h_bytes_per_step": B * 8192 * 4, "api": "kernix_capi_forward, page-locked host buffers"},
+            "achieved_tflops": flops * args.steps / t / 1e12,
+            "weight_stream_gbs_per_gpu": 2 * 2.147e9 / world * args.steps / t / 1e9,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 if __name__ == "__main__":
     a = parse()
     if a.kernel_case:
         kernel_case(a.kernel_case, a.kernel_k, a.kernel_act)
+    elif a.workload == "c5-rows":
+        run_c5_rows(a)
     elif a.impl == "reference":
         run_reference(a)
     else:
