@@ -148,6 +148,17 @@ KERNIX_API int kx_fma_relu(const float* a, const float* x, const float* b, float
  * sharding.) */
 KERNIX_API int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y, int ldy, void* stream);
 
+/* One time step of one direction of an LSTM (kind 0), GRU (1) or SimpleRNN (2) (kernix_rnn_dir,
+ * include/kernix_model.h:560-634). zx: (B*T) x G*u input projections x.W + b of all steps (G = 4, 3, 1); U: u x G*u
+ * recurrent weights (row-major as in the file); brec: GRU recurrent bias (G*u); h_prev / h_next: B x u states
+ * (h_prev unused when first); c: B x u LSTM cell state; the state at time t goes to out + (b*T + t)*stride when
+ * ret_seq, else (when last) to out + b*stride. u <= 12288. */
+KERNIX_API int kx_rnn_step(int kind, const float* zx, const float* U, const float* brec, const float* h_prev, float* h_next,
+                           float* c, float* out, long stride, int B, int T, int t, int u, int first, int ret_seq, int last,
+                           int act, float alpha, void* stream);
+/* Merge of a bidirectional RNN's directions in place (kernix_rnn_run :641-646): merge 1 sum, 2 product, 3 average. */
+KERNIX_API int kx_rnn_merge(float* y, const float* bw, long n, int merge, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -201,7 +201,8 @@ static int parse_op(kx_rd* r, int ver, kx_step* s, const char** err) {
             kx_weight* wx = d ? &s->wk : &s->w; /* input and recurrent weights, per direction */
             kx_weight* wr = d ? &s->wo : &s->wv;
             if (rd_weight(r, ver, a[0], gu, 0, wx, err) != 0 || rd_weight(r, ver, a[1], gu, 1, wr, err) != 0) return -1;
-            if (rd_floats(r, nb) == NULL) return -1;
+            const float** bp = d ? &s->bk : &s->bias; /* input bias (gu), then for GRU the recurrent bias (gu) */
+            if ((*bp = rd_floats(r, nb)) == NULL) return -1;
         }
         return 0;
     }

@@ -149,6 +149,27 @@ static int prep_i8(kx_weight* w, cudaStream_t st) {
     return rc;
 }
 
+/* recurrent weights u x G*u as plain fp32 rows on the device (int8 blocks kept as int8 are dequantised first,
+ * as the reference's float copy of them, kernix_qweight_unpack :91-95) */
+static int upload_raw_f32(kx_weight* w, cudaStream_t st) {
+    if (!w->int8) return upload_f(&w->d_raw, w->f, (size_t)w->k * w->n, st);
+    const size_t cnt = (size_t)w->k * w->n;
+    float* tmp = malloc(cnt * sizeof(float));
+    if (tmp == NULL) return -1;
+    for (size_t i = 0; i < (size_t)w->k; i++)
+        for (size_t j = 0; j < (size_t)w->n; j++) {
+            float sc;
+            memcpy(&sc, w->scale_h + j, sizeof sc);
+            tmp[i * w->n + j] = (float)w->q[i * w->n + j] * sc;
+        }
+    int rc = upload_f(&w->d_raw, tmp, cnt, st);
+    if (rc == 0 && cudaStreamSynchronize(st) != cudaSuccess) rc = -1;
+    free(tmp);
+    return rc;
+}
+
+static size_t rnn_gates(int kind) { return kind == KERNIX_OP_LSTM ? 4 : kind == KERNIX_OP_GRU ? 3 : 1; }
+
 static void weight_dev_free(kx_weight* w) {
     cudaFree(w->d_hi);
     cudaFree(w->d_lo);
@@ -184,6 +205,14 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
         return upload_f(&s->d_bias, s->bias, (size_t)s->out, st);
     case KERNIX_OP_LAYERNORM:
         return upload_f(&s->d_gamma, s->gamma, (size_t)s->in, st) || upload_f(&s->d_beta, s->beta, (size_t)s->in, st) ? -1 : 0;
+    case KERNIX_OP_LSTM:
+    case KERNIX_OP_GRU:
+    case KERNIX_OP_RNN: {
+        const size_t gu = rnn_gates(s->kind) * (size_t)s->out, nb = s->kind == KERNIX_OP_GRU ? 2 * gu : gu;
+        if (prep_f32(&s->w, st) || upload_raw_f32(&s->wv, st) || upload_f(&s->d_bias, s->bias, nb, st)) return -1;
+        if (s->dirs == 2 && (prep_f32(&s->wk, st) || upload_raw_f32(&s->wo, st) || upload_f(&s->d_bk, s->bk, nb, st))) return -1;
+        return 0;
+    }
     case KERNIX_OP_AFFINE:
         return upload_f(&s->d_gamma, s->gamma, (size_t)s->in, st) || upload_f(&s->d_beta, s->beta, (size_t)s->in, st) ? -1 : 0;
     case KERNIX_OP_ADD_CONST:
@@ -244,6 +273,11 @@ static size_t step_scratch(const kx_graph* g, const kx_step* s, size_t* per_samp
     } else if (s->kind == KERNIX_OP_LINEAR && s->w.int8) {
         const size_t ldq = round_up((size_t)s->in, 16);
         *per_sample = (size_t)vi->r * (round_up(ldq, 16) + 4 * 4);
+    } else if (s->kind == KERNIX_OP_LSTM || s->kind == KERNIX_OP_GRU || s->kind == KERNIX_OP_RNN) {
+        /* input projections of all steps, two state buffers, the cell state, the second direction's output */
+        const size_t T = (size_t)vi->r, u = (size_t)s->out, gu = rnn_gates(s->kind) * u;
+        *per_sample = (T * gu + 3 * u + (s->dirs == 2 && s->merge != 0 ? (s->ret_seq ? T : 1) * u : 0)) * sizeof(float) +
+                      4 * KX_ALIGN;
     } else if (s->kind == KERNIX_OP_ATTENTION) {
         const kx_val* vv = &g->vals[s->inp[s->n_in > 1 ? 1 : 0]];
         const size_t hk = (size_t)s->heads * s->dk, hv = (size_t)s->heads * s->dv;
@@ -467,9 +501,40 @@ static int step_run(kernix_model* m, int i, int B) {
     }
     case KERNIX_OP_LSTM:
     case KERNIX_OP_GRU:
-    case KERNIX_OP_RNN:
-        fprintf(stderr, "forward: LSTM/GRU/RNN steps are not implemented on the B200 path\n");
-        return -1;
+    case KERNIX_OP_RNN: { /* kernix_rnn_run (:636-648): per direction, input projections of all steps in one GEMM,
+                           * then one fused kernel per time step */
+        const int kind = s->kind == KERNIX_OP_LSTM ? 0 : (s->kind == KERNIX_OP_GRU ? 1 : 2);
+        const int T = vi->r, u = s->out, gu = (int)rnn_gates(s->kind) * u;
+        const int concat = s->dirs == 2 && s->merge == 0;
+        const long uo = concat ? 2L * u : u;
+        float* zx = (float*)align_ptr(im->scratch);
+        float* h0 = (float*)align_ptr(zx + (size_t)rin * gu);
+        float* h1 = (float*)align_ptr(h0 + (size_t)B * u);
+        float* cst = (float*)align_ptr(h1 + (size_t)B * u);
+        float* bw = (float*)align_ptr(cst + (size_t)B * u);
+        for (int d = 0; d < s->dirs; d++) {
+            const kx_weight* W = d ? &s->wk : &s->w;
+            const kx_weight* U = d ? &s->wo : &s->wv;
+            const float* bias = d ? s->d_bk : s->d_bias;
+            float* dst = d == 0 ? y : (concat ? y + u : bw);
+            const long stride = d == 0 ? uo : (concat ? uo : u);
+            if (kx_gemm_f32(a, s->in, W->d_hi, W->d_lo, W->ldw, bias, zx, gu, (int)rin, gu, s->in, KERNIX_ACT_NONE, 0.0f,
+                            im->status, st) != 0)
+                return -1;
+            float *hp = h0, *hn = h1;
+            for (int step = 0; step < T; step++) {
+                const int t = d ? T - 1 - step : step;
+                if (kx_rnn_step(kind, zx, U->d_raw, kind == 1 ? bias + gu : NULL, hp, hn, cst, dst, stride, B, T, t, u, step == 0,
+                                s->ret_seq, step == T - 1, s->act, s->alpha, st) != 0)
+                    return -1;
+                float* tmp = hp;
+                hp = hn;
+                hn = tmp;
+            }
+        }
+        if (s->dirs == 2 && !concat) return kx_rnn_merge(y, bw, (long)B * (s->ret_seq ? T : 1) * u, s->merge, st);
+        return 0;
+    }
     default:
         return -1;
     }

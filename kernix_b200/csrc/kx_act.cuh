@@ -3,7 +3,7 @@
 // (include/kernix_model.h:468-517), which src/kernix_metal.m's bias_act kernel (:269-299) mirrors.
 // Products and sums use explicit round-to-nearest intrinsics so that the compiler cannot contract them
 // into fused multiply-adds; exp/tanh/expm1/log1p are CUDA's accurate library functions (max ~2 ulp), so
-// results agree with the CPU reference to a few ulp, not bit for bit.
+// results agree with the CPU reference to a few ulp, not bit for bit. GELU is the exception (see gelu_as).
 #pragma once
 #include <cmath>
 

@@ -51,7 +51,8 @@ typedef struct {
     int axis, start, len, squeeze;
     int bop;
     int heads, dk, dv, causal;
-    int seq, ret_seq, dirs, merge; /* LSTM / GRU / RNN (parsed; not executed on this path) */
+    int seq, ret_seq, dirs, merge; /* LSTM / GRU / RNN: weights w (input) and wv (recurrent) of the forward
+                                      * direction, wk and wo of the backward one; biases bias and bk */
     /* device */
     float *d_bias, *d_bk, *d_bv, *d_bo, *d_gamma, *d_beta, *d_cst;
     int qkv_fused;        /* ATTENTION with q = k = v: one GEMM with [Wq | Wk | Wv] */

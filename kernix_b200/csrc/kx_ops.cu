@@ -751,9 +751,122 @@ __global__ void k_unshard_cols(const float* __restrict__ src, int world, long ro
     }
 }
 
+// One time step of an LSTM / GRU / SimpleRNN direction (kernix_rnn_dir, include/kernix_model.h:560-634).
+// Block: RB sequences x TU hidden units; the RB previous states sit in shared memory, each thread accumulates
+// h . U for its unit in every gate (U is units x gates*units row-major, reads coalesced across the block), then
+// applies the gates in the reference's order with IEEE steps:
+//   LSTM (i, f, g, o): z = x.W + b + h.U; c = i*g + f*c (c = i*g at step 0); h = act(c)*o
+//   GRU (z, r, h~):    zh = b_rec + h.U (b_rec at step 0); z, r = sigmoid(x_z,r + zh_z,r);
+//                      h~ = act(r*zh_h + x_h); h = (h - h~)*z + h~ (h = -h~*z + h~ at step 0)
+//   RNN:               h = act(x.W + b + h.U)
+// zx holds x.W + b for all steps ((B*T) x gu). Writes h_next, c (LSTM), and the state at time t to
+// out + (b*T + t)*stride (ret_seq) or, at the last step, to out + b*stride.
+template <int KIND>  // 0 LSTM, 1 GRU, 2 RNN
+__global__ void k_rnn_step(const float* __restrict__ zx, const float* __restrict__ U, const float* __restrict__ brec,
+                           const float* __restrict__ hp, float* __restrict__ hn, float* __restrict__ c, float* __restrict__ out,
+                           long stride, int B, int T, int t, int u, int first, int ret_seq, int last, int act, float alpha,
+                           int RB) {
+    constexpr int G = KIND == 0 ? 4 : (KIND == 1 ? 3 : 1);
+    constexpr int RBM = 8;
+    extern __shared__ float hs[];  // RB x u
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int b0 = blockIdx.y * RB;
+    const int nb = min(RB, B - b0);
+    if (!first)
+        for (int i = threadIdx.x; i < nb * u; i += blockDim.x) hs[i] = hp[static_cast<long>(b0) * u + i];
+    __syncthreads();
+    if (j >= u) return;
+    const long gu = static_cast<long>(G) * u;
+    float acc[RBM][G];
+#pragma unroll
+    for (int r = 0; r < RBM; r++)
+#pragma unroll
+        for (int g = 0; g < G; g++) acc[r][g] = 0.0f;
+    if (!first)
+        for (int k = 0; k < u; k++) {
+            float w[G];
+#pragma unroll
+            for (int g = 0; g < G; g++) w[g] = __ldg(U + k * gu + g * u + j);
+#pragma unroll
+            for (int r = 0; r < RBM; r++) {
+                if (r >= nb) break;
+                const float hv = hs[r * u + k];
+#pragma unroll
+                for (int g = 0; g < G; g++) acc[r][g] = __fmaf_rn(hv, w[g], acc[r][g]);
+            }
+        }
+#pragma unroll
+    for (int r = 0; r < RBM; r++) {
+        if (r >= nb) break;
+        const int b = b0 + r;
+        const float* z = zx + (static_cast<long>(b) * T + t) * gu;
+        float h;
+        if (KIND == 0) {
+            float zg[4];
+#pragma unroll
+            for (int g = 0; g < 4; g++) zg[g] = first ? z[g * u + j] : __fadd_rn(z[g * u + j], acc[r][g]);
+            const float ig = kx::act_apply(kx::ACT_SIGMOID, zg[0], 0.0f), fg = kx::act_apply(kx::ACT_SIGMOID, zg[1], 0.0f);
+            const float gg = kx::act_apply(act, zg[2], alpha), og = kx::act_apply(kx::ACT_SIGMOID, zg[3], 0.0f);
+            float* cb = c + static_cast<long>(b) * u + j;
+            const float cn = first ? __fmul_rn(ig, gg) : __fadd_rn(__fmul_rn(ig, gg), __fmul_rn(fg, *cb));
+            *cb = cn;
+            h = __fmul_rn(kx::act_apply(act, cn, alpha), og);
+        } else if (KIND == 1) {
+            float zh[3];
+#pragma unroll
+            for (int g = 0; g < 3; g++) zh[g] = first ? brec[g * u + j] : __fadd_rn(acc[r][g], brec[g * u + j]);
+            const float zgt = kx::act_apply(kx::ACT_SIGMOID, __fadd_rn(z[j], zh[0]), 0.0f);
+            const float rgt = kx::act_apply(kx::ACT_SIGMOID, __fadd_rn(z[u + j], zh[1]), 0.0f);
+            const float hh = kx::act_apply(act, __fadd_rn(__fmul_rn(rgt, zh[2]), z[2 * u + j]), alpha);
+            const float d = first ? -hh : __fsub_rn(hs[r * u + j], hh);
+            h = __fadd_rn(__fmul_rn(d, zgt), hh);
+        } else {
+            h = kx::act_apply(act, first ? z[j] : __fadd_rn(z[j], acc[r][0]), alpha);
+        }
+        hn[static_cast<long>(b) * u + j] = h;
+        if (ret_seq) out[(static_cast<long>(b) * T + t) * stride + j] = h;
+        else if (last) out[static_cast<long>(b) * stride + j] = h;
+    }
+}
+
+// Elementwise merge of two directions (kernix_rnn_run :641-646): y = y * bw, y + bw, or (y + bw) * 0.5.
+__global__ void k_rnn_merge(float* __restrict__ y, const float* __restrict__ bw, long n, int merge) {
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const float a = y[i], b = bw[i];
+        y[i] = merge == 2 ? __fmul_rn(a, b) : (merge == 3 ? __fmul_rn(__fadd_rn(a, b), 0.5f) : __fadd_rn(a, b));
+    }
+}
+
 }  // namespace
 
 extern "C" {
+
+int kx_rnn_step(int kind, const float* zx, const float* U, const float* brec, const float* h_prev, float* h_next, float* c,
+                float* out, long stride, int B, int T, int t, int u, int first, int ret_seq, int last, int act, float alpha,
+                void* stream) {
+    if (B <= 0) return 0;
+    if (u <= 0 || T <= 0 || t < 0 || t >= T || kind < 0 || kind > 2 || (kind == 1 && brec == nullptr) || (kind == 0 && c == nullptr))
+        return -1;
+    int RB = 8;
+    while (RB > 1 && static_cast<long>(RB) * u * 4 > 48 * 1024) RB >>= 1;
+    if (static_cast<long>(u) * 4 > 48 * 1024) return -1;  // one state row must fit the block's shared memory
+    const int TU = u >= 128 ? 128 : (u + 31) / 32 * 32;
+    dim3 grid((u + TU - 1) / TU, (B + RB - 1) / RB);
+    const size_t smem = static_cast<size_t>(RB) * u * sizeof(float);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (kind == 0) k_rnn_step<0><<<grid, TU, smem, st>>>(zx, U, brec, h_prev, h_next, c, out, stride, B, T, t, u, first, ret_seq, last, act, alpha, RB);
+    else if (kind == 1) k_rnn_step<1><<<grid, TU, smem, st>>>(zx, U, brec, h_prev, h_next, c, out, stride, B, T, t, u, first, ret_seq, last, act, alpha, RB);
+    else k_rnn_step<2><<<grid, TU, smem, st>>>(zx, U, brec, h_prev, h_next, c, out, stride, B, T, t, u, first, ret_seq, last, act, alpha, RB);
+    return launch_ok();
+}
+
+int kx_rnn_merge(float* y, const float* bw, long n, int merge, void* stream) {
+    if (n <= 0) return 0;
+    if (merge < 1 || merge > 3) return -1;
+    k_rnn_merge<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(y, bw, n, merge);
+    return launch_ok();
+}
+
 
 int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y, int ldy, void* stream) {
     if (rows <= 0 || world <= 0 || slice <= 0) return 0;

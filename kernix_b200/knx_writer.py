@@ -169,6 +169,22 @@ class Graph:
         s0[ax] = sum(self.shape(v)[ax] for v in xs)
         return self._add("CONCAT", xs, [axis], [], s0)
 
+    def rnn(self, x, kind, units, weights, act="tanh", ret_seq=False, merge="concat"):
+        """LSTM / GRU / RNN over the sequence axis of x (T x in). weights: one (W in x gu, U units x gu, bias) per
+        direction (two = bidirectional), gu = gates * units with gates 4 (LSTM: i, f, g, o), 3 (GRU: z, r, h~)
+        or 1; bias has gu values (GRU: 2 * gu, input then recurrent). merge of two directions: concat, sum, mul,
+        ave. In int8 mode the recurrent weights are written I8_COL (kept int8) and the input weights I8_COL too
+        (dequantised at load)."""
+        T, cin = self.shape(x)[-2], self.shape(x)[-1]
+        dirs = len(weights)
+        mg = dict(concat=0, sum=1, mul=2, ave=3)[merge]
+        blobs = []
+        for w, u, b in weights:
+            blobs += [("w", w, "i8_col"), ("w", u, "i8_col"), ("f", b)]
+        uo = 2 * units if dirs == 2 and mg == 0 else units
+        return self._add(kind.upper(), [x], [cin, units, ACT[act], int(ret_seq), dirs, mg], blobs,
+                         (T, uo) if ret_seq else (uo,))
+
     def embedding(self, x, table):
         return self._add("EMBEDDING", [x], [table.shape[0], table.shape[1]], [("w", table, "i8_row")],
                          self.shape(x) + (table.shape[1],))

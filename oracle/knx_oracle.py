@@ -20,7 +20,7 @@ What it restates (file:line in the KERNIX reference, include/kernix_model.h unle
 
 Float32 sums (sgemm, softmax/LN sums) follow numpy's/OpenBLAS's summation order, so agreement with the
 reference is to rounding (tests pin it at 1e-5 relative); integer work (int8 quantisation and
-accumulators) is bit-exact. LSTM/GRU/RNN records are parsed but not executed (outside the GPU path).
+accumulators) is bit-exact. LSTM/GRU/RNN steps follow kernix_rnn_dir / kernix_rnn_run (:560-648).
 """
 import struct
 
@@ -142,10 +142,7 @@ def _parse_op(r, ver, kind):
         g = {OP["LSTM"]: 4, OP["GRU"]: 3, OP["RNN"]: 1}[kind]
         gu = g * a[1]
         nb = 2 * gu if kind == OP["GRU"] else gu
-        for _ in range(dirs):
-            _weight(r, ver, a[0], gu, False)
-            _weight(r, ver, a[1], gu, True)
-            r.f32(nb)
+        s["rnn"] = [(_weight(r, ver, a[0], gu, False), _weight(r, ver, a[1], gu, True), r.f32(nb)) for _ in range(dirs)]
         s.update(inp_c=a[0], out=a[1], act=a[2], ret_seq=a[3], dirs=dirs, merge=merge, seq=seq)
     elif kind == OP["CONV"]:
         a = r.u32(14)
@@ -686,6 +683,84 @@ def attention(s, q2, vq, k2, v2, vv):
     return dense(ctx, _wf(s["wo"]), s["bo"], ACT_NONE, 0)
 
 
+INT8_MAX_ROWS = 2  # KERNIX_INT8_MAX_ROWS (:50)
+MERGE_CONCAT, MERGE_SUM, MERGE_MUL, MERGE_AVE = 0, 1, 2, 3  # KERNIX_MERGE_* (:35)
+ACT_SIGMOID = ACT_NAMES.index("sigmoid")
+
+
+def rnn_dir(s, d, x, B, T):
+    """kernix_rnn_dir (:560-634): one direction of an LSTM / GRU / SimpleRNN over B sequences of T rows (x is
+    (B*T) x in). The input projection x.W + b is one dense for all steps; each step adds h.U (sgemm with beta = 1,
+    or kernix_qmatmul when U is int8 and B <= 2) and applies the gates in the reference's operation order:
+    LSTM (i, f, g, o): c = i*g + f*c (c = i*g at step 0), h = act(c)*o; GRU (z, r, h~, recurrent bias after the
+    reset gate): h~ = act(x_h + r*(h.U_h + b_h)), h = (h - h~)*z + h~; RNN: h = act(x.W + b + h.U).
+    The backward direction reads t = T-1 .. 0 and writes each state at its own time position. Returns
+    (B, T, u) states when ret_seq, else (B, u) final states."""
+    kind, u, a, alpha = s["kind"], s["out"], s["act"], F32(s["alpha"])
+    g = {OP["LSTM"]: 4, OP["GRU"]: 3, OP["RNN"]: 1}[kind]
+    gu = g * u
+    Ww, Uw, bias = s["rnn"][d]
+    gru = kind == OP["GRU"]
+    brec = bias[gu:2 * gu] if gru else None
+    zx = dense(x, _wf(Ww), bias[:gu], ACT_NONE, 0.0).reshape(B, T, gu)
+    h = np.zeros((B, u), F32)
+    c = np.zeros((B, u), F32)
+    out = np.zeros((B, T, u), F32) if s["ret_seq"] else None
+    q8 = Uw[0] == "i8"
+    with np.errstate(all="ignore"):
+        for step in range(T):
+            t = T - 1 - step if d else step
+            z = zx[:, t, :].copy()
+            zh = None
+            if step == 0:
+                if gru:
+                    zh = np.broadcast_to(brec, (B, gu)).astype(F32)
+            elif q8 and B <= INT8_MAX_ROWS:
+                v = qlinear(h, Uw[1], Uw[2], brec)
+                if gru:
+                    zh = v
+                else:
+                    z = (z + v).astype(F32)
+            else:
+                hu = np.matmul(h, _wf(Uw)).astype(F32)
+                if gru:
+                    zh = (hu + brec[None, :]).astype(F32)
+                else:
+                    z = (z + hu).astype(F32)
+            if kind == OP["LSTM"]:
+                i_ = act(z[:, 0:u], ACT_SIGMOID, 0.0)
+                f_ = act(z[:, u:2 * u], ACT_SIGMOID, 0.0)
+                g_ = act(z[:, 2 * u:3 * u], a, alpha)
+                o_ = act(z[:, 3 * u:4 * u], ACT_SIGMOID, 0.0)
+                c = (i_ * g_).astype(F32) if step == 0 else ((i_ * g_).astype(F32) + (f_ * c).astype(F32)).astype(F32)
+                h = (act(c, a, alpha) * o_).astype(F32)
+            elif gru:
+                zr = act((z[:, :2 * u] + zh[:, :2 * u]).astype(F32), ACT_SIGMOID, 0.0)
+                hh = act(((zr[:, u:] * zh[:, 2 * u:]).astype(F32) + z[:, 2 * u:]).astype(F32), a, alpha)
+                dh = -hh if step == 0 else (h - hh).astype(F32)
+                h = ((dh * zr[:, :u]).astype(F32) + hh).astype(F32)
+            else:
+                h = act(z, a, alpha)
+            if out is not None:
+                out[:, t] = h
+    return out if out is not None else h
+
+
+def rnn(s, x, B, T):
+    """kernix_rnn_run (:636-648): one or two directions; two are concatenated per position or merged
+    elementwise (sum, product, average = (fw + bw) * 0.5)."""
+    fw = rnn_dir(s, 0, x, B, T)
+    if s["dirs"] == 1:
+        return fw
+    bw = rnn_dir(s, 1, x, B, T)
+    if s["merge"] == MERGE_CONCAT:
+        return np.concatenate([fw, bw], axis=-1)
+    if s["merge"] == MERGE_MUL:
+        return (fw * bw).astype(F32)
+    y = (fw + bw).astype(F32)
+    return (y * F32(0.5)).astype(F32) if s["merge"] == MERGE_AVE else y
+
+
 def forward(model, x, trace=None):
     """kernix_model_forward on (rows, in_dim) float32, rows a multiple of seq_len. Returns (B, out_dim).
     trace: optional list that receives every value (index = original value id, (B*r) x c arrays)."""
@@ -755,6 +830,8 @@ def forward(model, x, trace=None):
             y = np.zeros((B, Ho, Wo, vi["c"]), F32)
             y[:, s["pt"]:s["pt"] + H, s["pl"]:s["pl"] + W] = xx
             y = y.reshape(-1, vo["c"])
+        elif k in (OP["LSTM"], OP["GRU"], OP["RNN"]):
+            y = rnn(s, a, B, vi["r"])
         elif k == OP["UPSAMPLE"]:
             H, W = _hw(vi)
             Ho, Wo = _hw(vo)

@@ -6,7 +6,8 @@
   * the reference's int8 known answers (test/model_test.c:363-446): LCG-generated cases, NaN and zero rows, the int32
     overflow edge -- oracle == a scalar int64 restatement of the test's ref_qmatmul, and == the compiled reference's
     kernix_qmatmul bit for bit when oracle/_ref is built;
-  * the five benchmark configurations, when the compiled reference is present."""
+  * the five benchmark configurations, and LSTM / GRU / SimpleRNN steps in every direction, merge and output mode
+    with float and int8 recurrent weights, when the compiled reference is present."""
 import os
 
 import numpy as np
@@ -17,7 +18,7 @@ from oracle import knx_oracle as ko
 from oracle import ref_lib
 
 GOLD = os.path.join(ROOT, "tests", "golden")
-FIXTURES = ["small", "wide", "inplace_first", "small_int8", "q8_s", "cnn_s", "tfm_s", "g_cnn", "g_attn"]
+FIXTURES = ["small", "wide", "inplace_first", "small_int8", "q8_s", "cnn_s", "tfm_s", "g_cnn", "g_attn", "g_rnn"]
 INT8 = {"small_int8", "q8_s"}
 
 
@@ -104,3 +105,33 @@ def test_oracle_matches_reference_on_configs(cfg, batch, tmp_path):
         m.set_workspace_limit(1)
     x = configs.inputs(cfg, batch)
     assert rel_err(ko.forward(ko.load(p), x), m.forward(x)) <= (1e-4 if cfg == "c2" else 1e-5)
+
+
+def rnn_model(path, kind, T, cin, u, dirs, merge, ret_seq, act, int8, rng):
+    from kernix_b200 import knx_writer
+    g = {"lstm": 4, "gru": 3, "rnn": 1}[kind]
+    gu = g * u
+    G = knx_writer.Graph((T, cin), int8=int8)
+    ws = [(rng.normal(0, 0.4, (cin, gu)).astype(np.float32), rng.normal(0, 0.4, (u, gu)).astype(np.float32),
+           rng.normal(0, 0.3, 2 * gu if kind == "gru" else gu).astype(np.float32)) for _ in range(dirs)]
+    G.rnn(0, kind, u, ws, act=act, ret_seq=ret_seq, merge=merge)
+    G.write(path)
+
+
+@pytest.mark.reference
+@pytest.mark.skipif(not ref_lib.available(), reason="compiled reference (oracle/_ref) not built here")
+@pytest.mark.parametrize("kind", ["lstm", "gru", "rnn"])
+@pytest.mark.parametrize("dirs,merge", [(1, "concat"), (2, "concat"), (2, "sum"), (2, "mul"), (2, "ave")])
+def test_oracle_rnn_matches_reference(kind, dirs, merge, tmp_path):
+    """kernix_rnn_dir / kernix_rnn_run (include/kernix_model.h:560-648): every output mode, float recurrent weights,
+    and int8 ones both below (the reference's int8 kernel, B <= 2) and above its row threshold."""
+    rng = np.random.default_rng(len(kind) * 10 + dirs)
+    for ret_seq in (0, 1):
+        for int8, B in ((False, 5), (True, 2), (True, 4)):
+            p = str(tmp_path / f"{kind}_{ret_seq}_{int8}.knx")
+            rnn_model(p, kind, 7, 5, 6, dirs, merge, ret_seq, "relu" if kind == "rnn" else "tanh", int8, rng)
+            x = rng.standard_normal((B * 7, 5)).astype(np.float32)
+            r = ref_lib.RefModel(p)
+            want = r.forward(x)
+            r.close()
+            assert rel_err(ko.forward(ko.load(p), x), want) <= 1e-6, (ret_seq, int8, B)
