@@ -510,7 +510,8 @@ def run_c5_rows(args):
             "e2e": {"value": B * args.steps / t_e2e, "unit": "samples/s", "h2d_bytes_per_step": B * 8192 * 4,
                     "d2h_bytes_per_step": B * 8192 * 4, "api": "kernix_capi_forward, page-locked host buffers"},
             "achieved_tflops": flops * args.steps / t / 1e12,
-            "weight_stream_gbs_per_gpu": 2 * 2.147e9 / world * args.steps / t / 1e9,
+            # weight bytes streamed per step per GPU: the fp32 copy on the skinny path (<= 16 rows), else tf32 hi + lo
+            "weight_stream_gbs_per_gpu": (1 if B <= 16 else 2) * 2.147e9 / world * args.steps / t / 1e9,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

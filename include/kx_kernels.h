@@ -159,6 +159,15 @@ KERNIX_API int kx_rnn_step(int kind, const float* zx, const float* U, const floa
 /* Merge of a bidirectional RNN's directions in place (kernix_rnn_run :641-646): merge 1 sum, 2 product, 3 average. */
 KERNIX_API int kx_rnn_merge(float* y, const float* bw, long n, int merge, void* stream);
 
+/* Dense layer for at most KX_SKINNY_MAX_ROWS rows (weight streaming) on the CUDA cores in fp32:
+ * y = act(x . W + bias) with W the k x n row-major fp32 weight as in the file; K is split into kx_skinny_slices(n, k)
+ * slices whose partial sums (part: slices x m x n floats) are added in slice order. (Extension; the reference runs
+ * every dense layer through one sgemm.) */
+#define KX_SKINNY_MAX_ROWS 16
+KERNIX_API int kx_skinny_slices(int n, int k);
+KERNIX_API int kx_gemm_f32_skinny(const float* x, int ldx, const float* w, const float* bias, float* y, int ldy, int m, int n,
+                                  int k, int act, float alpha, float* part, size_t part_floats, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,8 @@ struct kx_model_impl {
     float* xin;           /* device input rows */
     uint8_t* scratch;     /* per-step scratch: int8 activations, attention Q/K/V/context */
     int* status;          /* device status word of bounded waits */
+    float* skinny_part;   /* partial sums of the skinny dense path (LINEAR steps of <= KX_SKINNY_MAX_ROWS rows) */
+    size_t skinny_floats;
     int* status_h;        /* pinned host copy */
     size_t scratch_per_row_max;
     /* output-column sharding (kernix_model_load_sharded) */
@@ -100,8 +102,9 @@ static int upload_f(float** dst, const float* src, size_t n, cudaStream_t st) {
     return upload((void**)dst, src, n * sizeof(float), st);
 }
 
-/* float weight k x n -> tf32 split planes n x ldw at rows [row0, row0+n) of (hi, lo) */
-static int prep_f32_into(const kx_weight* w, float* hi, float* lo, int ldw, size_t row0, cudaStream_t st) {
+/* float weight k x n -> tf32 split planes n x ldw at rows [row0, row0+n) of (hi, lo); the uploaded k x n copy is
+ * kept in *keep_raw when given (the skinny dense path streams it), freed otherwise */
+static int prep_f32_into(const kx_weight* w, float* hi, float* lo, int ldw, size_t row0, cudaStream_t st, float** keep_raw) {
     float* raw = NULL;
     if (upload((void**)&raw, w->f, (size_t)w->k * w->n * sizeof(float), st) != 0) {
         cudaFree(raw);
@@ -109,7 +112,8 @@ static int prep_f32_into(const kx_weight* w, float* hi, float* lo, int ldw, size
     }
     int rc = kx_prep_f32_weight(raw, w->k, w->n, hi + row0 * (size_t)ldw, lo + row0 * (size_t)ldw, ldw, st);
     if (cudaStreamSynchronize(st) != cudaSuccess) rc = -1;
-    cudaFree(raw);
+    if (keep_raw) *keep_raw = raw;
+    else cudaFree(raw);
     return rc;
 }
 
@@ -124,15 +128,15 @@ static int prep_f32_cols(kx_weight* w, int c0, int n, cudaStream_t st) {
                                (size_t)w->k, cudaMemcpyHostToDevice, st) == cudaSuccess ? 0 : -1;
     if (rc == 0) rc = kx_prep_f32_weight(raw, w->k, n, w->d_hi, w->d_lo, w->ldw, st);
     if (cudaStreamSynchronize(st) != cudaSuccess) rc = -1;
-    cudaFree(raw);
+    w->d_raw = raw; /* k x n fp32, kept for the skinny dense path */
     return rc;
 }
 
-static int prep_f32(kx_weight* w, cudaStream_t st) {
+static int prep_f32(kx_weight* w, cudaStream_t st, int keep_raw) {
     w->ldw = (int)round_up((size_t)w->k, 32);
     const size_t bytes = (size_t)w->n * w->ldw * sizeof(float);
     if (cudaMalloc((void**)&w->d_hi, bytes) != cudaSuccess || cudaMalloc((void**)&w->d_lo, bytes) != cudaSuccess) return -1;
-    return prep_f32_into(w, w->d_hi, w->d_lo, w->ldw, 0, st);
+    return prep_f32_into(w, w->d_hi, w->d_lo, w->ldw, 0, st, keep_raw ? &w->d_raw : NULL);
 }
 
 static int prep_i8(kx_weight* w, cudaStream_t st) {
@@ -194,12 +198,12 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
             if (prep_f32_cols(&s->w, s->shard_c0, s->shard_n, st)) return -1;
             return upload_f(&s->d_bias, s->bias ? s->bias + s->shard_c0 : NULL, (size_t)s->shard_n, st);
         }
-        if (s->w.int8 ? prep_i8(&s->w, st) : prep_f32(&s->w, st)) return -1;
+        if (s->w.int8 ? prep_i8(&s->w, st) : prep_f32(&s->w, st, 1)) return -1;
         return upload_f(&s->d_bias, s->bias, (size_t)s->out, st);
     case KERNIX_OP_CONV:
         if (conv_depthwise(s)) {
             if (upload_f(&s->w.d_raw, s->w.f, (size_t)s->w.k * s->w.n, st) != 0) return -1;
-        } else if (prep_f32(&s->w, st) != 0) {
+        } else if (prep_f32(&s->w, st, 0) != 0) {
             return -1;
         }
         return upload_f(&s->d_bias, s->bias, (size_t)s->out, st);
@@ -209,8 +213,8 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
     case KERNIX_OP_GRU:
     case KERNIX_OP_RNN: {
         const size_t gu = rnn_gates(s->kind) * (size_t)s->out, nb = s->kind == KERNIX_OP_GRU ? 2 * gu : gu;
-        if (prep_f32(&s->w, st) || upload_raw_f32(&s->wv, st) || upload_f(&s->d_bias, s->bias, nb, st)) return -1;
-        if (s->dirs == 2 && (prep_f32(&s->wk, st) || upload_raw_f32(&s->wo, st) || upload_f(&s->d_bk, s->bk, nb, st))) return -1;
+        if (prep_f32(&s->w, st, 0) || upload_raw_f32(&s->wv, st) || upload_f(&s->d_bias, s->bias, nb, st)) return -1;
+        if (s->dirs == 2 && (prep_f32(&s->wk, st, 0) || upload_raw_f32(&s->wo, st) || upload_f(&s->d_bk, s->bk, nb, st))) return -1;
         return 0;
     }
     case KERNIX_OP_AFFINE:
@@ -230,8 +234,8 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
             const size_t bytes = (size_t)f->n * f->ldw * sizeof(float);
             if (cudaMalloc((void**)&f->d_hi, bytes) != cudaSuccess || cudaMalloc((void**)&f->d_lo, bytes) != cudaSuccess)
                 return -1;
-            if (prep_f32_into(&s->w, f->d_hi, f->d_lo, f->ldw, 0, st) || prep_f32_into(&s->wk, f->d_hi, f->d_lo, f->ldw, hk, st) ||
-                prep_f32_into(&s->wv, f->d_hi, f->d_lo, f->ldw, 2 * hk, st))
+            if (prep_f32_into(&s->w, f->d_hi, f->d_lo, f->ldw, 0, st, NULL) || prep_f32_into(&s->wk, f->d_hi, f->d_lo, f->ldw, hk, st, NULL) ||
+                prep_f32_into(&s->wv, f->d_hi, f->d_lo, f->ldw, 2 * hk, st, NULL))
                 return -1;
             if (s->bias) {
                 if (cudaMalloc((void**)&s->d_bqkv, (2 * hk + hv) * sizeof(float)) != cudaSuccess) return -1;
@@ -241,10 +245,10 @@ static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
                     return -1;
             }
         } else {
-            if (prep_f32(&s->w, st) || prep_f32(&s->wk, st) || prep_f32(&s->wv, st)) return -1;
+            if (prep_f32(&s->w, st, 0) || prep_f32(&s->wk, st, 0) || prep_f32(&s->wv, st, 0)) return -1;
             if (upload_f(&s->d_bias, s->bias, hk, st) || upload_f(&s->d_bk, s->bk, hk, st) || upload_f(&s->d_bv, s->bv, hv, st)) return -1;
         }
-        if (prep_f32(&s->wo, st) != 0) return -1;
+        if (prep_f32(&s->wo, st, 0) != 0) return -1;
         return upload_f(&s->d_bo, s->bo, (size_t)s->out, st);
     }
     default:
@@ -385,11 +389,14 @@ static int step_run(kernix_model* m, int i, int B) {
             return kx_gemm_i8(xq, ldq, sx, s->w.d_q, s->w.ldw, s->w.d_scale, s->d_bias, y, s->out, (int)rin, s->out, s->in,
                               s->act, s->alpha, im->status, st);
         }
+        const int skinny = rin <= KX_SKINNY_MAX_ROWS && s->w.d_raw != NULL && im->skinny_part != NULL;
         if (s->shard_n > 0) { /* this rank's columns, all-gather across ranks, re-interleave into full rows */
             float* yl = (float*)align_ptr(im->scratch);
             float* yg = (float*)align_ptr(yl + (size_t)rin * s->shard_n);
-            if (kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, yl, s->shard_n, (int)rin, s->shard_n, s->in,
-                            s->act, s->alpha, im->status, st) != 0)
+            if ((skinny ? kx_gemm_f32_skinny(a, s->in, s->w.d_raw, s->d_bias, yl, s->shard_n, (int)rin, s->shard_n, s->in, s->act,
+                                             s->alpha, im->skinny_part, im->skinny_floats, st)
+                        : kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, yl, s->shard_n, (int)rin, s->shard_n,
+                                      s->in, s->act, s->alpha, im->status, st)) != 0)
                 return -1;
             if (im->gather(im->gather_ctx, yl, yg, (size_t)rin * s->shard_n, st) != 0) {
                 fprintf(stderr, "forward: the all-gather of step %d failed\n", i);
@@ -397,6 +404,9 @@ static int step_run(kernix_model* m, int i, int B) {
             }
             return kx_unshard_cols(yg, im->world, rin, s->shard_n, y, s->out, st);
         }
+        if (skinny) /* few rows: stream the fp32 weights on the CUDA cores, K split over the SMs */
+            return kx_gemm_f32_skinny(a, s->in, s->w.d_raw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act, s->alpha,
+                                      im->skinny_part, im->skinny_floats, st);
         return kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act,
                            s->alpha, im->status, st);
     case KERNIX_OP_ACT:
@@ -793,6 +803,18 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
     for (int i = 0; why == NULL && i < g->n_steps; i++)
         if (step_upload(g, &g->steps[i], im->stream) != 0) why = "cannot copy the weights to the GPU";
     if (why == NULL && cudaStreamSynchronize(im->stream) != cudaSuccess) why = "cannot copy the weights to the GPU";
+    if (why == NULL) { /* partial sums of the skinny dense path: slices x KX_SKINNY_MAX_ROWS x columns, the largest step */
+        size_t mx = 0;
+        for (int i = 0; i < g->n_steps; i++) {
+            const kx_step* s = &g->steps[i];
+            if (s->kind != KERNIX_OP_LINEAR || s->w.int8) continue;
+            const int n = s->shard_n > 0 ? s->shard_n : s->out;
+            const size_t f = (size_t)kx_skinny_slices(n, s->in) * KX_SKINNY_MAX_ROWS * n;
+            if (f > mx) mx = f;
+        }
+        if (mx > 0 && cudaMalloc((void**)&im->skinny_part, mx * sizeof(float)) != cudaSuccess) why = "cannot allocate device memory";
+        im->skinny_floats = mx;
+    }
     if (prev >= 0 && prev != im->device) cudaSetDevice(prev);
     if (why != NULL) {
         fprintf(stderr, "model load failed (%s): %s (%s)\n", path, why, cudaGetErrorString(cudaGetLastError()));
@@ -834,6 +856,7 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
         if (im->g != NULL)
             for (int i = 0; i < im->g->n_steps; i++) step_dev_free(&im->g->steps[i]);
         if (im->status_h) cudaFreeHost(im->status_h);
+        cudaFree(im->skinny_part);
         for (int i = 0; i < KX_PIPE_MAX; i++) {
             cudaEvent_t* evs[6] = {im->ev_is, im->ev_in, im->ev_cs, im->ev_comp, im->ev_os, im->ev_out};
             for (int k = 0; k < 6; k++)

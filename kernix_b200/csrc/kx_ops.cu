@@ -837,9 +837,121 @@ __global__ void k_rnn_merge(float* __restrict__ y, const float* __restrict__ bw,
     }
 }
 
+// Skinny dense layer (M <= 16 rows) on the CUDA cores, for weight streaming: fp32 W k x n row-major as in the
+// file. Block = 256 threads x CPT consecutive columns each (16-, 8- or 4-byte loads of W, coalesced across the
+// block) over one K slice; the slice of the M input rows is staged in shared memory in pieces of 256 K; each thread
+// keeps MT x CPT (<= 32) fp32 fma accumulators and eight K steps of W loads in flight. Partial sums
+// [slice][row][column] are reduced in slice order by k_skinny_reduce, which adds the bias and applies the
+// activation (act(x.W + b), as the reference's sgemm then bias_act).
+constexpr int SK_THREADS = 256, SK_KC = 256;
+template <int CPT> struct SkVec;
+template <> struct SkVec<4> { using T = float4; };
+template <> struct SkVec<2> { using T = float2; };
+template <> struct SkVec<1> { using T = float; };
+template <int CPT>
+__device__ __forceinline__ void sk_unpack(const typename SkVec<CPT>::T& v, float (&o)[CPT]) {
+    if constexpr (CPT == 4) { o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w; }
+    else if constexpr (CPT == 2) { o[0] = v.x; o[1] = v.y; }
+    else { o[0] = v; }
+}
+
+template <int MT, int CPT>
+__global__ void __launch_bounds__(SK_THREADS, 2) k_skinny(const float* __restrict__ x, int ldx, const float* __restrict__ w,
+                                                         int n, float* __restrict__ part, int M, int K, int kslice) {
+    using V = typename SkVec<CPT>::T;
+    __shared__ float xs[MT][SK_KC];
+    const int col = (blockIdx.x * SK_THREADS + threadIdx.x) * CPT;
+    const int k0 = blockIdx.y * kslice, k1 = min(K, k0 + kslice);
+    float acc[MT][CPT];
+#pragma unroll
+    for (int m = 0; m < MT; m++)
+#pragma unroll
+        for (int c = 0; c < CPT; c++) acc[m][c] = 0.0f;
+    for (int kc = k0; kc < k1; kc += SK_KC) {
+        const int nk = min(SK_KC, k1 - kc);
+        __syncthreads();
+        for (int i = threadIdx.x; i < MT * SK_KC; i += SK_THREADS) {
+            const int m = i / SK_KC, kk = i - m * SK_KC;
+            xs[m][kk] = (m < M && kk < nk) ? x[static_cast<long>(m) * ldx + kc + kk] : 0.0f;
+        }
+        __syncthreads();
+        if (col < n) {
+            const float* wp = w + static_cast<long>(kc) * n + col;
+#pragma unroll 8
+            for (int kk = 0; kk < nk; kk++) {
+                float wv[CPT];
+                sk_unpack<CPT>(__ldg(reinterpret_cast<const V*>(wp + static_cast<long>(kk) * n)), wv);
+#pragma unroll
+                for (int m = 0; m < MT; m++)
+#pragma unroll
+                    for (int c = 0; c < CPT; c++) acc[m][c] = __fmaf_rn(xs[m][kk], wv[c], acc[m][c]);
+            }
+        }
+    }
+    if (col < n) {
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (m >= M) break;
+#pragma unroll
+            for (int c = 0; c < CPT; c++) part[(static_cast<long>(blockIdx.y) * M + m) * n + col + c] = acc[m][c];
+        }
+    }
+}
+
+__global__ void k_skinny_reduce(const float* __restrict__ part, int S, int M, int n, const float* __restrict__ bias,
+                                float* __restrict__ y, int ldy, int act, float alpha) {
+    const long total = static_cast<long>(M) * n;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const int m = static_cast<int>(i / n), c = static_cast<int>(i - static_cast<long>(m) * n);
+        float v = part[i];
+        for (int sl = 1; sl < S; sl++) v = __fadd_rn(v, part[static_cast<long>(sl) * total + i]);
+        if (bias) v = __fadd_rn(v, bias[c]);
+        y[static_cast<long>(m) * ldy + c] = kx::act_apply(act, v, alpha);
+    }
+}
+
 }  // namespace
 
 extern "C" {
+
+// columns per thread of the skinny kernel for m rows and n columns (m * CPT accumulators <= 32; n divisible)
+static int sk_cpt(int m, int n) {
+    const int c = m <= 8 ? 4 : 2;
+    return n % c == 0 ? c : 1;
+}
+
+int kx_skinny_slices(int n, int k) {
+    const int nblk = (n + 4 * SK_THREADS - 1) / (4 * SK_THREADS);  // column blocks at four columns per thread (the fewest)
+    int S = (2 * 148 + nblk - 1) / nblk;  // about two blocks per SM
+    const int smax = (k + SK_KC - 1) / SK_KC;
+    if (S > smax) S = smax;
+    return S < 1 ? 1 : S;
+}
+
+int kx_gemm_f32_skinny(const float* x, int ldx, const float* w, const float* bias, float* y, int ldy, int m, int n, int k, int act,
+                       float alpha, float* part, size_t part_floats, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (m > KX_SKINNY_MAX_ROWS || k <= 0 || ldx < k || ldy < n || part == nullptr) return -1;
+    if (reinterpret_cast<uintptr_t>(w) & 15) return -1;
+    const int S = kx_skinny_slices(n, k);
+    if (static_cast<size_t>(S) * m * n > part_floats) return -1;
+    const int cpt = sk_cpt(m, n);
+    const int kslice = ((k + S - 1) / S + SK_KC - 1) / SK_KC * SK_KC;
+    const int S_used = (k + kslice - 1) / kslice;
+    dim3 grid((n + SK_THREADS * cpt - 1) / (SK_THREADS * cpt), S_used);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (m <= 8) {
+        if (cpt == 4) k_skinny<8, 4><<<grid, SK_THREADS, 0, st>>>(x, ldx, w, n, part, m, k, kslice);
+        else k_skinny<8, 1><<<grid, SK_THREADS, 0, st>>>(x, ldx, w, n, part, m, k, kslice);
+    } else {
+        if (cpt == 2) k_skinny<16, 2><<<grid, SK_THREADS, 0, st>>>(x, ldx, w, n, part, m, k, kslice);
+        else k_skinny<16, 1><<<grid, SK_THREADS, 0, st>>>(x, ldx, w, n, part, m, k, kslice);
+    }
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    k_skinny_reduce<<<grid_for(static_cast<long>(m) * n, 256), 256, 0, st>>>(part, S_used, m, n, bias, y, ldy, act, alpha);
+    return launch_ok();
+}
+
 
 int kx_rnn_step(int kind, const float* zx, const float* U, const float* brec, const float* h_prev, float* h_next, float* c,
                 float* out, long stride, int B, int T, int t, int u, int first, int ret_seq, int last, int act, float alpha,

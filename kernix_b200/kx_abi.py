@@ -36,6 +36,8 @@ SIGNATURES = {
     "kx_unshard_cols": [_vp, _i, _l, _i, _vp, _i, _vp],
     "kx_rnn_step": [_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _l, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp],
     "kx_rnn_merge": [_vp, _vp, _l, _i, _vp],
+    "kx_skinny_slices": [_i, _i],
+    "kx_gemm_f32_skinny": [_vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp],
     "kx_knx_plan": [ctypes.c_char_p, ctypes.POINTER(_i), ctypes.POINTER(_i), _i],
     "kx_knx_inspect": [ctypes.c_char_p, ctypes.POINTER(_l), ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i), _i,
                        ctypes.c_char_p, _i],

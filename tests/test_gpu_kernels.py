@@ -227,6 +227,28 @@ def test_gemm_f32_3xtf32(kx, m, k, n, act):
     assert rel_err(got, ref) <= 1e-5
 
 
+@pytest.mark.parametrize("m,k,n,act", [(1, 8192, 16384, 0), (5, 1000, 300, -1), (16, 4096, 2050, 0), (3, 77, 9, -1),
+                                      (9, 16384, 1024, 0), (8, 300, 4096, 4)])
+def test_gemm_f32_skinny(kx, m, k, n, act):
+    """Dense layer for <= 16 rows (weight streaming on the CUDA cores, K split over the SMs, partial sums added in
+    slice order) vs float64: fp32 fma accumulation, within a few 1e-6 of the output scale."""
+    rng = np.random.default_rng(m * 7 + k + n)
+    x = rng.uniform(-1, 1, (m, k)).astype(F32)
+    w = (rng.standard_normal((k, n)) * np.sqrt(2.0 / k)).astype(F32)
+    b = rng.standard_normal(n).astype(F32) * 0.1
+    S = kx.lib().kx_skinny_slices(n, k)
+    part = torch.empty(S * 16 * n, dtype=torch.float32, device="cuda")
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    db, dw = dev(b), dev(w)
+    kx.call("kx_gemm_f32_skinny", dev(x).data_ptr(), k, dw.data_ptr(), db.data_ptr(), y.data_ptr(), n, m, n, k, act, 0.0,
+            part.data_ptr(), part.numel(), sp())
+    ref = ko.act((x.astype(np.float64) @ w.astype(np.float64) + b).astype(F32), act) if act == 4 else \
+        x.astype(np.float64) @ w.astype(np.float64) + b
+    if act == 0:
+        ref = np.maximum(ref, 0)
+    assert rel_err(host(y), ref) <= 3e-6  # fp32 fma over up to K / slices terms per thread, like a CPU sgemm
+
+
 @pytest.mark.parametrize("cfg", [
     dict(B=2, H=8, W=8, C=3, Co=16, k=3, s=1, d=1, p=1, g=1),
     dict(B=3, H=9, W=7, C=64, Co=64, k=3, s=1, d=1, p=1, g=1),
