@@ -17,7 +17,7 @@
 //   warp 1      TMEM allocator + MMA issuer (elected lane)
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32*(w%4)..+31), then
 //               dequant/bias/act and global stores
-//   warps 6-9   (3xTF32 only) A converters
+//   warps 6-13  (3xTF32 only) A converters
 // Shared memory holds STAGES operand stages in the canonical K-major 128-byte-swizzle layout; full/empty
 // mbarriers form the ring. Every wait is bounded (kx_sm100.cuh); a timeout sets the status word, the CTA
 // drains its in-flight copies and MMAs, frees TMEM and returns.
@@ -77,19 +77,6 @@ struct SmemCtl {
     uint32_t tmem;
     int abort;
 };
-
-// epilogue store of 32 consecutive columns of one row
-__device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], int ncols_valid, bool vec_ok) {
-    if (vec_ok && ncols_valid >= 32) {
-        float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-        for (int j = 0; j < 8; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (j < ncols_valid) dst[j] = v[j];
-    }
-}
 
 // ------------------------------------------------------------------------------------------ int8
 // Persistent kernel: each CTA walks output tiles t = blockIdx.x, +gridDim.x, ... (M-tile fastest so the CTAs
@@ -539,6 +526,9 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // running sum in a third region with round-to-nearest adds (((P0 + P1) + P2) + ..., a fixed order), which bounds
 // the truncated accumulation length by 32 MMAs: about 5e-7 per layer at any K. The result is running sum (or
 // Ah.Bh sum) + cross terms, rounded to nearest.
+// shared-memory bytes of the control block; the tile's bias (BN floats) follows it
+constexpr int F32_CTL_BYTES = (static_cast<int>(sizeof(SmemCtl)) + 15) & ~15;
+
 constexpr int KC_BLOCKS = 8;
 constexpr int DRAIN_MIN_K = 1024;  // reductions longer than this drain
 template <int BN, int STAGES, bool DRAIN = false>
@@ -547,7 +537,7 @@ struct F32Cfg {
     static constexpr int A_BYTES = BM * BK * 4;
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // A hi, A lo, B hi, B lo
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + static_cast<int>(sizeof(SmemCtl));
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + F32_CTL_BYTES + BN * 4;  // + the tile's bias
     // TMEM: [Ah.Bh | cross] or, draining, [Ah.Bh chunk 0 | Ah.Bh chunk 1 | cross | running sum]
     static constexpr uint32_t MAIN0 = 0, CROSS = DRAIN ? 2 * BN : BN, RUN = 3 * BN;
     static constexpr uint32_t TMEM_COLS = DRAIN ? 512 : 2 * BN;
@@ -573,8 +563,239 @@ struct ConvGeom {
     int H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog;
 };
 
+// ---- pieces shared by the one-CTA and the CTA-pair 3xTF32 kernels
+// Thread roles (448 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue, warps 6-13 A converters.
+// Converter warp cw (0..7) covers tile rows A_ROWS_PER_WARP cw .. + A_ROWS_PER_WARP - 1; per pass, lanes 8i..8i+7
+// read one row's 128 contiguous bytes (coalesced), split them, and write the 16-byte chunks to their swizzled
+// places. For a convolution each thread's rows have their output-pixel geometry computed once per tile.
+constexpr int F32_THREADS = 448;
+constexpr int A_CONV_WARPS = 8;
+constexpr int A_ROWS_PER_WARP = BM / A_CONV_WARPS;  // 16
+constexpr int A_PASSES = A_ROWS_PER_WARP / 4;       // rows of one thread
+struct ARows {
+    long rbase[A_PASSES];
+    int iy0[A_PASSES], ix0[A_PASSES];
+};
+
+template <bool CONV>
+__device__ __forceinline__ bool a_vec_ok(const float* A, int lda, const ConvGeom& cv) {
+    return CONV ? ((cv.cg & 3) == 0 && (cv.C & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0)
+                : (((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0));
+}
+
+template <bool CONV>
+__device__ __forceinline__ void a_rows_setup(ARows& g, const ConvGeom& cv, int m0, int cw, int lane) {
+    if constexpr (CONV) {
+#pragma unroll
+        for (int it = 0; it < A_PASSES; it++) {
+            const int gm = m0 + cw * A_ROWS_PER_WARP + it * 4 + (lane >> 3);
+            const int hw = cv.Ho * cv.Wo;
+            const int b = gm / hw, rem = gm - b * hw, oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+            g.rbase[it] = static_cast<long>(b) * cv.H;
+            g.iy0[it] = oy * cv.sh - cv.pt;
+            g.ix0[it] = ox * cv.sw - cv.pl;
+        }
+    }
+}
+
+// K block [k0, k0 + 32) of this warp's 32 rows (tile origin m0): load into registers (zero outside A)
+template <bool CONV>
+__device__ __forceinline__ void a_load_block(const float* __restrict__ A, int lda, bool vec, const ConvGeom& cv,
+                                             const ARows& g, int M, int K, int m0, int cw, int lane, int k0,
+                                             float4 (&v)[A_PASSES]) {
+    const int gk = k0 + (lane & 7) * 4;
+    int ky = 0, kx2 = 0, ci = 0;
+    if (CONV && gk < K) {
+        const int tap = gk / cv.cg;
+        ci = gk - tap * cv.cg;
+        ky = tap / cv.kw;
+        kx2 = tap - ky * cv.kw;
+    }
+#pragma unroll
+    for (int it = 0; it < A_PASSES; it++) {
+        const int gm = m0 + cw * A_ROWS_PER_WARP + it * 4 + (lane >> 3);
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gm < M && gk < K) {
+            if (!CONV) {
+                const float* src = A + static_cast<size_t>(gm) * lda + gk;
+                if (vec && gk + 3 < K) {
+                    t = __ldg(reinterpret_cast<const float4*>(src));
+                } else {
+                    t.x = __ldg(src);
+                    if (gk + 1 < K) t.y = __ldg(src + 1);
+                    if (gk + 2 < K) t.z = __ldg(src + 2);
+                    if (gk + 3 < K) t.w = __ldg(src + 3);
+                }
+            } else if (vec) {  // 4 consecutive channels of one tap
+                const int iy = g.iy0[it] + ky * cv.dh, ix = g.ix0[it] + kx2 * cv.dw;
+                if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
+                    t = __ldg(reinterpret_cast<const float4*>(A + ((g.rbase[it] + iy) * cv.W + ix) * cv.C + ci));
+            } else {  // channels per group not a multiple of 4: element by element
+                float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int kq = gk + q;
+                    if (kq >= K) break;
+                    const int tap = kq / cv.cg, c = kq - tap * cv.cg, yy = tap / cv.kw, xx = tap - yy * cv.kw;
+                    const int iy = g.iy0[it] + yy * cv.dh, ix = g.ix0[it] + xx * cv.dw;
+                    if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
+                        e[q] = __ldg(A + ((g.rbase[it] + iy) * cv.W + ix) * cv.C + c);
+                }
+                t = make_float4(e[0], e[1], e[2], e[3]);
+            }
+        }
+        v[it] = t;
+    }
+}
+
+// split the loaded block into hi / lo and store both into the stage's swizzled A tiles
+__device__ __forceinline__ void a_store_block(const float4 (&v)[A_PASSES], int cw, int lane, uint8_t* hi, uint8_t* lo) {
+#pragma unroll
+    for (int it = 0; it < A_PASSES; it++) {
+        const int r = cw * A_ROWS_PER_WARP + it * 4 + (lane >> 3);
+        const int j = lane & 7;
+        const int off = r * 128 + ((j ^ (r & 7)) << 4);
+        float4 h, l;
+        tf32_split(v[it].x, h.x, l.x);
+        tf32_split(v[it].y, h.y, l.y);
+        tf32_split(v[it].z, h.z, l.z);
+        tf32_split(v[it].w, h.w, l.w);
+        *reinterpret_cast<float4*>(hi + off) = h;
+        *reinterpret_cast<float4*>(lo + off) = l;
+    }
+}
+
+// Dense A: converter warp cw asks L2 for the 128-byte segments of its rows in the K block at k0; lane l takes row
+// A_ROWS_PER_WARP cw + l % 16, the first float (lanes 0-15) or the last (lanes 16-31), so a segment that
+// straddles two lines brings both.
+__device__ __forceinline__ void a_prefetch_block(const float* __restrict__ A, int lda, int M, int K, int m0, int cw,
+                                                 int lane, int k0) {
+    static_assert(A_ROWS_PER_WARP == 16, "two prefetching lanes per row");
+    const int gm = m0 + cw * A_ROWS_PER_WARP + (lane & 15);
+    if (gm >= M || k0 >= K) return;
+    const int off = lane < 16 ? 0 : (K - k0 < 32 ? K - k0 : 32) - 1;
+    kx::prefetch_l2(A + static_cast<size_t>(gm) * lda + k0 + off);
+}
+constexpr int A_L2_AHEAD = 5;  // K blocks between the L2 prefetch of a block and its register load
+
+// The converter warps' loop. Blocks kb + 1 and kb + 2 are in flight into registers (three rotating buffers, no
+// register copies) while block kb waits for its stage and is split and stored, and (dense A) block
+// kb + A_L2_AHEAD is requested into L2, so the load latency of A is hidden behind two stages. `arrive(s)` signals
+// that stage s holds this warp's rows.
+template <bool CONV, int BK, int STAGES, class StageA, class Arrive>
+__device__ __forceinline__ void a_convert_loop(const float* __restrict__ A, int lda, const ConvGeom& cv, int M, int K,
+                                               int m0, int cw, int lane, int nk, SmemCtl* ctl, volatile int* abort_flag,
+                                               int* status, StageA stage_a, Arrive arrive) {
+    const bool vec = a_vec_ok<CONV>(A, lda, cv);
+    ARows g;
+    a_rows_setup<CONV>(g, cv, m0, cw, lane);
+    if constexpr (!CONV)
+        for (int j = 2; j < A_L2_AHEAD; j++) a_prefetch_block(A, lda, M, K, m0, cw, lane, j * BK);
+    float4 va[A_PASSES], vb[A_PASSES], vc[A_PASSES];
+    a_load_block<CONV>(A, lda, vec, cv, g, M, K, m0, cw, lane, 0, va);
+    if (nk > 1) a_load_block<CONV>(A, lda, vec, cv, g, M, K, m0, cw, lane, BK, vb);
+    // block kb from `cur`; block kb + 2 into `ahead`; false on a timeout
+    auto step = [&](int kb, float4 (&cur)[A_PASSES], float4 (&ahead)[A_PASSES]) {
+        const int s = kb % STAGES;
+        if constexpr (!CONV) a_prefetch_block(A, lda, M, K, m0, cw, lane, (kb + A_L2_AHEAD) * BK);
+        if (kb + 2 < nk) a_load_block<CONV>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
+        if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) return false;
+        a_store_block(cur, cw, lane, stage_a(s), stage_a(s) + BM * BK * 4);
+        kx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) arrive(s);
+        return true;
+    };
+    for (int kb = 0; kb < nk; kb += 3) {
+        if (!step(kb, va, vc) || kb + 1 >= nk) break;
+        if (!step(kb + 1, vb, va) || kb + 2 >= nk) break;
+        if (!step(kb + 2, vc, vb)) break;
+    }
+}
+
+// DRAIN: add the finished Ah.Bh chunk at TMEM address t_chunk into the running sum at t_run (BN columns of this
+// warp's 32 lanes; the first chunk is copied)
+template <int BN>
+__device__ __forceinline__ void f32_add_chunk(uint32_t t_chunk, uint32_t t_run, bool first) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t p[32], t[32];
+        kx::tmem_ld32(t_chunk + c0, p);
+        if (!first) kx::tmem_ld32(t_run + c0, t);
+        kx::tmem_ld_wait();
+        if (!first) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) p[j] = __float_as_uint(__fadd_rn(__uint_as_float(t[j]), __uint_as_float(p[j])));
+        }
+        kx::tmem_st32(t_run + c0, p);
+    }
+    kx::tmem_st_wait();
+}
+
+// The epilogue warps copy the tile's bias columns [n0, n0 + BN) into shared memory while the mainloop runs (zero
+// past N), then meet on named barrier 1 (the four epilogue warps only).
+template <int BN>
+__device__ __forceinline__ void f32_stage_bias(float* sbias, const float* __restrict__ bias, int n0, int N, int ew,
+                                               int lane) {
+    for (int i = ew * 32 + lane; i < BN; i += 128) sbias[i] = (bias && n0 + i < N) ? __ldg(bias + n0 + i) : 0.0f;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Final epilogue of one warp's 32 rows (TMEM lanes; thread = row row0 + lane): (Ah.Bh sum + cross terms) rounded
+// to nearest, bias (from the shared-memory copy), activation. Each 32-column block is staged through one of the
+// warp's two 4 KB shared-memory buffers `stg` (row r's float4 j at r * 8 + (j ^ (r & 7)), conflict-free both ways;
+// the two alternate, so the next block's staging never waits for this block's reads) and written with lanes
+// 8i..8i+7 covering one row's 128 contiguous bytes, four full rows per store instruction. `ok` must be the same in
+// the whole warp.
+template <int BN, int ACTC>
+__device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross, bool ok, int row0, int lane, int n0,
+                                               const float* sbias, bool has_bias, float* __restrict__ y, int ldy,
+                                               int M, int N, int act, float alpha, float4* stg) {
+    const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32], x[32];
+        kx::tmem_ld32(t_sum + c0, r);
+        kx::tmem_ld32(t_cross + c0, x);
+        kx::tmem_ld_wait();
+        const int col0 = n0 + c0;
+        if (!ok || col0 >= N) continue;
+        float4* buf = stg + ((c0 >> 5) & 1) * 256;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; j4++) {
+            const float4 b4 = reinterpret_cast<const float4*>(sbias)[(c0 >> 2) + j4];
+            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float t = __fadd_rn(__uint_as_float(r[4 * j4 + e]), __uint_as_float(x[4 * j4 + e]));
+                if (has_bias) t = __fadd_rn(t, bb[e]);
+                v[e] = epi_act<ACTC>(t, act, alpha);
+            }
+            buf[lane * 8 + (j4 ^ (lane & 7))] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        __syncwarp();
+        const int q = lane & 7, gcol = col0 + 4 * q;
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            const int rr = 4 * p + (lane >> 3), grow = row0 + rr;
+            const float4 w = buf[rr * 8 + (q ^ (rr & 7))];
+            if (grow >= M || gcol >= N) continue;
+            float* dst = y + static_cast<size_t>(grow) * ldy + gcol;
+            if (vec && gcol + 3 < N) {
+                *reinterpret_cast<float4*>(dst) = w;
+            } else {
+                dst[0] = w.x;
+                if (gcol + 1 < N) dst[1] = w.y;
+                if (gcol + 2 < N) dst[2] = w.z;
+                if (gcol + 3 < N) dst[3] = w.w;
+            }
+        }
+    }
+}
+
 template <int BN, int STAGES, bool CONV, int ACTC, bool DRAIN>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
               const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
               int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv) {
@@ -601,7 +822,7 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            kx::mbar_init(&ctl->full[s], 1 + 4);  // TMA producer + 4 converter warps
+            kx::mbar_init(&ctl->full[s], 1 + A_CONV_WARPS);  // TMA producer + the converter warps
             kx::mbar_init(&ctl->empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {  // DRAIN: chunk buffer b holds a finished chunk / has been added in
@@ -669,27 +890,16 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         __syncwarp();
     } else if (warp < 6) {
         const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
         const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        float* sbias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);
+        f32_stage_bias<BN>(sbias, bias, n0, N, warp - 2, lane);
         uint32_t sum_col = C::MAIN0;  // TMEM column of the finished Ah.Bh sums
         if (DRAIN) {  // add each chunk into the running sum
             const int nchunks = (nk + KC_BLOCKS - 1) / KC_BLOCKS;
             for (int c = 0; c < nchunks; c++) {
                 if (!kx::mbar_wait(&ctl->acc_full[c & 1], (c >> 1) & 1, abort_flag, status)) break;
                 kx::tc_fence_after();
-#pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
-                    uint32_t p[32], t[32];
-                    kx::tmem_ld32(tmem + lanes + (c & 1) * BN + c0, p);
-                    if (c > 0) kx::tmem_ld32(tmem + lanes + C::RUN + c0, t);
-                    kx::tmem_ld_wait();
-                    if (c > 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j++) p[j] = __float_as_uint(__fadd_rn(__uint_as_float(t[j]), __uint_as_float(p[j])));
-                    }
-                    kx::tmem_st32(tmem + lanes + C::RUN + c0, p);
-                }
-                kx::tmem_st_wait();
+                f32_add_chunk<BN>(tmem + lanes + (c & 1) * BN, tmem + lanes + C::RUN, c == 0);
                 kx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[c & 1]);
@@ -698,123 +908,193 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         }
         drain_wait(&ctl->accf, 0);
         kx::tc_fence_after();
-        const bool ok = !*abort_flag;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            uint32_t r[32], x[32];
-            kx::tmem_ld32(tmem + lanes + sum_col + c0, r);
-            kx::tmem_ld32(tmem + lanes + C::CROSS + c0, x);
-            kx::tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; j++) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(x[j])));
-            const int col = n0 + c0;
-            if (!ok || row >= M || col >= N) continue;
-            const int nv = N - col;
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const int cc = col + (j < nv ? j : 0);
-                float t = __uint_as_float(r[j]);
-                if (bias) t = __fadd_rn(t, __ldg(bias + cc));
-                v[j] = epi_act<ACTC>(t, act, alpha);
-            }
-            store_row32(y + static_cast<size_t>(row) * ldy + col, v, nv,
-                        ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0));
-        }
+        // every MMA has completed: the operand stages are free, and warp w stages its stores in 8 KB of them
+        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+        f32_store_tile<BN, ACTC>(tmem + lanes + sum_col, tmem + lanes + C::CROSS, ok, m0 + q * 32, lane, n0, sbias,
+                                 bias != nullptr, y, ldy, M, N, act, alpha,
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192));
     } else {
-        // A converters: warp cw covers tile rows 32*cw .. 32*cw+31; per pass, lanes 8i..8i+7 read one row's
-        // 128 contiguous bytes (coalesced), split, and write the 16-byte chunks to their swizzled places.
-        const int cw = warp - 6;
-        const bool vec = CONV ? ((cv.cg & 3) == 0 && (cv.C & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0)
-                              : (((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0));
-        // conv: per-thread output-row geometry of its 8 rows, computed once
-        long rbase[8];
-        int iy0[8], ix0[8];
-        if (CONV) {
-#pragma unroll
-            for (int it = 0; it < 8; it++) {
-                const int gm = m0 + cw * 32 + it * 4 + (lane >> 3);
-                const int hw = cv.Ho * cv.Wo;
-                const int b = gm / hw, rem = gm - b * hw, oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
-                rbase[it] = static_cast<long>(b) * cv.H;
-                iy0[it] = oy * cv.sh - cv.pt;
-                ix0[it] = ox * cv.sw - cv.pl;
-            }
-        }
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % STAGES;
-            if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
-            const int k0 = kb * C::BK;
-            const int gk = k0 + (lane & 7) * 4;
-            int ky = 0, kx2 = 0, ci = 0;
-            if (CONV && gk < K) {
-                const int tap = gk / cv.cg;
-                ci = gk - tap * cv.cg;
-                ky = tap / cv.kw;
-                kx2 = tap - ky * cv.kw;
-            }
-            float4 v[8];
-#pragma unroll
-            for (int it = 0; it < 8; it++) {
-                const int r = cw * 32 + it * 4 + (lane >> 3);
-                const int gm = m0 + r;
-                float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (gm < M && gk < K) {
-                    if (!CONV) {
-                        const float* src = A + static_cast<size_t>(gm) * lda + gk;
-                        if (vec && gk + 3 < K) {
-                            t = __ldg(reinterpret_cast<const float4*>(src));
-                        } else {
-                            t.x = __ldg(src);
-                            if (gk + 1 < K) t.y = __ldg(src + 1);
-                            if (gk + 2 < K) t.z = __ldg(src + 2);
-                            if (gk + 3 < K) t.w = __ldg(src + 3);
-                        }
-                    } else if (vec) {  // 4 consecutive channels of one tap
-                        const int iy = iy0[it] + ky * cv.dh, ix = ix0[it] + kx2 * cv.dw;
-                        if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
-                            t = __ldg(reinterpret_cast<const float4*>(A + ((rbase[it] + iy) * cv.W + ix) * cv.C + ci));
-                    } else {  // channels per group not a multiple of 4: element by element
-                        float e[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const int kq = gk + q;
-                            if (kq >= K) break;
-                            const int tap = kq / cv.cg, c = kq - tap * cv.cg, yy = tap / cv.kw, xx = tap - yy * cv.kw;
-                            const int iy = iy0[it] + yy * cv.dh, ix = ix0[it] + xx * cv.dw;
-                            if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
-                                e[q] = __ldg(A + ((rbase[it] + iy) * cv.W + ix) * cv.C + c);
-                        }
-                        t = make_float4(e[0], e[1], e[2], e[3]);
-                    }
-                }
-                v[it] = t;
-            }
-            uint8_t* hi = sAhi(s);
-            uint8_t* lo = sAlo(s);
-#pragma unroll
-            for (int it = 0; it < 8; it++) {
-                const int r = cw * 32 + it * 4 + (lane >> 3);
-                const int j = lane & 7;
-                const int off = r * 128 + ((j ^ (r & 7)) << 4);
-                float4 h, l;
-                tf32_split(v[it].x, h.x, l.x);
-                tf32_split(v[it].y, h.y, l.y);
-                tf32_split(v[it].z, h.z, l.z);
-                tf32_split(v[it].w, h.w, l.w);
-                *reinterpret_cast<float4*>(hi + off) = h;
-                *reinterpret_cast<float4*>(lo + off) = l;
-            }
-            kx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) kx::mbar_arrive(&ctl->full[s]);
-        }
+        a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, ctl, abort_flag, status, sAhi,
+                                            [&](int s) { kx::mbar_arrive(&ctl->full[s]); });
     }
     kx::tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         kx::tc_fence_after();
         kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------ 3xTF32, CTA pairs
+// The same GEMM on 256 x BN output tiles computed by a cluster of two CTAs with M = 256 tcgen05.mma
+// (cta_group::2). CTA rank r converts A rows [m0 + 128 r, +128) of each K block into its own shared memory and
+// TMA-loads the hi / lo planes of B rows [n0 + (BN/2) r, +BN/2); the MMAs, issued by rank 0, read both CTAs'
+// halves and leave rows [m0 + 128 r, +128) x BN columns in rank r's TMEM, which rank r's epilogue warps drain.
+// Per SM a K block moves (BN/2) x 32 x 8 bytes of B instead of BN x 32 x 8 for the same MMA work, which halves
+// the L2 -> SM traffic of B and frees shared memory for more stages (BN = 256: 3 stages of 64 KB where the
+// one-CTA kernel holds 2 of 96 KB).
+// Synchronisation: rank 0's full[s] completes on its producer's arrive (armed with both CTAs' B bytes), the
+// arrivals of the sixteen converter warps of both CTAs (each after fence.proxy.async, which makes its shared-memory
+// stores visible to the tensor core's async proxy; the same default-semantics remote arrive CUTLASS's sm100
+// transform pipelines use to hand a converted stage to the 2-SM MMA) and both CTAs' TMA bytes. Rank 0's MMA thread
+// commits each stage to empty[s] of both CTAs, each DRAIN chunk to acc_full of both and its last MMAs to accf of
+// both (one commit per CTA, no multicast); the DRAIN epilogue warps of both CTAs arrive on rank 0's acc_empty.
+// Every wait is bounded; neither CTA leaves before the closing cluster barrier.
+template <int BN, bool DRAIN>
+struct F32PairCfg {
+    static constexpr int BK = 32;
+    static constexpr int STAGES = BN == 256 ? 3 : 4;
+    static constexpr int A_BYTES = BM * BK * 4;        // this CTA's 128 rows of one plane
+    static constexpr int B_BYTES = (BN / 2) * BK * 4;  // this CTA's BN / 2 rows of one plane
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + F32_CTL_BYTES + BN * 4;  // + the tile's bias
+    static constexpr uint32_t MAIN0 = 0, CROSS = DRAIN ? 2 * BN : BN, RUN = 3 * BN;
+    static constexpr uint32_t TMEM_COLS = DRAIN ? 512 : 2 * BN;
+    static_assert((DRAIN ? 4 : 2) * BN <= 512, "accumulator regions exceed TMEM");
+};
+
+template <int BN, bool CONV, int ACTC, bool DRAIN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F32_THREADS, 1)
+k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
+                   const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y,
+                   int ldy, int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv) {
+    using C = F32PairCfg<BN, DRAIN>;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);  // the same offset in both CTAs (same kernel, same static layout)
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + STAGES * C::STAGE_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    auto sAhi = [&](int s) { return smem + s * C::STAGE_BYTES; };
+    auto sAlo = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto sBhi = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::A_BYTES; };
+    auto sBlo = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = kx::cluster_ctarank();
+    const int n0 = static_cast<int>(blockIdx.x >> 1) * BN, m0 = blockIdx.y * (2 * BM) + static_cast<int>(rank) * BM;
+    const int nk = (K + C::BK - 1) / C::BK;
+    const int grp = CONV ? static_cast<int>(blockIdx.z) : 0;
+    const int brow0 = grp * (CONV ? cv.cog : 0);
+    if (CONV) {
+        A += grp * cv.cg;
+        y += brow0;
+        if (bias) bias += brow0;
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1 + 2 * A_CONV_WARPS);  // rank 0's producer + the converter warps of both CTAs
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            kx::mbar_init(&ctl->acc_full[b], 1);
+            kx::mbar_init(&ctl->acc_empty[b], 8);  // the epilogue warps of both CTAs
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {  // warp 1 of both CTAs, same destination offset
+        kx::tmem_alloc_pair(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish_pair();
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+    const uint32_t full0 = kx::mapa(kx::smem_u32(&ctl->full[0]), 0);  // rank 0's full[0]; full[s] = + 8 s
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmBhi);
+            kx::tma_prefetch_desc(&tmBlo);
+            const int brow = brow0 + n0 + static_cast<int>(rank) * (BN / 2);
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                if (rank == 0) kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * 2 * C::B_BYTES);
+                const uint32_t bar = full0 + 8u * static_cast<uint32_t>(s);
+                kx::tma_load_2d_pair(sBhi(s), &tmBhi, kb * C::BK, brow, bar);
+                kx::tma_load_2d_pair(sBlo(s), &tmBlo, kb * C::BK, brow, bar);
+                issued = kb + 1;
+            }
+            if (*abort_flag && rank == 0)  // the stages armed here also carry the peer's copies
+                for (int kb = issued > STAGES ? issued - STAGES : 0; kb < issued; kb++)
+                    drain_wait(&ctl->full[kb % STAGES], (kb / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = kx::idesc_tf32(2 * BM, BN);
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                const int c = DRAIN ? kb / KC_BLOCKS : 0, kc = DRAIN ? kb % KC_BLOCKS : kb;
+                const uint32_t d = tmem + (DRAIN ? (c & 1) * BN : C::MAIN0), dx = tmem + C::CROSS;
+                if (DRAIN && kc == 0) {
+                    if (!kx::mbar_wait(&ctl->acc_empty[c & 1], ((c >> 1) & 1) ^ 1, abort_flag, status)) break;
+                    kx::tc_fence_after();
+                }
+                if (!kx::mbar_wait(&ctl->full[s], (kb / STAGES) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t ah = kx::smem_u32(sAhi(s)), al = kx::smem_u32(sAlo(s));
+                const uint32_t bh = kx::smem_u32(sBhi(s)), bl = kx::smem_u32(sBlo(s));
+#pragma unroll
+                for (int kk = 0; kk < C::BK / 8; kk++) {
+                    const uint32_t o = kk * 32;
+                    kx::mma_tf32_pair(dx, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
+                    kx::mma_tf32_pair(dx, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                    kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
+                }
+                const uint32_t e = kx::smem_u32(&ctl->empty[s]);
+                kx::mma_commit_pair(e);
+                kx::mma_commit_pair(kx::mapa(e, 1));
+                if (DRAIN && (kc == KC_BLOCKS - 1 || kb == nk - 1)) {
+                    const uint32_t f = kx::smem_u32(&ctl->acc_full[c & 1]);
+                    kx::mma_commit_pair(f);
+                    kx::mma_commit_pair(kx::mapa(f, 1));
+                }
+            }
+            const uint32_t f = kx::smem_u32(&ctl->accf);
+            kx::mma_commit_pair(f);
+            kx::mma_commit_pair(kx::mapa(f, 1));
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        const int q = warp & 3;
+        const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        float* sbias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);
+        f32_stage_bias<BN>(sbias, bias, n0, N, warp - 2, lane);
+        uint32_t sum_col = C::MAIN0;
+        if (DRAIN) {
+            const uint32_t acc_empty0 = kx::mapa(kx::smem_u32(&ctl->acc_empty[0]), 0);
+            const int nchunks = (nk + KC_BLOCKS - 1) / KC_BLOCKS;
+            for (int c = 0; c < nchunks; c++) {
+                if (!kx::mbar_wait(&ctl->acc_full[c & 1], (c >> 1) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                f32_add_chunk<BN>(tmem + lanes + (c & 1) * BN, tmem + lanes + C::RUN, c == 0);
+                kx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) kx::mbar_arrive_remote(acc_empty0 + 8u * static_cast<uint32_t>(c & 1));
+            }
+            sum_col = C::RUN;
+        }
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        // every MMA has completed: the operand stages are free, and warp w stages its stores in 8 KB of them
+        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+        f32_store_tile<BN, ACTC>(tmem + lanes + sum_col, tmem + lanes + C::CROSS, ok, m0 + q * 32, lane, n0, sbias,
+                                 bias != nullptr, y, ldy, M, N, act, alpha,
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192));
+    } else {
+        a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, ctl, abort_flag, status, sAhi,
+                                            [&](int s) { kx::mbar_arrive_remote(full0 + 8u * static_cast<uint32_t>(s)); });
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc_pair(tmem, C::TMEM_COLS);
     }
 }
 
@@ -1006,7 +1286,25 @@ int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int 
     auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
-    kern<<<grid, 320, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+template <int BN, bool CONV, int ACTC, bool DRAIN>
+int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias,
+                    float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st,
+                    const ConvGeom& cv, int groups) {
+    using C = F32PairCfg<BN, DRAIN>;
+    CUtensorMap th, tl;
+    if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BN / 2) != 0 ||
+        make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BN / 2) != 0)
+        return -1;
+    auto kern = k_gemm_tf32x3_pair<BN, CONV, ACTC, DRAIN>;
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+    dim3 grid(2 * ((n + BN - 1) / BN), (m + 2 * BM - 1) / (2 * BM), groups);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -1069,22 +1367,40 @@ int dispatch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, in
     }
 }
 
-template <int BN, bool CONV, bool DRAIN = false>
+#define KX_F32_ARGS x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups
+template <int BN, bool CONV, bool DRAIN, bool PAIR>
+int launch_f32_act(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias,
+                   float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st,
+                   const ConvGeom& cv, int groups) {
+    if constexpr (PAIR) {
+        switch (act_class(act)) {
+        case -1: return launch_f32_pair<BN, CONV, -1, DRAIN>(KX_F32_ARGS);
+        case 0: return launch_f32_pair<BN, CONV, 0, DRAIN>(KX_F32_ARGS);
+        case 1: return launch_f32_pair<BN, CONV, 1, DRAIN>(KX_F32_ARGS);
+        default: return launch_f32_pair<BN, CONV, ACT_GENERIC, DRAIN>(KX_F32_ARGS);
+        }
+    } else {
+        switch (act_class(act)) {
+        case -1: return launch_f32<BN, CONV, -1, DRAIN>(KX_F32_ARGS);
+        case 0: return launch_f32<BN, CONV, 0, DRAIN>(KX_F32_ARGS);
+        case 1: return launch_f32<BN, CONV, 1, DRAIN>(KX_F32_ARGS);
+        default: return launch_f32<BN, CONV, ACT_GENERIC, DRAIN>(KX_F32_ARGS);
+        }
+    }
+}
+
+// Tile choice: more than 128 rows -> CTA pairs (256-row tiles); reductions longer than DRAIN_MIN_K -> 128-column
+// tiles with chunk draining; otherwise BN (128 for at most 128 output columns, else 256).
+template <int BN, bool CONV>
 int dispatch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
                  int groups) {
-    if (!DRAIN && k > DRAIN_MIN_K)  // long reductions: 128-column tiles with chunk draining
-        return dispatch_f32<128, CONV, true>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv,
-                                             groups);
-    switch (act_class(act)) {
-    case -1: return launch_f32<BN, CONV, -1, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
-    case 0: return launch_f32<BN, CONV, 0, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
-    case 1: return launch_f32<BN, CONV, 1, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups);
-    default:
-        return launch_f32<BN, CONV, ACT_GENERIC, DRAIN>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st,
-                                                        cv, groups);
-    }
+    const bool pair = m > BM;
+    if (k > DRAIN_MIN_K)
+        return pair ? launch_f32_act<128, CONV, true, true>(KX_F32_ARGS) : launch_f32_act<128, CONV, true, false>(KX_F32_ARGS);
+    return pair ? launch_f32_act<BN, CONV, false, true>(KX_F32_ARGS) : launch_f32_act<BN, CONV, false, false>(KX_F32_ARGS);
 }
+#undef KX_F32_ARGS
 
 }  // namespace
 

@@ -257,6 +257,8 @@ def test_gemm_f32_skinny(kx, m, k, n, act):
     dict(B=2, H=6, W=5, C=8, Co=300, k=2, s=1, d=1, p=0, g=1),
     dict(B=3, H=16, W=16, C=64, Co=128, k=3, s=1, d=1, p=1, g=1),
     dict(B=2, H=8, W=8, C=128, Co=256, k=3, s=1, d=1, p=1, g=1),
+    dict(B=5, H=8, W=8, C=128, Co=256, k=3, s=1, d=1, p=1, g=1),
+    dict(B=4, H=12, W=12, C=32, Co=48, k=3, s=1, d=1, p=1, g=2),
 ])
 def test_conv_implicit_gemm(kx, cfg):
     """implicit-GEMM conv (no im2col buffer) vs the oracle's im2col + sgemm restatement of kernix_conv_run."""
