@@ -38,8 +38,10 @@ struct kx_model_impl {
     cudaEvent_t ev_os[KX_PIPE_MAX], ev_out[KX_PIPE_MAX];
     int pipe;             /* pieces per chunk when pipelining ($KERNIX_PIPELINE; default 4) */
     int pipe_fixed;       /* 1: $KERNIX_PIPELINE was given, use it as is */
-    int pipe_now;         /* pieces per chunk for the current chunk size (decided after two timed calls) */
-    int tune_calls;       /* timed calls at the current chunk size */
+    int pipe_now;         /* pieces per chunk for the current chunk size (tuned over the first calls) */
+    int tune_calls;       /* calls made at the current chunk size, while tuning */
+    int tune_best;        /* fastest piece count tried so far, and its span in ms */
+    float tune_best_ms;
     int last_pieces;      /* pieces of the last chunk of the last call (whose events hold its timings) */
     /* workspace (one arena) */
     void* arena;
@@ -357,6 +359,7 @@ static int model_alloc(kernix_model* m, int rows) {
     m->batch = rows;
     im->pipe_now = im->pipe;
     im->tune_calls = 0;
+    im->tune_best = 0;
     return 0;
 }
 
@@ -671,20 +674,26 @@ static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float
     return rc ? -1 : 0;
 }
 
-/* Choose the piece count from the timings of the last call's last chunk: cutting pays when the copies are a
- * sizeable part of the work; when the kernels take more than 3x as long as either copy direction, smaller
- * pieces only make the kernels less efficient, so the chunk runs whole. Decided once per chunk size, after the
- * second call (the first one also pays for loading the kernels). */
+/* Choose the piece count by trying it: the calls after the first at a chunk size (the first also pays for loading
+ * the kernels) run with 1, 2, 3, 4, 6 and 8 pieces in turn, each timed on the device from its last chunk's first
+ * input copy to its last output copy, and the fastest count is kept from then on. How many pieces pay depends on
+ * the model (kernels that are much longer than the copies want one, kernels that lose efficiency on small pieces
+ * want few) and on the link, so it is measured rather than guessed. The result does not depend on the count. */
+static const int kx_pipe_cand[] = {1, 2, 3, 4, 6, 8};
+#define KX_PIPE_NCAND ((int)(sizeof kx_pipe_cand / sizeof kx_pipe_cand[0]))
 static void pipe_tune(struct kx_model_impl* im) {
-    if (im->pipe_fixed || im->tune_calls >= 2 || ++im->tune_calls < 2) return;
-    float t_in = 0.f, t_cmp = 0.f, t_out = 0.f, v;
-    for (int p = 0; p < im->last_pieces; p++) {
-        if (cudaEventElapsedTime(&v, im->ev_is[p], im->ev_in[p]) == cudaSuccess) t_in += v;
-        if (cudaEventElapsedTime(&v, im->ev_cs[p], im->ev_comp[p]) == cudaSuccess) t_cmp += v;
-        if (cudaEventElapsedTime(&v, im->ev_os[p], im->ev_out[p]) == cudaSuccess) t_out += v;
+    if (im->pipe_fixed || im->tune_calls > KX_PIPE_NCAND) return;
+    const int c = im->tune_calls++; /* call c at this chunk size ran with pipe_now pieces */
+    if (c >= 1 && im->last_pieces > 0) {
+        float v;
+        if (cudaEventElapsedTime(&v, im->ev_is[0], im->ev_out[im->last_pieces - 1]) == cudaSuccess &&
+            (c == 1 || v < im->tune_best_ms)) {
+            im->tune_best_ms = v;
+            im->tune_best = im->pipe_now;
+        }
+        cudaGetLastError();
     }
-    cudaGetLastError();
-    im->pipe_now = t_cmp > 3.0f * (t_in > t_out ? t_in : t_out) ? 1 : im->pipe;
+    im->pipe_now = c < KX_PIPE_NCAND ? kx_pipe_cand[c] : (im->tune_best > 0 ? im->tune_best : im->pipe);
 }
 
 /* host-memory forward: enqueue, then wait for every stream and check the status word */

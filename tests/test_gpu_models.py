@@ -150,6 +150,19 @@ def test_pipelined_host_forward_is_cut_invariant(Model, model_dir, monkeypatch, 
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
 
 
+def test_piece_count_tuning_keeps_results(Model, model_dir, monkeypatch):
+    """Without $KERNIX_PIPELINE the first calls at a chunk size try 1, 2, 3, 4, 6 and 8 pieces and keep the
+    fastest: every call, during and after the tuning, returns bitwise the same rows."""
+    from kernix_b200 import configs
+    monkeypatch.delenv("KERNIX_PIPELINE", raising=False)
+    x = configs.inputs("c2", 1000)
+    m = Model(cfg_path("c2", model_dir))
+    first = m(x)
+    for _ in range(9):
+        assert np.array_equal(m(x), first)
+    m.close()
+
+
 def test_pipelined_forward_of_a_view_only_graph(Model, model_dir, monkeypatch):
     """A graph that is only a RESHAPE of its input: the output rows are read from the pieces' input rows."""
     from kernix_b200 import knx_writer
