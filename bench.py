@@ -50,6 +50,7 @@ def parse():
                     help="profiling case: only run the int8 GEMM of c2's 4096x4096 layer with M rows, 3 launches, then exit")
     ap.add_argument("--kernel-k", type=int, default=4096, help="K of the profiling case (1024: c2's first layer)")
     ap.add_argument("--kernel-act", type=int, default=1, help="activation of the profiling case (1 GELU, -1 none)")
+    ap.add_argument("--kernel-dtype", choices=["i8", "f32"], default="i8", help="GEMM of the profiling case")
     ap.add_argument("--workload", choices=["c2", "c5-rows"], default="c2",
                     help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
                          "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling)")
@@ -57,9 +58,10 @@ def parse():
     return ap.parse_args()
 
 
-def kernel_case(m_rows, k=4096, act=1):
-    """Three launches of the int8 GEMM (GELU epilogue by default) on an M x K x 4096 problem -- for an ncu capture
-    of one kernel on a case larger than L2 (M = 8192, K = 4096: 32 MB A + 16 MB B + 128 MB C)."""
+def kernel_case(m_rows, k=4096, act=1, dtype="i8"):
+    """Three launches of the int8 GEMM (GELU epilogue by default), or with dtype "f32" of the 3xTF32 GEMM, on an
+    M x K x 4096 problem -- for an ncu capture of one kernel on a case larger than L2 (M = 8192, K = 4096: 32 MB A
+    + 16 MB B + 128 MB C for int8)."""
     import numpy as np
     import torch
 
@@ -68,6 +70,21 @@ def kernel_case(m_rows, k=4096, act=1):
     L = kx_abi.lib()
     n = 4096
     rng = np.random.default_rng(0)
+    if dtype == "f32":
+        ldw = (k + 31) // 32 * 32
+        w = torch.from_numpy((rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)).cuda()
+        hi = torch.empty((n, ldw), device="cuda")
+        lo = torch.empty((n, ldw), device="cuda")
+        kx_abi.call("kx_prep_f32_weight", w.data_ptr(), k, n, hi.data_ptr(), lo.data_ptr(), ldw, None)
+        x = torch.from_numpy(rng.standard_normal((m_rows, k)).astype(np.float32)).cuda()
+        b = torch.zeros(n, device="cuda")
+        y = torch.empty((m_rows, n), device="cuda")
+        for _ in range(3):
+            kx_abi.call("kx_gemm_f32", x.data_ptr(), k, hi.data_ptr(), lo.data_ptr(), ldw, b.data_ptr(), y.data_ptr(), n,
+                        m_rows, n, k, act, 0.0, None, None)
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel_case": "k_gemm_tf32x3", "m": m_rows, "n": n, "k": k, "act": act, "launches": 3}))
+        return
     xq = torch.from_numpy(rng.integers(-127, 128, (m_rows, k), dtype=np.int8)).cuda()
     wq = torch.from_numpy(rng.integers(-127, 128, (n, k), dtype=np.int8)).cuda()
     sx = torch.full((m_rows,), 0.01, device="cuda")
@@ -525,7 +542,7 @@ def run_c5_rows(args):
 if __name__ == "__main__":
     a = parse()
     if a.kernel_case:
-        kernel_case(a.kernel_case, a.kernel_k, a.kernel_act)
+        kernel_case(a.kernel_case, a.kernel_k, a.kernel_act, a.kernel_dtype)
     elif a.workload == "c5-rows":
         run_c5_rows(a)
     elif a.impl == "reference":
