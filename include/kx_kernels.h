@@ -136,9 +136,11 @@ KERNIX_API int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo,
 
 /* scaled dot-product attention per (sample, head): ctx = softmax(scale * Q K^T [+ causal -inf]) V with
  * scale = 1/sqrt(dk) (kernix_attention_run :1015-1046). q: (B*Rq) rows of H*dk at leading dim ldq, k: (B*S) rows
- * of H*dk (ldk), v: (B*S) rows of H*dv (ldv), ctx: (B*Rq) rows of H*dv (ldc). */
+ * of H*dk (ldk), v: (B*S) rows of H*dv (ldv), ctx: (B*Rq) rows of H*dv (ldc). Rq, S <= 128 with head dims <= 64
+ * run on the tensor cores (3xTF32), the rest on the CUDA cores. status: device word that receives
+ * KX_STATUS_TIMEOUT if a bounded wait gives up (may be NULL). */
 KERNIX_API int kx_attention(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* ctx, int ldc, int B,
-                 int Rq, int S, int H, int dk, int dv, int causal, void* stream);
+                 int Rq, int S, int H, int dk, int dv, int causal, int* status, void* stream);
 
 /* y = max(a*x + b, 0), fused multiply-add then max (src/kernix_metal.m:331-338; include/kernix.h:990) */
 KERNIX_API int kx_fma_relu(const float* a, const float* x, const float* b, float* y, size_t n, void* stream);

@@ -492,7 +492,7 @@ static int step_run(kernix_model* m, int i, int B) {
             if (kx_gemm_f32(a, s->in, s->wqkv.d_hi, s->wqkv.d_lo, s->wqkv.ldw, s->d_bqkv, qkv, nq, (int)rin, nq, s->in,
                             KERNIX_ACT_NONE, 0.0f, im->status, st) != 0 ||
                 kx_attention(qkv, nq, qkv + hk, nq, qkv + 2 * hk, nq, ctx, hv, B, vi->r, vv->r, s->heads, s->dk, s->dv,
-                             s->causal, st) != 0)
+                             s->causal, im->status, st) != 0)
                 return -1;
         } else {
             float* Q = (float*)align_ptr(im->scratch);
@@ -506,7 +506,8 @@ static int step_run(kernix_model* m, int i, int B) {
                             KERNIX_ACT_NONE, 0.0f, im->status, st) != 0 ||
                 kx_gemm_f32(val_ptr(im, vid), vv->c, s->wv.d_hi, s->wv.d_lo, s->wv.ldw, s->d_bv, V, hv, (int)S, hv, vv->c,
                             KERNIX_ACT_NONE, 0.0f, im->status, st) != 0 ||
-                kx_attention(Q, hk, K, hk, V, hv, ctx, hv, B, vi->r, vv->r, s->heads, s->dk, s->dv, s->causal, st) != 0)
+                kx_attention(Q, hk, K, hk, V, hv, ctx, hv, B, vi->r, vv->r, s->heads, s->dk, s->dv, s->causal, im->status,
+                             st) != 0)
                 return -1;
         }
         return kx_gemm_f32(ctx, hv, s->wo.d_hi, s->wo.d_lo, s->wo.ldw, s->d_bo, y, s->out, (int)rin, s->out, hv,

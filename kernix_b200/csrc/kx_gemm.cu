@@ -544,17 +544,7 @@ struct F32Cfg {
     static_assert((DRAIN ? 4 : 2) * BN <= 512, "accumulator regions exceed TMEM");
 };
 
-// split v into hi (v rounded to tf32: 10 explicit mantissa bits, ties away from zero) and lo = v - hi (exact)
-__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
-    const uint32_t b = __float_as_uint(v);
-    if ((b & 0x7F800000u) == 0x7F800000u) {  // inf / nan pass through unchanged
-        hi = v;
-        lo = 0.0f;
-        return;
-    }
-    hi = __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
-    lo = __fsub_rn(v, hi);
-}
+using kx::tf32_split;
 
 // Implicit-GEMM convolution geometry: output row m = (b, oy, ox), reduction index k = (ky, kx, ci) with ci
 // fastest, matching the file's weight row order (tools/knx3.py:93-104). Group g = blockIdx.z reads input

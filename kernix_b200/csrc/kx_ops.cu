@@ -912,6 +912,10 @@ __global__ void k_skinny_reduce(const float* __restrict__ part, int S, int M, in
 
 }  // namespace
 
+// tensor-core attention core (kx_attn.cu): 0 done, 1 shape not covered, -1 launch error
+int kx_attention_tc(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* ctx, int ldc, int B,
+                    int Rq, int S, int H, int dk, int dv, int causal, float scale, int* status, cudaStream_t st);
+
 extern "C" {
 
 // columns per thread of the skinny kernel for m rows and n columns (m * CPT accumulators <= 32; n divisible)
@@ -1133,10 +1137,15 @@ int kx_conv_depthwise(const float* x, const float* w, const float* bias, float* 
 }
 
 int kx_attention(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* ctx, int ldc, int B,
-                 int Rq, int S, int H, int dk, int dv, int causal, void* stream) {
+                 int Rq, int S, int H, int dk, int dv, int causal, int* status, void* stream) {
     if (B <= 0 || Rq <= 0) return 0;
     if (S <= 0 || dk <= 0 || dv <= 0 || dk > 128 || dv > 128) return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    {  // tensor cores (kx_attn.cu) when the shape fits one CTA per (sample, head)
+        const int rc = kx_attention_tc(q, ldq, k, ldk, v, ldv, ctx, ldc, B, Rq, S, H, dk, dv, causal,
+                                       1.0f / sqrtf(static_cast<float>(dk)), status, st);
+        if (rc <= 0) return rc;
+    }
     if (S <= ATT_SMAX && dk <= ATT_D && dv <= ATT_D) {
         const int SP = (S + 15) / 16 * 16;
         const size_t smem = static_cast<size_t>(att_smem_floats(SP)) * sizeof(float);

@@ -134,6 +134,19 @@ __device__ __forceinline__ uint64_t desc_sw128_kmajor(uint32_t smem_addr) {
     return d;
 }
 
+// split v into hi (v rounded to tf32: 10 explicit mantissa bits, ties away from zero) and lo = v - hi (exact): the
+// operand halves of the 3xTF32 product a.b = ah.bh + (al.bh + ah.bl)
+__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
+    const uint32_t b = __float_as_uint(v);
+    if ((b & 0x7F800000u) == 0x7F800000u) {  // inf / nan pass through unchanged
+        hi = v;
+        lo = 0.0f;
+        return;
+    }
+    hi = __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+    lo = __fsub_rn(v, hi);
+}
+
 // Instruction descriptors (kind::i8 and kind::tf32): dense, no negation, both operands K-major.
 // bits [4,6) accumulator format (1 = f32, 2 = s32), [7,10) A format, [10,13) B format
 // (tf32 = 2; signed int8 = 1), [17,23) N >> 3, [24,29) M >> 4.

@@ -387,11 +387,14 @@ def test_depthwise_embedding_fma_relu(kx):
 
 @pytest.mark.parametrize("Rq,S,H,dk,dv,causal,packed", [(128, 128, 8, 64, 64, False, False), (10, 10, 4, 4, 4, True, False),
                                                         (5, 17, 2, 32, 48, False, False), (128, 128, 8, 64, 64, False, True),
+                                                        (128, 96, 2, 60, 36, True, False), (128, 128, 3, 62, 30, False, True),
+                                                        (128, 128, 1, 64, 64, True, True), (1, 1, 1, 8, 8, False, False),
                                                         (200, 200, 4, 64, 64, True, False), (256, 256, 2, 16, 64, False, True),
                                                         (70, 300, 2, 80, 96, True, False), (33, 257, 3, 64, 64, False, False)])
 def test_attention_core(kx, Rq, S, H, dk, dv, causal, packed):
-    """packed: Q, K, V are column blocks of one [Q | K | V] row buffer (the fused-projection layout). S <= 256 with
-    head dims <= 64 run the register-tiled kernel (ragged query tiles, causal masks); longer or wider heads the
+    """packed: Q, K, V are column blocks of one [Q | K | V] row buffer (the fused-projection layout). Rq, S <= 128 with
+    head dims <= 64 run on the tensor cores (3xTF32: ragged rows and keys, head dims not multiples of 8, causal
+    masks); S <= 256 with head dims <= 64 the register-tiled CUDA-core kernel; longer or wider heads the
     one-row-per-thread kernel."""
     rng = np.random.default_rng(Rq + S + dk)
     B = 3
@@ -399,15 +402,16 @@ def test_attention_core(kx, Rq, S, H, dk, dv, causal, packed):
     k = rng.standard_normal((B * S, H * dk)).astype(F32)
     v = rng.standard_normal((B * S, H * dv)).astype(F32)
     ctx = torch.empty((B * Rq, H * dv), dtype=torch.float32, device="cuda")
+    st = status()
     if packed:
         qkv = dev(np.concatenate([q, k, v], axis=1))
         ld = 2 * H * dk + H * dv
         base = qkv.data_ptr()
         kx.call("kx_attention", base, ld, base + 4 * H * dk, ld, base + 8 * H * dk, ld, ctx.data_ptr(), H * dv, B, Rq, S, H, dk,
-                dv, int(causal), sp())
+                dv, int(causal), st.data_ptr(), sp())
     else:
         kx.call("kx_attention", dev(q).data_ptr(), H * dk, dev(k).data_ptr(), H * dk, dev(v).data_ptr(), H * dv,
-                ctx.data_ptr(), H * dv, B, Rq, S, H, dk, dv, int(causal), sp())
+                ctx.data_ptr(), H * dv, B, Rq, S, H, dk, dv, int(causal), st.data_ptr(), sp())
     Q = q.reshape(B, Rq, H, dk).transpose(0, 2, 1, 3).astype(np.float64)
     K = k.reshape(B, S, H, dk).transpose(0, 2, 1, 3).astype(np.float64)
     V = v.reshape(B, S, H, dv).transpose(0, 2, 1, 3).astype(np.float64)
@@ -417,4 +421,5 @@ def test_attention_core(kx, Rq, S, H, dk, dv, causal, packed):
     P = np.exp(P - P.max(-1, keepdims=True))
     P /= P.sum(-1, keepdims=True)
     want = (P @ V).transpose(0, 2, 1, 3).reshape(B * Rq, H * dv)
+    check_status(st)
     assert rel_err(host(ctx), want) <= 1e-5

@@ -209,7 +209,8 @@ def test_attention_composition_by_hand(libkx, B):
     assert rel_err(qkv.cpu().numpy(), want_qkv) <= 1e-5, "QKV GEMM"
     ctx = torch.empty((B * S, d), device="cuda")
     base = qkv.data_ptr()
-    kx.call("kx_attention", base, 3 * d, base + 4 * d, 3 * d, base + 8 * d, 3 * d, ctx.data_ptr(), d, B, S, S, H, dk, dk, 0, None)
+    kx.call("kx_attention", base, 3 * d, base + 4 * d, 3 * d, base + 8 * d, 3 * d, ctx.data_ptr(), d, B, S, S, H, dk, dk, 0, None,
+            None)
     torch.cuda.synchronize()
     Q, K, V = (want_qkv[:, i * d:(i + 1) * d].reshape(B, S, H, dk).transpose(0, 2, 1, 3) for i in range(3))
     P = Q @ K.transpose(0, 1, 3, 2) / np.sqrt(dk)
