@@ -528,6 +528,8 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // Ah.Bh sum) + cross terms, rounded to nearest.
 // shared-memory bytes of the control block; the tile's bias (BN floats) follows it
 constexpr int F32_CTL_BYTES = (static_cast<int>(sizeof(SmemCtl)) + 15) & ~15;
+// warps per TMEM lane quarter in the final epilogue: the epilogue warp and the two converter warps of that quarter
+constexpr int F32_EPI_PARTS = 3;
 
 constexpr int KC_BLOCKS = 8;
 constexpr int DRAIN_MIN_K = 1024;  // reductions longer than this drain
@@ -731,7 +733,8 @@ __device__ __forceinline__ void f32_stage_bias(float* sbias, const float* __rest
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-// Final epilogue of one warp's 32 rows (TMEM lanes; thread = row row0 + lane): (Ah.Bh sum + cross terms) rounded
+// Final epilogue of one warp's 32 rows (TMEM lanes; thread = row row0 + lane), 32-column blocks part, part + 3, ...
+// (the three warps of a TMEM lane quarter share a tile's blocks): (Ah.Bh sum + cross terms) rounded
 // to nearest, bias (from the shared-memory copy), activation. Each 32-column block is staged through one of the
 // warp's two 4 KB shared-memory buffers `stg` (row r's float4 j at r * 8 + (j ^ (r & 7)), conflict-free both ways;
 // the two alternate, so the next block's staging never waits for this block's reads) and written with lanes
@@ -740,10 +743,10 @@ __device__ __forceinline__ void f32_stage_bias(float* sbias, const float* __rest
 template <int BN, int ACTC>
 __device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross, bool ok, int row0, int lane, int n0,
                                                const float* sbias, bool has_bias, float* __restrict__ y, int ldy,
-                                               int M, int N, int act, float alpha, float4* stg) {
+                                               int M, int N, int act, float alpha, float4* stg, int part) {
     const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = 32 * part; c0 < BN; c0 += 32 * F32_EPI_PARTS) {
         uint32_t r[32], x[32];
         kx::tmem_ld32(t_sum + c0, r);
         kx::tmem_ld32(t_cross + c0, x);
@@ -883,7 +886,6 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
         float* sbias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);
         f32_stage_bias<BN>(sbias, bias, n0, N, warp - 2, lane);
-        uint32_t sum_col = C::MAIN0;  // TMEM column of the finished Ah.Bh sums
         if (DRAIN) {  // add each chunk into the running sum
             const int nchunks = (nk + KC_BLOCKS - 1) / KC_BLOCKS;
             for (int c = 0; c < nchunks; c++) {
@@ -894,18 +896,25 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
                 __syncwarp();
                 if (lane == 0) kx::mbar_arrive(&ctl->acc_empty[c & 1]);
             }
-            sum_col = C::RUN;
         }
-        drain_wait(&ctl->accf, 0);
-        kx::tc_fence_after();
-        // every MMA has completed: the operand stages are free, and warp w stages its stores in 8 KB of them
-        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
-        f32_store_tile<BN, ACTC>(tmem + lanes + sum_col, tmem + lanes + C::CROSS, ok, m0 + q * 32, lane, n0, sbias,
-                                 bias != nullptr, y, ldy, M, N, act, alpha,
-                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192));
     } else {
         a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, ctl, abort_flag, status, sAhi,
                                             [&](int s) { kx::mbar_arrive(&ctl->full[s]); });
+    }
+    if (warp >= 2) {
+        // Final epilogue on twelve warps: per TMEM lane quarter the epilogue warp and the two converter warps of that
+        // quarter share the tile's 32-column blocks. Every MMA has completed (accf): the operand stages are free and
+        // warp w stages its stores in 8 KB of them; named barrier 2 (these twelve warps) makes the bias copy visible.
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        asm volatile("bar.sync 2, 384;" ::: "memory");
+        const int q = warp & 3, part = warp < 6 ? 0 : (warp < 10 ? 1 : 2);
+        const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        const float* sbias = reinterpret_cast<const float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);
+        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+        f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
+                                 n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part);
     }
     kx::tc_fence_before();
     __syncthreads();
@@ -1055,7 +1064,6 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
         const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
         float* sbias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);
         f32_stage_bias<BN>(sbias, bias, n0, N, warp - 2, lane);
-        uint32_t sum_col = C::MAIN0;
         if (DRAIN) {
             const uint32_t acc_empty0 = kx::mapa(kx::smem_u32(&ctl->acc_empty[0]), 0);
             const int nchunks = (nk + KC_BLOCKS - 1) / KC_BLOCKS;
@@ -1067,18 +1075,25 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
                 __syncwarp();
                 if (lane == 0) kx::mbar_arrive_remote(acc_empty0 + 8u * static_cast<uint32_t>(c & 1));
             }
-            sum_col = C::RUN;
         }
-        drain_wait(&ctl->accf, 0);
-        kx::tc_fence_after();
-        // every MMA has completed: the operand stages are free, and warp w stages its stores in 8 KB of them
-        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
-        f32_store_tile<BN, ACTC>(tmem + lanes + sum_col, tmem + lanes + C::CROSS, ok, m0 + q * 32, lane, n0, sbias,
-                                 bias != nullptr, y, ldy, M, N, act, alpha,
-                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192));
     } else {
         a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, ctl, abort_flag, status, sAhi,
                                             [&](int s) { kx::mbar_arrive_remote(full0 + 8u * static_cast<uint32_t>(s)); });
+    }
+    if (warp >= 2) {
+        // Final epilogue on twelve warps: per TMEM lane quarter the epilogue warp and the two converter warps of that
+        // quarter share the tile's 32-column blocks. Every MMA has completed (accf): the operand stages are free and
+        // warp w stages its stores in 8 KB of them; named barrier 2 (these twelve warps) makes the bias copy visible.
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        asm volatile("bar.sync 2, 384;" ::: "memory");
+        const int q = warp & 3, part = warp < 6 ? 0 : (warp < 10 ? 1 : 2);
+        const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        const float* sbias = reinterpret_cast<const float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);
+        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+        f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
+                                 n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part);
     }
     kx::tc_fence_before();
     kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
