@@ -51,10 +51,13 @@ def parse():
     ap.add_argument("--kernel-k", type=int, default=4096, help="K of the profiling case (1024: c2's first layer)")
     ap.add_argument("--kernel-act", type=int, default=1, help="activation of the profiling case (1 GELU, -1 none)")
     ap.add_argument("--kernel-dtype", choices=["i8", "f32"], default="i8", help="GEMM of the profiling case")
-    ap.add_argument("--workload", choices=["c2", "c5-rows"], default="c2",
+    ap.add_argument("--workload", choices=["c2", "c5-rows", "c1", "c3", "c4", "c5"], default="c2",
                     help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
-                         "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling)")
-    ap.add_argument("--batch", type=int, default=64, help="global batch of --workload c5-rows")
+                         "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling). c1, c3, c4, "
+                         "c5: the device-resident forward of that configuration at --batch samples per GPU")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="samples per step: global batch of c5-rows (default 64), per-GPU batch of c1/c3/c4/c5 "
+                         "(default: the configuration's own, 256 / 1024 / 512 / 256)")
     return ap.parse_args()
 
 
@@ -442,6 +445,85 @@ def gemm_roofline(L, torch, np, steps, flush):
             "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
 
 
+# algorithmic FLOPs per sample (2 per MAC) of the configurations, and their default batch
+CONFIG_FLOPS = {"c1": 2 * 535040, "c3": 2 * 115018240, "c4": 2 * 2516582400, "c5": 2 * 536870912}
+CONFIG_BATCH = {"c1": 256, "c3": 1024, "c4": 512, "c5": 256}
+
+
+def run_config(args):
+    """Device-resident forward of configuration c1, c3, c4 or c5 (kernix_model_forward_device; inputs already in
+    HBM): each step is one forward of --batch samples per GPU after a 256 MB L2 flush, timed with CUDA events on the
+    model's stream; value = samples of all ranks / max over ranks of the timed steps (weak scaling)."""
+    import datetime
+
+    import torch
+
+    cfg = args.workload
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=torch.device("cuda", local))
+    from kernix_b200 import Model, build, configs, kx_abi
+    build.build()
+    L = kx_abi.lib()
+    L.kernix_model_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    L.kernix_model_forward_device.restype = ctypes.c_int
+    L.kernix_model_check.argtypes = [ctypes.c_void_p]
+    L.kernix_model_check.restype = ctypes.c_int
+    model_dir = os.environ.get("KERNIX_MODEL_DIR", f"/tmp/kernix_models_r{rank}")
+    os.environ["KERNIX_DEVICE"] = str(local)
+    m = Model(configs.model_path(cfg, model_dir), workspace_mb=0)
+    B = args.batch or CONFIG_BATCH[cfg]
+    x = torch.from_numpy(configs.inputs(cfg, B, seed=100 + rank)).cuda()
+    rows = x.shape[0]
+    y = torch.empty((B, m.out_dim), dtype=torch.float32, device="cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")  # 256 MB, larger than L2
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+
+    def step():
+        if L.kernix_model_forward_device(m._h, x.data_ptr(), rows, y.data_ptr(), stream.cuda_stream) != 0:
+            raise RuntimeError("forward_device failed")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    if L.kernix_model_check(m._h) != 0:
+        raise RuntimeError("a kernel reported a failure")
+    t = reduce_max(dist, sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3, "cuda")
+    if rank == 0:
+        line = {
+            "metric": f"samples/s, configuration {cfg}, device-resident forward", "value": world * B * args.steps / t,
+            "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic: the configuration's seeded inputs and weights",
+            "config": {"workload": cfg, "batch_per_gpu": B, "global_batch": B * world, "parallelism": f"dp{world}",
+                       "l2": "flushed (256 MB write) before every step"},
+            "achieved_tflops": CONFIG_FLOPS[cfg] * B * world * args.steps / t / 1e12,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_c5_rows(args):
     """Config c5 (fp32 MLP 8192-16384-16384-8192, ReLU) at a small batch, its three layers split by output columns
     over the ranks (kernix_model_load_sharded + NCCL all-gather on the model's stream). value: batch * steps / (max
@@ -474,7 +556,7 @@ def run_c5_rows(args):
     path = configs.model_path("c5")
     os.environ["KERNIX_DEVICE"] = str(local)
     m = Model(path, workspace_mb=0, shard=(rank, world, shard.torch_allgather()) if world > 1 else None)
-    B = args.batch
+    B = args.batch or 64
     x_pin = torch.from_numpy(configs.inputs("c5", B, seed=100)).pin_memory()
     out_pin = torch.empty((B, 8192), dtype=torch.float32).pin_memory()
     x_dev = x_pin.cuda()
@@ -545,6 +627,8 @@ if __name__ == "__main__":
         kernel_case(a.kernel_case, a.kernel_k, a.kernel_act, a.kernel_dtype)
     elif a.workload == "c5-rows":
         run_c5_rows(a)
+    elif a.workload in CONFIG_FLOPS and a.impl != "reference":
+        run_config(a)
     elif a.impl == "reference":
         run_reference(a)
     else:

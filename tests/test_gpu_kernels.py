@@ -207,7 +207,7 @@ def test_prep_f32_split_is_exact(kx):
 @pytest.mark.parametrize("act", [ko.ACT_NONE, 0])
 def test_gemm_f32_3xtf32(kx, m, k, n, act):
     """3xTF32 GEMM + bias + act vs float64: max abs error <= 1e-5 x output scale (the dense-MLP bound). tcgen05's
-    truncating fp32 accumulation adds ~2e-9 * (accumulation length): reductions longer than 1024 drain their
+    truncating fp32 accumulation adds ~2e-9 * (accumulation length): reductions longer than 2048 drain their
     partial sums every 256 and meet 1e-5 up to K = 16384."""
     rng = np.random.default_rng(m + 7 * k + n)
     x = rng.standard_normal((m, k)).astype(F32)
