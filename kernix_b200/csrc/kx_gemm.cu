@@ -1315,6 +1315,113 @@ int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo,
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+// ------------------------------------------------------------------- direct convolution, tiny K
+// For reductions of at most DC_MAXK with at most 64 output channels per group (the first 3x3 layer over RGB: K = 27,
+// 64 channels) a tensor-core tile spends its time on pipeline set-up and a whole epilogue per 32 K, so these layers run
+// on the CUDA cores. Persistent blocks of 256 threads: lane l of every warp owns output channels l and l + 32 (their
+// K weights in registers, w = hi + lo of the split planes, exact); per tile of DC_PIX consecutive output pixels the
+// block gathers their K inputs into shared memory (zero outside the image, the file's (ky, kx, ci) order, through
+// per-pixel and per-k offset tables), then warp w computes pixels w, w + 8, ...: fp32 fmas over the reduction in
+// order, bias, activation, and two coalesced 128-byte stores per pixel.
+constexpr int DC_MAXK = 32, DC_MAXCO = 64, DC_PIX = 64;
+template <int ACTC>
+__global__ void __launch_bounds__(256) k_conv_direct(const float* __restrict__ x, const float* __restrict__ whi,
+                                                      const float* __restrict__ wlo, int ldw, const float* __restrict__ bias,
+                                                      float* __restrict__ y, int M, int Co, int K, const ConvGeom cv,
+                                                      int act, float alpha) {
+    __shared__ __align__(16) float xs[DC_PIX][DC_MAXK];
+    __shared__ int kdy[DC_MAXK], kdx[DC_MAXK], kci[DC_MAXK];  // per reduction index: input row / column offset, channel
+    __shared__ int pb[DC_PIX], py[DC_PIX], px[DC_PIX];        // per pixel of the tile: image, top row, left column
+    const int g = blockIdx.y, cog = cv.cog, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hw = cv.Ho * cv.Wo;
+    if (threadIdx.x < DC_MAXK) {
+        const int k = threadIdx.x, tap = k / cv.cg, ci = k - tap * cv.cg, ky = tap / cv.kw, kx2 = tap - ky * cv.kw;
+        kdy[k] = ky * cv.dh;
+        kdx[k] = kx2 * cv.dw;
+        kci[k] = g * cv.cg + ci;
+    }
+    float w0[DC_MAXK], w1[DC_MAXK];
+    const int c0 = lane, c1 = lane + 32;
+#pragma unroll
+    for (int k = 0; k < DC_MAXK; k++) {
+        w0[k] = 0.0f;
+        w1[k] = 0.0f;
+        if (k < K) {
+            if (c0 < cog) {
+                const size_t src = static_cast<size_t>(g * cog + c0) * ldw + k;
+                w0[k] = __fadd_rn(__ldg(whi + src), __ldg(wlo + src));
+            }
+            if (c1 < cog) {
+                const size_t src = static_cast<size_t>(g * cog + c1) * ldw + k;
+                w1[k] = __fadd_rn(__ldg(whi + src), __ldg(wlo + src));
+            }
+        }
+    }
+    const float b0 = (bias && c0 < cog) ? __ldg(bias + g * cog + c0) : 0.0f;
+    const float b1 = (bias && c1 < cog) ? __ldg(bias + g * cog + c1) : 0.0f;
+    for (int p0 = blockIdx.x * DC_PIX; p0 < M; p0 += gridDim.x * DC_PIX) {
+        __syncthreads();  // the previous tile's inputs have been read
+        if (threadIdx.x < DC_PIX) {
+            const int m = p0 + threadIdx.x;
+            const int b = m / hw, rem = m - b * hw, oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+            pb[threadIdx.x] = b * cv.H;
+            py[threadIdx.x] = oy * cv.sh - cv.pt;
+            px[threadIdx.x] = ox * cv.sw - cv.pl;
+        }
+        __syncthreads();
+        constexpr int PER = DC_PIX * DC_MAXK / 256;  // inputs gathered per thread, all loads issued before the stores
+        float v[PER];
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+            const int i = u * 256 + threadIdx.x, p = i / DC_MAXK, k = i % DC_MAXK;
+            v[u] = 0.0f;
+            if (k < K && p0 + p < M) {
+                const int iy = py[p] + kdy[k], ix = px[p] + kdx[k];
+                if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
+                    v[u] = __ldg(x + ((static_cast<size_t>(pb[p]) + iy) * cv.W + ix) * cv.C + kci[k]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+            const int i = u * 256 + threadIdx.x;
+            xs[i / DC_MAXK][i % DC_MAXK] = v[u];
+        }
+        __syncthreads();
+        for (int p = warp; p < DC_PIX; p += 8) {
+            const int m = p0 + p;
+            if (m >= M) break;
+            float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+            for (int k4 = 0; k4 < DC_MAXK / 4; k4++) {
+                if (4 * k4 >= K) break;
+                const float4 xv = *reinterpret_cast<const float4*>(&xs[p][4 * k4]);
+                const float xk[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    a0 = __fmaf_rn(xk[e], w0[4 * k4 + e], a0);
+                    a1 = __fmaf_rn(xk[e], w1[4 * k4 + e], a1);
+                }
+            }
+            float* yr = y + static_cast<size_t>(m) * Co + g * cog;
+            if (c0 < cog) yr[c0] = epi_act<ACTC>(bias ? __fadd_rn(a0, b0) : a0, act, alpha);
+            if (c1 < cog) yr[c1] = epi_act<ACTC>(bias ? __fadd_rn(a1, b1) : a1, act, alpha);
+        }
+    }
+}
+
+int launch_conv_direct(const float* x, const float* whi, const float* wlo, int ldw, const float* bias, float* y, int m,
+                       int Co, int k, const ConvGeom& cv, int groups, int act, float alpha, cudaStream_t st) {
+    const int tiles = (m + DC_PIX - 1) / DC_PIX, cap = sm_count() * 4;  // 4 blocks of 256 threads per SM
+    dim3 grid(tiles < cap ? tiles : cap, groups);
+    switch (act_class(act)) {
+    case -1: k_conv_direct<-1><<<grid, 256, 0, st>>>(x, whi, wlo, ldw, bias, y, m, Co, k, cv, act, alpha); break;
+    case 0: k_conv_direct<0><<<grid, 256, 0, st>>>(x, whi, wlo, ldw, bias, y, m, Co, k, cv, act, alpha); break;
+    case 1: k_conv_direct<1><<<grid, 256, 0, st>>>(x, whi, wlo, ldw, bias, y, m, Co, k, cv, act, alpha); break;
+    default: k_conv_direct<ACT_GENERIC><<<grid, 256, 0, st>>>(x, whi, wlo, ldw, bias, y, m, Co, k, cv, act, alpha); break;
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 // ---------------------------------------------------------------------------- weight preparation
 // q_kn: k x n int8 row-major (in x out, the file's order) -> wq: n x ldw (K-major), zero padded
 __global__ void k_prep_i8(const int8_t* __restrict__ q, int k, int n, int8_t* __restrict__ wq, int ldw) {
@@ -1463,6 +1570,8 @@ int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, c
     if (m > INT32_MAX || k > ldw) return -1;
     const ConvGeom cv{H, W, C, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, cg, cog};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (k <= DC_MAXK && cog <= DC_MAXCO && groups <= 65535)
+        return launch_conv_direct(x, w_hi, w_lo, ldw, bias, y, static_cast<int>(m), Co, k, cv, groups, act, alpha, st);
     if (cog <= 128)
         return dispatch_f32<128, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status,
                                        st, cv, groups);
