@@ -4,7 +4,7 @@
  *   float_tensor           include/kernix.h:39-43   (row-major rows x col floats, host memory)
  *   KERNIX_ACT_*           include/kernix.h:928-942 (numbering is part of the .knx format)
  *   floats_fma_relu        include/kernix.h:990     (fused y = max(a*x + b, 0); reference name floats_fma_relu_metal)
- * The 27 general-purpose 2-D ops of the reference header are not part of this library.
+ * The reference header's 2-D tensor operations stay header-only; their GPU backend is include/kernix_gpu.h.
  */
 #ifndef KERNIX_H
 #define KERNIX_H

@@ -18,6 +18,7 @@
 
 #include "kernix_capi.h"
 #include "kernix_cuda.h"
+#include "kernix_gpu.h"
 #include "kx_inspect.h"
 #include "kernix_model.h"
 #include "kx_internal.h"
@@ -1037,7 +1038,7 @@ KERNIX_API void kernix_capi_shapes(const void* mv, int* in_nd, int* in_shape, in
 /* -------------------------------------------------------------------------------- kernix.h extras */
 KERNIX_API void float_free(float_tensor* t) {
     if (t == NULL) return;
-    free(t->tensor);
+    if (!kernix_metal_free(t->tensor)) free(t->tensor); /* backend storage goes back to its cache (kernix_gpu.h) */
     free(t);
 }
 
