@@ -559,16 +559,18 @@ struct ConvGeom {
 
 // ---- pieces shared by the one-CTA and the CTA-pair 3xTF32 kernels
 // Thread roles (448 threads): warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue, warps 6-13 A converters.
-// Converter warp cw (0..7) covers tile rows A_ROWS_PER_WARP cw .. + A_ROWS_PER_WARP - 1; per pass, lanes 8i..8i+7
-// read one row's 128 contiguous bytes (coalesced), split them, and write the 16-byte chunks to their swizzled
-// places. For a convolution each thread's rows have their output-pixel geometry computed once per tile.
+// Converter warp cw (0..7) covers tile rows 4 P cw .. 4 P cw + 4 P - 1 (P = rows per thread: A_PASSES, or
+// CM_PASSES for the 256-pixel tiles of the channel-major convolution); per pass, lanes 8i..8i+7 read one row's 128
+// contiguous bytes (coalesced), split them, and write the 16-byte chunks to their swizzled places. For a
+// convolution each thread's rows have their output-pixel geometry computed once per tile.
 constexpr int F32_THREADS = 448;
 constexpr int A_CONV_WARPS = 8;
 constexpr int A_ROWS_PER_WARP = BM / A_CONV_WARPS;  // 16
 constexpr int A_PASSES = A_ROWS_PER_WARP / 4;       // rows of one thread
-struct ARows {
-    long rbase[A_PASSES];
-    int iy0[A_PASSES], ix0[A_PASSES];
+template <int P>
+struct ARowsT {
+    long rbase[P];
+    int iy0[P], ix0[P];
 };
 
 template <bool CONV>
@@ -577,12 +579,12 @@ __device__ __forceinline__ bool a_vec_ok(const float* A, int lda, const ConvGeom
                 : (((lda & 3) == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0));
 }
 
-template <bool CONV>
-__device__ __forceinline__ void a_rows_setup(ARows& g, const ConvGeom& cv, int m0, int cw, int lane) {
+template <bool CONV, int P>
+__device__ __forceinline__ void a_rows_setup(ARowsT<P>& g, const ConvGeom& cv, int m0, int cw, int lane) {
     if constexpr (CONV) {
 #pragma unroll
-        for (int it = 0; it < A_PASSES; it++) {
-            const int gm = m0 + cw * A_ROWS_PER_WARP + it * 4 + (lane >> 3);
+        for (int it = 0; it < P; it++) {
+            const int gm = m0 + cw * 4 * P + it * 4 + (lane >> 3);
             const int hw = cv.Ho * cv.Wo;
             const int b = gm / hw, rem = gm - b * hw, oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
             g.rbase[it] = static_cast<long>(b) * cv.H;
@@ -593,10 +595,10 @@ __device__ __forceinline__ void a_rows_setup(ARows& g, const ConvGeom& cv, int m
 }
 
 // K block [k0, k0 + 32) of this warp's 32 rows (tile origin m0): load into registers (zero outside A)
-template <bool CONV>
+template <bool CONV, int P>
 __device__ __forceinline__ void a_load_block(const float* __restrict__ A, int lda, bool vec, const ConvGeom& cv,
-                                             const ARows& g, int M, int K, int m0, int cw, int lane, int k0,
-                                             float4 (&v)[A_PASSES]) {
+                                             const ARowsT<P>& g, int M, int K, int m0, int cw, int lane, int k0,
+                                             float4 (&v)[P]) {
     const int gk = k0 + (lane & 7) * 4;
     int ky = 0, kx2 = 0, ci = 0;
     if (CONV && gk < K) {
@@ -606,8 +608,8 @@ __device__ __forceinline__ void a_load_block(const float* __restrict__ A, int ld
         kx2 = tap - ky * cv.kw;
     }
 #pragma unroll
-    for (int it = 0; it < A_PASSES; it++) {
-        const int gm = m0 + cw * A_ROWS_PER_WARP + it * 4 + (lane >> 3);
+    for (int it = 0; it < P; it++) {
+        const int gm = m0 + cw * 4 * P + it * 4 + (lane >> 3);
         float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
         if (gm < M && gk < K) {
             if (!CONV) {
@@ -643,10 +645,11 @@ __device__ __forceinline__ void a_load_block(const float* __restrict__ A, int ld
 }
 
 // split the loaded block into hi / lo and store both into the stage's swizzled A tiles
-__device__ __forceinline__ void a_store_block(const float4 (&v)[A_PASSES], int cw, int lane, uint8_t* hi, uint8_t* lo) {
+template <int P>
+__device__ __forceinline__ void a_store_block(const float4 (&v)[P], int cw, int lane, uint8_t* hi, uint8_t* lo) {
 #pragma unroll
-    for (int it = 0; it < A_PASSES; it++) {
-        const int r = cw * A_ROWS_PER_WARP + it * 4 + (lane >> 3);
+    for (int it = 0; it < P; it++) {
+        const int r = cw * 4 * P + it * 4 + (lane >> 3);
         const int j = lane & 7;
         const int off = r * 128 + ((j ^ (r & 7)) << 4);
         float4 h, l;
@@ -675,29 +678,33 @@ constexpr int A_L2_AHEAD = 5;  // K blocks between the L2 prefetch of a block an
 // The converter warps' loop. Blocks kb + 1 and kb + 2 are in flight into registers (three rotating buffers, no
 // register copies) while block kb waits for its stage and is split and stored, and (dense A) block
 // kb + A_L2_AHEAD is requested into L2, so the load latency of A is hidden behind two stages. `arrive(s)` signals
-// that stage s holds this warp's rows.
-template <bool CONV, int BK, int STAGES, class StageA, class Arrive>
+// that stage s holds this warp's rows. P: rows per thread (the tile has 32 P rows). LATE: request block kb + 2
+// after block kb has been stored and fenced instead of before, so that the fence, which may wait for this thread's
+// outstanding loads, finds the loads of one step earlier.
+template <bool CONV, int BK, int STAGES, int P = A_PASSES, bool LATE = false, class StageA, class Arrive>
 __device__ __forceinline__ void a_convert_loop(const float* __restrict__ A, int lda, const ConvGeom& cv, int M, int K,
                                                int m0, int cw, int lane, int nk, SmemCtl* ctl, volatile int* abort_flag,
                                                int* status, StageA stage_a, Arrive arrive) {
     const bool vec = a_vec_ok<CONV>(A, lda, cv);
-    ARows g;
-    a_rows_setup<CONV>(g, cv, m0, cw, lane);
+    static_assert(CONV || P == A_PASSES, "the L2 prefetch of dense A covers A_PASSES rows per thread");
+    ARowsT<P> g;
+    a_rows_setup<CONV, P>(g, cv, m0, cw, lane);
     if constexpr (!CONV)
         for (int j = 2; j < A_L2_AHEAD; j++) a_prefetch_block(A, lda, M, K, m0, cw, lane, j * BK);
-    float4 va[A_PASSES], vb[A_PASSES], vc[A_PASSES];
-    a_load_block<CONV>(A, lda, vec, cv, g, M, K, m0, cw, lane, 0, va);
-    if (nk > 1) a_load_block<CONV>(A, lda, vec, cv, g, M, K, m0, cw, lane, BK, vb);
+    float4 va[P], vb[P], vc[P];
+    a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, 0, va);
+    if (nk > 1) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, BK, vb);
     // block kb from `cur`; block kb + 2 into `ahead`; false on a timeout
-    auto step = [&](int kb, float4 (&cur)[A_PASSES], float4 (&ahead)[A_PASSES]) {
+    auto step = [&](int kb, float4 (&cur)[P], float4 (&ahead)[P]) {
         const int s = kb % STAGES;
         if constexpr (!CONV) a_prefetch_block(A, lda, M, K, m0, cw, lane, (kb + A_L2_AHEAD) * BK);
-        if (kb + 2 < nk) a_load_block<CONV>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
+        if (!LATE && kb + 2 < nk) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
         if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) return false;
-        a_store_block(cur, cw, lane, stage_a(s), stage_a(s) + BM * BK * 4);
+        a_store_block<P>(cur, cw, lane, stage_a(s), stage_a(s) + 4 * P * A_CONV_WARPS * BK * 4);
         kx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) arrive(s);
+        if (LATE && kb + 2 < nk) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
         return true;
     };
     for (int kb = 0; kb < nk; kb += 3) {
@@ -917,6 +924,152 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
                                  n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
                                  reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part);
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ 3xTF32 convolution, channel-major tiles
+// For at most 128 output channels per group the row-major tiles above leave most of each MMA's columns empty (a
+// 64-channel layer fills 64 of a 128-column tile) while a tcgen05.mma costs about the same time at N = 128 as at
+// N = 256 (measured), so here the operands swap roles: D^T = W . X^T, the group's weight rows (output channels,
+// padded to 128 by the TMA's zero fill) are the A operand and 256 gathered output pixels the B operand, one
+// M = 128 x N = 256 MMA per 8 K and product. TMEM lane c holds channel c, column p pixel p: Ah.Bh in columns
+// [0, 256), the cross terms in [256, 512). 320 threads: warp 0 TMA (weights), warp 1 MMA, warps 2-9 convert 32
+// pixel rows each (no separate epilogue warps, which leaves each converter thread the registers for its 8 rows);
+// after the last MMA the converter warps are the epilogue, two per TMEM lane quarter sharing its 32-pixel column
+// blocks, and lane c stores channel c of each pixel, so every store instruction writes a pixel's 32 consecutive
+// channels (128 bytes). Reductions of at most DRAIN_MIN_K only (no chunk draining).
+constexpr int CM_NP = 256;                              // output pixels per tile
+constexpr int CM_THREADS = 64 + 32 * A_CONV_WARPS;
+constexpr int CM_PASSES = CM_NP / A_CONV_WARPS / 4;      // pixel rows per converter thread
+struct CmCfg {
+    static constexpr int BK = 32;
+    static constexpr int STAGES = 2;
+    static constexpr int W_BYTES = BM * BK * 4;         // 128 weight rows of one plane
+    static constexpr int X_BYTES = CM_NP * BK * 4;      // 256 pixel rows of one plane
+    static constexpr int STAGE_BYTES = 2 * W_BYTES + 2 * X_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + F32_CTL_BYTES;
+    static constexpr uint32_t MAIN0 = 0, CROSS = CM_NP, TMEM_COLS = 2 * CM_NP;
+};
+
+template <int ACTC>
+__global__ void __launch_bounds__(CM_THREADS, 1)
+k_conv_tf32x3_cm(const float* __restrict__ X, const __grid_constant__ CUtensorMap tmWhi,
+                 const __grid_constant__ CUtensorMap tmWlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
+                 int M, int K, int act, float alpha, int* status, const ConvGeom cv) {
+    using C = CmCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + C::STAGES * C::STAGE_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    auto sWhi = [&](int s) { return smem + s * C::STAGE_BYTES; };
+    auto sWlo = [&](int s) { return smem + s * C::STAGE_BYTES + C::W_BYTES; };
+    auto sXhi = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::W_BYTES; };
+    auto sXlo = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::W_BYTES + C::X_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * CM_NP;
+    const int nk = (K + C::BK - 1) / C::BK;
+    const int grp = static_cast<int>(blockIdx.y);
+    const int wrow0 = grp * cv.cog;  // first weight row / output channel of this group
+    X += grp * cv.cg;
+    y += wrow0;
+    if (bias) bias += wrow0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1 + A_CONV_WARPS);  // TMA producer + the converter warps
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        kx::tmem_alloc(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish();
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmWhi);
+            kx::tma_prefetch_desc(&tmWlo);
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % C::STAGES;
+                if (!kx::mbar_wait(&ctl->empty[s], ((kb / C::STAGES) & 1) ^ 1, abort_flag, status)) break;
+                kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * C::W_BYTES);
+                kx::tma_load_2d(sWhi(s), &tmWhi, kb * C::BK, wrow0, &ctl->full[s]);
+                kx::tma_load_2d(sWlo(s), &tmWlo, kb * C::BK, wrow0, &ctl->full[s]);
+                issued = kb + 1;
+            }
+            if (*abort_flag)
+                for (int kb = issued > C::STAGES ? issued - C::STAGES : 0; kb < issued; kb++)
+                    drain_wait(&ctl->full[kb % C::STAGES], (kb / C::STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = kx::idesc_tf32(BM, CM_NP);
+            const uint32_t d = tmem + C::MAIN0, dx = tmem + C::CROSS;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % C::STAGES;
+                if (!kx::mbar_wait(&ctl->full[s], (kb / C::STAGES) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t wh = kx::smem_u32(sWhi(s)), wl = kx::smem_u32(sWlo(s));
+                const uint32_t xh = kx::smem_u32(sXhi(s)), xl = kx::smem_u32(sXlo(s));
+#pragma unroll
+                for (int kk = 0; kk < C::BK / 8; kk++) {
+                    const uint32_t o = kk * 32;  // 8 tf32 = 32 bytes of K per MMA
+                    kx::mma_tf32(dx, kx::desc_sw128_kmajor(wl + o), kx::desc_sw128_kmajor(xh + o), idesc, (kb | kk) != 0);
+                    kx::mma_tf32(dx, kx::desc_sw128_kmajor(wh + o), kx::desc_sw128_kmajor(xl + o), idesc, 1);
+                    kx::mma_tf32(d, kx::desc_sw128_kmajor(wh + o), kx::desc_sw128_kmajor(xh + o), idesc, (kb | kk) != 0);
+                }
+                kx::mma_commit(&ctl->empty[s]);
+            }
+            kx::mma_commit(&ctl->accf);
+        }
+        __syncwarp();
+    } else {
+        a_convert_loop<true, C::BK, C::STAGES, CM_PASSES, true>(X, 0, cv, M, K, m0, warp - 2, lane, nk, ctl, abort_flag, status,
+                                                          sXhi, [&](int s) { kx::mbar_arrive(&ctl->full[s]); });
+        // Final epilogue: warp w reads TMEM lane quarter q = w % 4 (channels 32 q .. 32 q + 31, thread = channel) and
+        // takes the quarter's 32-pixel column blocks part, part + 2, ...: (Ah.Bh + cross terms) rounded to nearest,
+        // bias, activation, then per pixel one 128-byte store of its 32 channels.
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        const int q = warp & 3, part = (warp - 2) >> 2;
+        const int ch = q * 32 + lane;
+        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+        if (ok && q * 32 < cv.cog) {
+            const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+            const bool live = ch < cv.cog;
+            const float bch = (bias && live) ? __ldg(bias + ch) : 0.0f;
+#pragma unroll 1
+            for (int c0 = 32 * part; c0 < CM_NP; c0 += 64) {
+                if (m0 + c0 >= M) break;
+                uint32_t r[32], x[32];
+                kx::tmem_ld32(tmem + lanes + C::MAIN0 + c0, r);
+                kx::tmem_ld32(tmem + lanes + C::CROSS + c0, x);
+                kx::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    float t = __fadd_rn(__uint_as_float(r[j]), __uint_as_float(x[j]));
+                    if (bias) t = __fadd_rn(t, bch);
+                    const int pix = m0 + c0 + j;
+                    if (live && pix < M) y[static_cast<size_t>(pix) * ldy + ch] = epi_act<ACTC>(t, act, alpha);
+                }
+            }
+        }
     }
     kx::tc_fence_before();
     __syncthreads();
@@ -1315,6 +1468,23 @@ int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo,
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+template <int ACTC>
+int launch_conv_cm(const float* x, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
+                   int ldy, int m, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv, int groups) {
+    using C = CmCfg;
+    CUtensorMap th, tl;
+    if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BM) != 0 ||
+        make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BM) != 0)
+        return -1;
+    auto kern = k_conv_tf32x3_cm<ACTC>;
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+    dim3 grid((m + CM_NP - 1) / CM_NP, groups);
+    kern<<<grid, CM_THREADS, C::SMEM, st>>>(x, th, tl, bias, y, ldy, m, k, act, alpha, status, cv);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 // ------------------------------------------------------------------- direct convolution, tiny K
 // For reductions of at most DC_MAXK with at most 64 output channels per group (the first 3x3 layer over RGB: K = 27,
 // 64 channels) a tensor-core tile spends its time on pipeline set-up and a whole epilogue per 32 K, so these layers run
@@ -1572,6 +1742,15 @@ int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, c
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (k <= DC_MAXK && cog <= DC_MAXCO && groups <= 65535)
         return launch_conv_direct(x, w_hi, w_lo, ldw, bias, y, static_cast<int>(m), Co, k, cv, groups, act, alpha, st);
+    if (cog <= 128 && m > BM && k <= DRAIN_MIN_K && groups <= 65535) {  // channel-major tiles
+        const int mi = static_cast<int>(m);
+        switch (act_class(act)) {
+        case -1: return launch_conv_cm<-1>(x, w_hi, w_lo, ldw, Co, bias, y, Co, mi, k, act, alpha, status, st, cv, groups);
+        case 0: return launch_conv_cm<0>(x, w_hi, w_lo, ldw, Co, bias, y, Co, mi, k, act, alpha, status, st, cv, groups);
+        case 1: return launch_conv_cm<1>(x, w_hi, w_lo, ldw, Co, bias, y, Co, mi, k, act, alpha, status, st, cv, groups);
+        default: return launch_conv_cm<ACT_GENERIC>(x, w_hi, w_lo, ldw, Co, bias, y, Co, mi, k, act, alpha, status, st, cv, groups);
+        }
+    }
     if (cog <= 128)
         return dispatch_f32<128, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status,
                                        st, cv, groups);

@@ -259,11 +259,22 @@ def test_gemm_f32_skinny(kx, m, k, n, act):
     dict(B=2, H=8, W=8, C=128, Co=256, k=3, s=1, d=1, p=1, g=1),
     dict(B=5, H=8, W=8, C=128, Co=256, k=3, s=1, d=1, p=1, g=1),
     dict(B=4, H=12, W=12, C=32, Co=48, k=3, s=1, d=1, p=1, g=2),
+    # channel-major tiles (at most 128 channels per group, more than 128 pixels, K <= 2048)
+    dict(B=2, H=32, W=32, C=64, Co=64, k=3, s=1, d=1, p=1, g=1, a=1),
+    dict(B=4, H=16, W=16, C=32, Co=100, k=3, s=1, d=1, p=1, g=1),
+    dict(B=3, H=11, W=13, C=6, Co=64, k=3, s=1, d=1, p=1, g=1, a=-1),
+    dict(B=2, H=20, W=20, C=64, Co=128, k=3, s=2, d=1, p=1, g=1),
+    dict(B=2, H=16, W=16, C=64, Co=64, k=3, s=1, d=1, p=1, g=4, a=1),
+    dict(B=2, H=16, W=16, C=128, Co=128, k=3, s=1, d=1, p=1, g=1),
+    dict(B=1, H=30, W=30, C=16, Co=8, k=5, s=1, d=1, p=2, g=1),
+    # K = 2304 > 2048 with 64 channels: drained CTA-pair tiles
+    dict(B=3, H=8, W=8, C=256, Co=64, k=3, s=1, d=1, p=1, g=1),
 ])
 def test_conv_implicit_gemm(kx, cfg):
     """implicit-GEMM conv (no im2col buffer) vs the oracle's im2col + sgemm restatement of kernix_conv_run."""
     rng = np.random.default_rng(cfg["C"] * cfg["Co"])
     B, H, W, C, Co, kk, s, d, p, g = (cfg[k] for k in ("B", "H", "W", "C", "Co", "k", "s", "d", "p", "g"))
+    act = cfg.get("a", 0)
     Ho = (H + 2 * p - d * (kk - 1) - 1) // s + 1
     Wo = (W + 2 * p - d * (kk - 1) - 1) // s + 1
     x = rng.standard_normal((B * H * W, C)).astype(F32)
@@ -275,10 +286,10 @@ def test_conv_implicit_gemm(kx, cfg):
     st = status()
     db = dev(b)
     kx.call("kx_conv_f32", dev(x).data_ptr(), hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y.data_ptr(), B, H, W, C, Co,
-            Ho, Wo, kk, kk, s, s, d, d, p, p, g, 0, 0.0, st.data_ptr(), sp())
+            Ho, Wo, kk, kk, s, s, d, d, p, p, g, act, 0.0, st.data_ptr(), sp())
     got = host(y)
     check_status(st)
-    step = dict(kind=ko.OP["CONV"], act=0, alpha=0.0, groups=g, kh=kk, kw=kk, sh=s, sw=s, dh=d, dw=d, pt=p, pb=p, pl=p, pr=p,
+    step = dict(kind=ko.OP["CONV"], act=act, alpha=0.0, groups=g, kh=kk, kw=kk, sh=s, sw=s, dh=d, dw=d, pt=p, pb=p, pl=p, pr=p,
                 w=("f32", w), bias=b)
     want = ko.conv(step, ko._val([H, W, C]), ko._val([Ho, Wo, Co]), x)
     assert rel_err(got, want) <= 1e-5
