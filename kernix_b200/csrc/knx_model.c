@@ -34,16 +34,18 @@ struct kx_model_impl {
     cudaStream_t stream;  /* kernels */
     cudaStream_t s_in;    /* host -> device copies of the host-memory forward */
     cudaStream_t s_out;   /* device -> host copies of the host-memory forward */
-    /* per piece: start / end of its input copy, kernels and output copy (timed, to choose the piece count) */
-    cudaEvent_t ev_is[KX_PIPE_MAX], ev_in[KX_PIPE_MAX], ev_cs[KX_PIPE_MAX], ev_comp[KX_PIPE_MAX];
-    cudaEvent_t ev_os[KX_PIPE_MAX], ev_out[KX_PIPE_MAX];
+    /* per piece: end of its input copy, kernels and output copy (dependencies between the three streams only:
+     * created without timing, which keeps cross-stream waits short) */
+    cudaEvent_t ev_in[KX_PIPE_MAX], ev_comp[KX_PIPE_MAX], ev_out[KX_PIPE_MAX];
+    cudaEvent_t ev_t0, ev_t1; /* start of the first input copy / end of the last output copy of the last chunk (timed,
+                               * to choose the piece count) */
     int pipe;             /* pieces per chunk when pipelining ($KERNIX_PIPELINE; default 4) */
     int pipe_fixed;       /* 1: $KERNIX_PIPELINE was given, use it as is */
     int pipe_now;         /* pieces per chunk for the current chunk size (tuned over the first calls) */
     int tune_calls;       /* calls made at the current chunk size, while tuning */
     int tune_best;        /* fastest piece count tried so far, and its span in ms */
     float tune_best_ms;
-    int last_pieces;      /* pieces of the last chunk of the last call (whose events hold its timings) */
+    int last_pieces;      /* pieces of the last chunk of the last call (0: no timed chunk yet) */
     /* workspace (one arena) */
     void* arena;
     size_t arena_bytes;
@@ -645,31 +647,29 @@ static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float
         for (int p = 0; p < P && rc == 0; p++) {
             const int a = p * q, np = n - a < q ? n - a : q;
             float* xr = xin_own + (size_t)a * in_ps;
+            /* the waits see the previous chunk's (or call's) records of this piece's events */
             rc |= cudaStreamWaitEvent(im->s_in, im->ev_comp[p], 0) != cudaSuccess;
             rc |= cudaStreamWaitEvent(im->s_in, im->ev_out[p], 0) != cudaSuccess;
-            rc |= cudaEventRecord(im->ev_is[p], im->s_in) != cudaSuccess;
+            if (p == 0) rc |= cudaEventRecord(im->ev_t0, im->s_in) != cudaSuccess;
             rc |= cudaMemcpyAsync(xr, x + (size_t)(s0 + a) * in_ps, (size_t)np * in_ps * sizeof(float),
                                   cudaMemcpyHostToDevice, im->s_in) != cudaSuccess;
             rc |= cudaEventRecord(im->ev_in[p], im->s_in) != cudaSuccess;
             rc |= cudaStreamWaitEvent(im->stream, im->ev_in[p], 0) != cudaSuccess;
             rc |= cudaStreamWaitEvent(im->stream, im->ev_out[p], 0) != cudaSuccess;
-            rc |= cudaEventRecord(im->ev_cs[p], im->stream) != cudaSuccess;
             if (rc) break;
             piece_view(im, xin_own, a, in_ps);
             rc |= chunk_run(m, np) != 0;
             rc |= cudaEventRecord(im->ev_comp[p], im->stream) != cudaSuccess;
-        }
-        for (int p = 0; p < P && rc == 0; p++) {
-            const int a = p * q, np = n - a < q ? n - a : q;
-            /* the output value of piece p: in its storage buffer at the piece's offset, or (a graph of views
-             * only) in the piece's input rows */
+            /* the piece's output copy is queued at once, so that it never waits for the host to queue the later
+             * pieces; its value is in its storage buffer at the piece's offset, or (a graph of views only) in the
+             * piece's input rows */
             const float* yp = out_st < 0 ? xin_own + (size_t)a * in_ps : im->st_base[out_st] + (size_t)a * im->g->st_cap[out_st];
             rc |= cudaStreamWaitEvent(im->s_out, im->ev_comp[p], 0) != cudaSuccess;
-            rc |= cudaEventRecord(im->ev_os[p], im->s_out) != cudaSuccess;
             rc |= cudaMemcpyAsync(out + (size_t)(s0 + a) * m->out_dim, yp, (size_t)np * m->out_dim * sizeof(float),
                                   cudaMemcpyDeviceToHost, im->s_out) != cudaSuccess;
             rc |= cudaEventRecord(im->ev_out[p], im->s_out) != cudaSuccess;
         }
+        rc |= cudaEventRecord(im->ev_t1, im->s_out) != cudaSuccess;
         im->last_pieces = P;
     }
     piece_view(im, xin_own, 0, in_ps);
@@ -688,7 +688,7 @@ static void pipe_tune(struct kx_model_impl* im) {
     const int c = im->tune_calls++; /* call c at this chunk size ran with pipe_now pieces */
     if (c >= 1 && im->last_pieces > 0) {
         float v;
-        if (cudaEventElapsedTime(&v, im->ev_is[0], im->ev_out[im->last_pieces - 1]) == cudaSuccess &&
+        if (cudaEventElapsedTime(&v, im->ev_t0, im->ev_t1) == cudaSuccess &&
             (c == 1 || v < im->tune_best_ms)) {
             im->tune_best_ms = v;
             im->tune_best = im->pipe_now;
@@ -799,10 +799,12 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
              cudaStreamCreateWithFlags(&im->s_out, cudaStreamNonBlocking) != cudaSuccess)
         why = "cannot create a CUDA stream";
     for (int i = 0; why == NULL && i < KX_PIPE_MAX; i++)
-        if (cudaEventCreate(&im->ev_is[i]) != cudaSuccess || cudaEventCreate(&im->ev_in[i]) != cudaSuccess ||
-            cudaEventCreate(&im->ev_cs[i]) != cudaSuccess || cudaEventCreate(&im->ev_comp[i]) != cudaSuccess ||
-            cudaEventCreate(&im->ev_os[i]) != cudaSuccess || cudaEventCreate(&im->ev_out[i]) != cudaSuccess)
+        if (cudaEventCreateWithFlags(&im->ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&im->ev_comp[i], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&im->ev_out[i], cudaEventDisableTiming) != cudaSuccess)
             why = "cannot create a CUDA event";
+    if (why == NULL && (cudaEventCreate(&im->ev_t0) != cudaSuccess || cudaEventCreate(&im->ev_t1) != cudaSuccess))
+        why = "cannot create a CUDA event";
     if (why == NULL && cudaHostAlloc((void**)&im->status_h, sizeof(int), cudaHostAllocDefault) != cudaSuccess)
         why = "cannot allocate host memory";
     const char* pe = getenv("KERNIX_PIPELINE");
@@ -869,10 +871,12 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
         if (im->status_h) cudaFreeHost(im->status_h);
         cudaFree(im->skinny_part);
         for (int i = 0; i < KX_PIPE_MAX; i++) {
-            cudaEvent_t* evs[6] = {im->ev_is, im->ev_in, im->ev_cs, im->ev_comp, im->ev_os, im->ev_out};
-            for (int k = 0; k < 6; k++)
+            cudaEvent_t* evs[3] = {im->ev_in, im->ev_comp, im->ev_out};
+            for (int k = 0; k < 3; k++)
                 if (evs[k][i]) cudaEventDestroy(evs[k][i]);
         }
+        if (im->ev_t0) cudaEventDestroy(im->ev_t0);
+        if (im->ev_t1) cudaEventDestroy(im->ev_t1);
         if (im->s_in) cudaStreamDestroy(im->s_in);
         if (im->s_out) cudaStreamDestroy(im->s_out);
         if (im->stream) cudaStreamDestroy(im->stream);
