@@ -31,6 +31,7 @@
 
 #include "kx_act.cuh"
 #include "kx_kernels.h"
+#include "kx_pdl.cuh"
 #include "kx_sm100.cuh"
 
 namespace {
@@ -419,6 +420,8 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     kx::cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
     kx::tc_fence_after();
     const uint32_t tmem = ctl->tmem;
+    kx::griddep_wait();  // launched as a dependent of the row quantiser: A and sx are its output
+    kx::griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -1427,8 +1430,8 @@ int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq,
     int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
     if (clusters <= 0) clusters = sm_count() / 2;
     if (clusters > tiles) clusters = tiles;
-    kern<<<2 * clusters, C::THREADS, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    return kx::launch_pdl(kern, dim3(2 * clusters), dim3(C::THREADS), C::SMEM, st, ta, tb, sx, scale, bias, y, acc, ldy, m, n,
+                          k, act, alpha, status);
 }
 
 template <int BN, bool CONV, int ACTC, bool DRAIN>

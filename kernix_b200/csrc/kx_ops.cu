@@ -10,6 +10,7 @@
 
 #include "kx_act.cuh"
 #include "kx_kernels.h"
+#include "kx_pdl.cuh"
 
 namespace {
 
@@ -48,6 +49,8 @@ constexpr int QV = 8;  // float4 per thread kept in registers (rows up to 4096 c
 
 __global__ void __launch_bounds__(QT) k_quant_rows(const float* __restrict__ x, int ldx, int k, int8_t* __restrict__ xq,
                                                    int ldq, float* __restrict__ sx) {
+    kx::griddep_wait();  // launched as a dependent of the kernel before it: x is its output
+    kx::griddep_launch_dependents();
     const long row = blockIdx.x;
     const float* xr = x + row * ldx;
     int8_t* qr = xq + row * ldq;
@@ -999,7 +1002,8 @@ int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y,
 int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream) {
     if (rows <= 0) return 0;
     if (k <= 0 || ldq < k || ldx < k) return -1;
-    k_quant_rows<<<rows, QT, 0, static_cast<cudaStream_t>(stream)>>>(x, ldx, k, xq, ldq, sx);
+    if (kx::launch_pdl(k_quant_rows, dim3(rows), dim3(QT), 0, static_cast<cudaStream_t>(stream), x, ldx, k, xq, ldq, sx) != 0)
+        return -1;
     return launch_ok();
 }
 
