@@ -618,14 +618,25 @@ static int forward_enqueue_device(kernix_model* m, const float* x, int rows, flo
     return 0;
 }
 
-/* Enqueue the forward of host rows x into host out. Each chunk is cut into up to im->pipe_now pieces; piece p's
- * host -> device copy (stream s_in), kernels (stream) and device -> host copy (s_out) are ordered by events, so
- * the copies of one piece overlap the kernels of its neighbours and the two copy directions overlap each other.
- * Piece p of every chunk reuses arena region p: its input copy waits until the last user of region p has been
- * computed and copied out, and its kernels wait for that copy-out too. Rows never mix across pieces, so the
- * result is the same for any cut (the chunking invariance of include/kernix_model.h:1691-1694). The copies of a
- * chunk's outputs are issued after all of its kernels, so a copy into pageable memory (which returns only when
- * done) does not hold back the next piece's launches. */
+/* 1 if the host buffer p is page-locked (registered or allocated by CUDA), so that copies into it are asynchronous */
+static int host_page_locked(const void* p) {
+    struct cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+/* Enqueue the forward of host rows x into host out. Each chunk is cut into up to im->pipe_now pieces; piece p's host -> device copy (stream s_in), kernels (stream) and device
+ * -> host copy (s_out) are ordered by events, so the copies of one piece overlap the kernels of its neighbours and
+ * the two copy directions overlap each other. Piece p of every chunk reuses arena region p: its input copy waits
+ * until the last user of region p has been computed and copied out, and its kernels wait for that copy-out too.
+ * Rows never mix across pieces, so the result is the same for any cut (the chunking invariance of
+ * include/kernix_model.h:1691-1694). Into page-locked memory a piece's output copy is queued right after its
+ * kernels, so that it never waits for the host to queue the later pieces; into pageable memory (a copy that returns
+ * only when done) the copies of a chunk are queued after all of its kernels, so that they do not hold back the
+ * later pieces' launches. */
 static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float* out) {
     struct kx_model_impl* im = m->impl;
     const int samples = rows / m->seq_len;
@@ -637,6 +648,7 @@ static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float
     const kx_val* vo = &im->g->vals[im->g->out_v];
     const int out_st = vo->st;
     float* const xin_own = im->xin;
+    const int eager_out = host_page_locked(out);
     int rc = 0;
     for (int s0 = 0; s0 < samples && rc == 0; s0 += chunk) {
         const int n = samples - s0 < chunk ? samples - s0 : chunk;
@@ -644,6 +656,18 @@ static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float
         while (P > 1 && (size_t)(n / P) * in_ps * sizeof(float) < KX_PIPE_MIN_BYTES) P--;
         const int q = (n + P - 1) / P;
         P = (n + q - 1) / q;
+        /* the output copy of piece p: its value is in its storage buffer at the piece's offset, or (a graph of views
+         * only) in the piece's input rows */
+        #define KX_QUEUE_OUT(p)                                                                                          \
+            do {                                                                                                         \
+                const int a_ = (p) * q, np_ = n - a_ < q ? n - a_ : q;                                                  \
+                const float* yp = out_st < 0 ? xin_own + (size_t)a_ * in_ps                                               \
+                                             : im->st_base[out_st] + (size_t)a_ * im->g->st_cap[out_st];                  \
+                rc |= cudaStreamWaitEvent(im->s_out, im->ev_comp[(p)], 0) != cudaSuccess;                                \
+                rc |= cudaMemcpyAsync(out + (size_t)(s0 + a_) * m->out_dim, yp, (size_t)np_ * m->out_dim * sizeof(float), \
+                                      cudaMemcpyDeviceToHost, im->s_out) != cudaSuccess;                                 \
+                rc |= cudaEventRecord(im->ev_out[(p)], im->s_out) != cudaSuccess;                                        \
+            } while (0)
         for (int p = 0; p < P && rc == 0; p++) {
             const int a = p * q, np = n - a < q ? n - a : q;
             float* xr = xin_own + (size_t)a * in_ps;
@@ -660,15 +684,11 @@ static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float
             piece_view(im, xin_own, a, in_ps);
             rc |= chunk_run(m, np) != 0;
             rc |= cudaEventRecord(im->ev_comp[p], im->stream) != cudaSuccess;
-            /* the piece's output copy is queued at once, so that it never waits for the host to queue the later
-             * pieces; its value is in its storage buffer at the piece's offset, or (a graph of views only) in the
-             * piece's input rows */
-            const float* yp = out_st < 0 ? xin_own + (size_t)a * in_ps : im->st_base[out_st] + (size_t)a * im->g->st_cap[out_st];
-            rc |= cudaStreamWaitEvent(im->s_out, im->ev_comp[p], 0) != cudaSuccess;
-            rc |= cudaMemcpyAsync(out + (size_t)(s0 + a) * m->out_dim, yp, (size_t)np * m->out_dim * sizeof(float),
-                                  cudaMemcpyDeviceToHost, im->s_out) != cudaSuccess;
-            rc |= cudaEventRecord(im->ev_out[p], im->s_out) != cudaSuccess;
+            if (eager_out) KX_QUEUE_OUT(p);
         }
+        if (!eager_out)
+            for (int p = 0; p < P && rc == 0; p++) KX_QUEUE_OUT(p);
+        #undef KX_QUEUE_OUT
         rc |= cudaEventRecord(im->ev_t1, im->s_out) != cudaSuccess;
         im->last_pieces = P;
     }

@@ -681,13 +681,12 @@ constexpr int A_L2_AHEAD = 5;  // K blocks between the L2 prefetch of a block an
 // The converter warps' loop. Blocks kb + 1 and kb + 2 are in flight into registers (three rotating buffers, no
 // register copies) while block kb waits for its stage and is split and stored, and (dense A) block
 // kb + A_L2_AHEAD is requested into L2, so the load latency of A is hidden behind two stages. `arrive(s)` signals
-// that stage s holds this warp's rows. P: rows per thread (the tile has 32 P rows). LATE: request block kb + 2
-// after block kb has been stored and fenced instead of before, so that the fence, which may wait for this thread's
-// outstanding loads, finds the loads of one step earlier.
-template <bool CONV, int BK, int STAGES, int P = A_PASSES, bool LATE = false, class StageA, class Arrive>
-__device__ __forceinline__ void a_convert_loop(const float* __restrict__ A, int lda, const ConvGeom& cv, int M, int K,
-                                               int m0, int cw, int lane, int nk, SmemCtl* ctl, volatile int* abort_flag,
-                                               int* status, StageA stage_a, Arrive arrive) {
+// that stage s holds this warp's rows. P: rows per thread (the tile has 32 P rows). it0: the stage-ring position
+// of block 0 (a persistent kernel's earlier tiles' blocks). False on a timeout.
+template <bool CONV, int BK, int STAGES, int P = A_PASSES, class StageA, class Arrive>
+__device__ __forceinline__ bool a_convert_loop(const float* __restrict__ A, int lda, const ConvGeom& cv, int M, int K,
+                                               int m0, int cw, int lane, int nk, int it0, SmemCtl* ctl,
+                                               volatile int* abort_flag, int* status, StageA stage_a, Arrive arrive) {
     const bool vec = a_vec_ok<CONV>(A, lda, cv);
     static_assert(CONV || P == A_PASSES, "the L2 prefetch of dense A covers A_PASSES rows per thread");
     ARowsT<P> g;
@@ -699,22 +698,24 @@ __device__ __forceinline__ void a_convert_loop(const float* __restrict__ A, int 
     if (nk > 1) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, BK, vb);
     // block kb from `cur`; block kb + 2 into `ahead`; false on a timeout
     auto step = [&](int kb, float4 (&cur)[P], float4 (&ahead)[P]) {
-        const int s = kb % STAGES;
+        const int it = it0 + kb, s = it % STAGES;
         if constexpr (!CONV) a_prefetch_block(A, lda, M, K, m0, cw, lane, (kb + A_L2_AHEAD) * BK);
-        if (!LATE && kb + 2 < nk) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
-        if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) return false;
+        if (kb + 2 < nk) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
+        if (!kx::mbar_wait(&ctl->empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, status)) return false;
         a_store_block<P>(cur, cw, lane, stage_a(s), stage_a(s) + 4 * P * A_CONV_WARPS * BK * 4);
         kx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) arrive(s);
-        if (LATE && kb + 2 < nk) a_load_block<CONV, P>(A, lda, vec, cv, g, M, K, m0, cw, lane, (kb + 2) * BK, ahead);
         return true;
     };
     for (int kb = 0; kb < nk; kb += 3) {
-        if (!step(kb, va, vc) || kb + 1 >= nk) break;
-        if (!step(kb + 1, vb, va) || kb + 2 >= nk) break;
-        if (!step(kb + 2, vc, vb)) break;
+        if (!step(kb, va, vc)) return false;
+        if (kb + 1 >= nk) break;
+        if (!step(kb + 1, vb, va)) return false;
+        if (kb + 2 >= nk) break;
+        if (!step(kb + 2, vc, vb)) return false;
     }
+    return true;
 }
 
 // DRAIN: add the finished Ah.Bh chunk at TMEM address t_chunk into the running sum at t_run (BN columns of this
@@ -910,7 +911,7 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
             }
         }
     } else {
-        a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, ctl, abort_flag, status, sAhi,
+        a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, 0, ctl, abort_flag, status, sAhi,
                                             [&](int s) { kx::mbar_arrive(&ctl->full[s]); });
     }
     if (warp >= 2) {
@@ -933,6 +934,247 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
     if (warp == 1) {
         kx::tc_fence_after();
         kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ 3xTF32, persistent CTA pairs
+// For dense layers with K <= PP_MAX_K and more 256 x 256 tiles than resident clusters: the CTA-pair kernel above,
+// made persistent so that a tile's epilogue overlaps the next tile's mainloop. A cluster walks tiles t = cluster,
+// + clusters, ... (M-tile fastest: the clusters running at once share B tiles in L2); the TMA producer and the
+// converters run ahead through the 3-stage ring across tile boundaries, and TMEM holds two 256-column accumulators
+// (one per tile in flight), so the three products of a tile (Ah.Bh, Al.Bh, Ah.Bl) share one accumulator instead of
+// keeping the cross terms apart: with the truncating accumulation of tcgen05 that costs ~6e-6 of the output scale
+// at K = 1024 (~3e-6 at K = 512), inside the 1e-5 bound of the other 3xTF32 paths. The four epilogue warps of each
+// CTA drain a tile (the next tile's bias columns fetched into registers a tile ahead, then copied into the warp's own
+// shared-memory buffer, so that no barrier joins the warps; 32x32 blocks staged through a 4 KB per-warp buffer;
+// full-row stores) and free its accumulator on rank 0's acc_empty.
+constexpr int PP_MAX_K = 1024;
+struct PpCfg {
+    static constexpr int BN = 256;
+    static constexpr int BK = 32;
+    static constexpr int STAGES = 3;
+    static constexpr int A_BYTES = BM * BK * 4;
+    static constexpr int B_BYTES = (BN / 2) * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STG_BYTES = 4096;  // per epilogue warp
+    static constexpr int BIAS_BYTES = 2 * BN * 4;  // per epilogue warp: two tiles' bias columns
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + F32_CTL_BYTES + 4 * BIAS_BYTES + 4 * STG_BYTES;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+};
+
+// one warp's 32 rows of a finished tile (thread = row row0 + lane): accumulator + bias, activation, 32-column blocks
+// staged through the warp's 4 KB buffer `stg` and written as full 128-byte row segments
+template <int ACTC>
+__device__ __forceinline__ void pp_store_tile(uint32_t t_acc, int row0, int lane, int n0, const float* sbias, bool has_bias,
+                                              float* __restrict__ y, int ldy, int M, int N, int act, float alpha, float4* stg) {
+    constexpr int BN = PpCfg::BN;
+    const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        kx::tmem_ld32(t_acc + c0, r);
+        kx::tmem_ld_wait();
+        const int col0 = n0 + c0;
+        if (col0 >= N) break;
+        __syncwarp();  // the previous block's reads of stg are done
+#pragma unroll
+        for (int j4 = 0; j4 < 8; j4++) {
+            const float4 b4 = reinterpret_cast<const float4*>(sbias)[(c0 >> 2) + j4];
+            const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float t = __uint_as_float(r[4 * j4 + e]);
+                if (has_bias) t = __fadd_rn(t, bb[e]);
+                v[e] = epi_act<ACTC>(t, act, alpha);
+            }
+            stg[lane * 8 + (j4 ^ (lane & 7))] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        __syncwarp();
+        const int q = lane & 7, gcol = col0 + 4 * q;
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            const int rr = 4 * p + (lane >> 3), grow = row0 + rr;
+            const float4 w = stg[rr * 8 + (q ^ (rr & 7))];
+            if (grow >= M || gcol >= N) continue;
+            float* dst = y + static_cast<size_t>(grow) * ldy + gcol;
+            if (vec && gcol + 3 < N) {
+                *reinterpret_cast<float4*>(dst) = w;
+            } else {
+                dst[0] = w.x;
+                if (gcol + 1 < N) dst[1] = w.y;
+                if (gcol + 2 < N) dst[2] = w.z;
+                if (gcol + 3 < N) dst[3] = w.w;
+            }
+        }
+    }
+}
+
+template <int ACTC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F32_THREADS, 1)
+k_gemm_tf32x3_pp(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
+                 const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
+                 int M, int N, int K, int act, float alpha, int* status) {
+    using C = PpCfg;
+    constexpr int BN = C::BN, STAGES = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);  // the same offset in both CTAs (same kernel, same static layout)
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + STAGES * C::STAGE_BYTES);
+    float* sbias_all = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + F32_CTL_BYTES);  // 4 warps x 2 x BN
+    float4* stg_all = reinterpret_cast<float4*>(sbias_all + 4 * 2 * BN);                           // 4 warps x 4 KB
+    volatile int* abort_flag = &ctl->abort;
+    auto sAhi = [&](int s) { return smem + s * C::STAGE_BYTES; };
+    auto sAlo = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto sBhi = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::A_BYTES; };
+    auto sBlo = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = kx::cluster_ctarank();
+    const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    const int nk = (K + C::BK - 1) / C::BK;
+    const TileMap tm{(M + 2 * BM - 1) / (2 * BM), (N + BN - 1) / BN};
+    const int n_tiles = tm.m_tiles * tm.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1 + 2 * A_CONV_WARPS);  // rank 0's producer + the converter warps of both CTAs
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            kx::mbar_init(&ctl->acc_full[b], 1);
+            kx::mbar_init(&ctl->acc_empty[b], 8);  // the epilogue warps of both CTAs
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {  // warp 1 of both CTAs, same destination offset
+        kx::tmem_alloc_pair(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish_pair();
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+    const uint32_t full0 = kx::mapa(kx::smem_u32(&ctl->full[0]), 0);  // rank 0's full[0]; full[s] = + 8 s
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmBhi);
+            kx::tma_prefetch_desc(&tmBlo);
+            int it = 0;
+            for (int t = cluster; t < n_tiles && !*abort_flag; t += n_clusters) {
+                int mt, nt;
+                tm.at(t, mt, nt);
+                const int brow = nt * BN + static_cast<int>(rank) * (BN / 2);
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                    if (rank == 0) kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * 2 * C::B_BYTES);
+                    const uint32_t bar = full0 + 8u * static_cast<uint32_t>(s);
+                    kx::tma_load_2d_pair(sBhi(s), &tmBhi, kb * C::BK, brow, bar);
+                    kx::tma_load_2d_pair(sBlo(s), &tmBlo, kb * C::BK, brow, bar);
+                }
+            }
+            if (*abort_flag && rank == 0)  // the stages armed here also carry the peer's copies
+                for (int i = it > STAGES ? it - STAGES : 0; i < it; i++) drain_wait(&ctl->full[i % STAGES], (i / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = kx::idesc_tf32(2 * BM, BN);
+            int it = 0, j = 0;
+            for (int t = cluster; t < n_tiles && !*abort_flag; t += n_clusters, j++) {
+                const int b = j & 1;
+                if (!kx::mbar_wait(&ctl->acc_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                bool ok = true;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->full[s], (it / STAGES) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    kx::tc_fence_after();
+                    const uint32_t ah = kx::smem_u32(sAhi(s)), al = kx::smem_u32(sAlo(s));
+                    const uint32_t bh = kx::smem_u32(sBhi(s)), bl = kx::smem_u32(sBlo(s));
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 8; kk++) {
+                        const uint32_t o = kk * 32;
+                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
+                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
+                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                    }
+                    const uint32_t e = kx::smem_u32(&ctl->empty[s]);
+                    kx::mma_commit_pair(e);
+                    kx::mma_commit_pair(kx::mapa(e, 1));
+                }
+                if (!ok) break;
+                const uint32_t f = kx::smem_u32(&ctl->acc_full[b]);
+                kx::mma_commit_pair(f);
+                kx::mma_commit_pair(kx::mapa(f, 1));
+            }
+            kx::mma_commit_pair(kx::smem_u32(&ctl->accf));  // completes once every MMA issued above has finished
+            drain_wait(&ctl->accf, 0);
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        const int ew = warp - 2, q = warp & 3;
+        const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+        float4* stg = stg_all + ew * (C::STG_BYTES / 16);
+        float* sbias = sbias_all + ew * 2 * BN;
+        const uint32_t acc_empty0 = kx::mapa(kx::smem_u32(&ctl->acc_empty[0]), 0);
+        const int bc = 8 * lane;  // the eight bias columns this lane fetches
+        auto fetch_bias = [&](int t, float (&v)[8]) {
+            int mt, nt;
+            tm.at(t, mt, nt);
+            const int c = nt * BN + bc;
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = (bias && c + e < N) ? __ldg(bias + c + e) : 0.0f;
+        };
+        float bcur[8], bnext[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) bcur[e] = bnext[e] = 0.0f;
+        if (cluster < n_tiles) fetch_bias(cluster, bcur);
+        int j = 0;
+        for (int t = cluster; t < n_tiles; t += n_clusters, j++) {
+            int mt, nt;
+            tm.at(t, mt, nt);
+            const int b = j & 1;
+            if (t + n_clusters < n_tiles) fetch_bias(t + n_clusters, bnext);
+            float* sb = sbias + b * BN;
+            reinterpret_cast<float4*>(sb + bc)[0] = make_float4(bcur[0], bcur[1], bcur[2], bcur[3]);
+            reinterpret_cast<float4*>(sb + bc)[1] = make_float4(bcur[4], bcur[5], bcur[6], bcur[7]);
+            __syncwarp();  // the tile's bias columns are in this warp's buffer
+            if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
+            kx::tc_fence_after();
+            pp_store_tile<ACTC>(tmem + lanes + b * BN, mt * 2 * BM + static_cast<int>(rank) * BM + q * 32, lane, nt * BN, sb,
+                                bias != nullptr, y, ldy, M, N, act, alpha, stg);
+#pragma unroll
+            for (int e = 0; e < 8; e++) bcur[e] = bnext[e];
+            kx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) kx::mbar_arrive_remote(acc_empty0 + 8u * static_cast<uint32_t>(b));
+        }
+    } else {
+        const int cw = warp - 6;
+        int j = 0;
+        for (int t = cluster; t < n_tiles && !*abort_flag; t += n_clusters, j++) {
+            int mt, nt;
+            tm.at(t, mt, nt);
+            const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM;
+            if (!a_convert_loop<false, C::BK, STAGES>(A, lda, ConvGeom{}, M, K, m0, cw, lane, nk, j * nk, ctl, abort_flag,
+                                                      status, sAhi,
+                                                      [&](int s) { kx::mbar_arrive_remote(full0 + 8u * static_cast<uint32_t>(s)); }))
+                break;
+        }
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc_pair(tmem, C::TMEM_COLS);
     }
 }
 
@@ -1043,7 +1285,7 @@ k_conv_tf32x3_cm(const float* __restrict__ X, const __grid_constant__ CUtensorMa
         }
         __syncwarp();
     } else {
-        a_convert_loop<true, C::BK, C::STAGES, CM_PASSES, true>(X, 0, cv, M, K, m0, warp - 2, lane, nk, ctl, abort_flag, status,
+        a_convert_loop<true, C::BK, C::STAGES, CM_PASSES>(X, 0, cv, M, K, m0, warp - 2, lane, nk, 0, ctl, abort_flag, status,
                                                           sXhi, [&](int s) { kx::mbar_arrive(&ctl->full[s]); });
         // Final epilogue: warp w reads TMEM lane quarter q = w % 4 (channels 32 q .. 32 q + 31, thread = channel) and
         // takes the quarter's 32-pixel column blocks part, part + 2, ...: (Ah.Bh + cross terms) rounded to nearest,
@@ -1235,7 +1477,7 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
             }
         }
     } else {
-        a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, ctl, abort_flag, status, sAhi,
+        a_convert_loop<CONV, C::BK, STAGES>(A, lda, cv, M, K, m0, warp - 6, lane, nk, 0, ctl, abort_flag, status, sAhi,
                                             [&](int s) { kx::mbar_arrive_remote(full0 + 8u * static_cast<uint32_t>(s)); });
     }
     if (warp >= 2) {
@@ -1471,6 +1713,28 @@ int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo,
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+// persistent CTA-pair 3xTF32 launch: 1 (nothing launched) when the tiles fit in one wave of clusters, where the
+// one-tile-per-cluster kernel (with its separate cross-term accumulator) costs the same
+template <int ACTC>
+int launch_f32_pp(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
+                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st) {
+    using C = PpCfg;
+    auto kern = k_gemm_tf32x3_pp<ACTC>;
+    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + C::BN - 1) / C::BN);
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+    int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), F32_THREADS, C::SMEM);
+    if (clusters <= 0) clusters = sm_count() / 2;
+    if (tiles <= clusters) return 1;
+    CUtensorMap th, tl;
+    if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, C::BN / 2) != 0 ||
+        make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, C::BN / 2) != 0)
+        return -1;
+    kern<<<2 * clusters, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 template <int ACTC>
 int launch_conv_cm(const float* x, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                    int ldy, int m, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv, int groups) {
@@ -1683,6 +1947,16 @@ int dispatch_f32(const float* x, int ldx, const float* whi, const float* wlo, in
                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
                  int groups) {
     const bool pair = m > BM;
+    if (!CONV && BN == 256 && pair && k <= PP_MAX_K) {  // persistent CTA pairs when there is more than one wave
+        int r;
+        switch (act_class(act)) {
+        case -1: r = launch_f32_pp<-1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st); break;
+        case 0: r = launch_f32_pp<0>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st); break;
+        case 1: r = launch_f32_pp<1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st); break;
+        default: r = launch_f32_pp<ACT_GENERIC>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st);
+        }
+        if (r <= 0) return r;
+    }
     if (k > DRAIN_MIN_K)
         return pair ? launch_f32_act<128, CONV, true, true>(KX_F32_ARGS) : launch_f32_act<128, CONV, true, false>(KX_F32_ARGS);
     return pair ? launch_f32_act<BN, CONV, false, true>(KX_F32_ARGS) : launch_f32_act<BN, CONV, false, false>(KX_F32_ARGS);

@@ -227,6 +227,31 @@ def test_gemm_f32_3xtf32(kx, m, k, n, act):
     assert rel_err(got, ref) <= 1e-5
 
 
+@pytest.mark.parametrize("m,k,n,act", [(4096, 512, 1536, 0), (5000, 1000, 2500, -1), (20000, 100, 1024, 0),
+                                       (4352, 1024, 2304, -1)])
+def test_gemm_f32_persistent_pairs(kx, m, k, n, act):
+    """More 256 x 256 tiles than resident CTA pairs and K <= 1024: the persistent CTA-pair kernel (each cluster walks
+    several tiles, a tile's epilogue overlapping the next tile's mainloop, ragged M, N and K), within the same 1e-5
+    bound as the other 3xTF32 paths although its three products share one accumulator."""
+    rng = np.random.default_rng(m + k + n)
+    x = rng.standard_normal((m, k)).astype(F32)
+    w = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(F32)
+    b = rng.standard_normal(n).astype(F32)
+    hi, lo, ldw = _prep_f32(kx, w)
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    st = status()
+    db = dev(b)
+    for _ in range(2):  # twice: the second call reuses the cached launch state
+        kx.call("kx_gemm_f32", dev(x).data_ptr(), k, hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y.data_ptr(), n, m, n,
+                k, act, 0.0, st.data_ptr(), sp())
+        got = host(y)
+        check_status(st)
+        ref = x.astype(np.float64) @ w.astype(np.float64) + b
+        if act == 0:
+            ref = np.maximum(ref, 0)
+        assert rel_err(got, ref) <= 1e-5
+
+
 @pytest.mark.parametrize("m,k,n,act", [(1, 8192, 16384, 0), (5, 1000, 300, -1), (16, 4096, 2050, 0), (3, 77, 9, -1),
                                       (9, 16384, 1024, 0), (8, 300, 4096, 4)])
 def test_gemm_f32_skinny(kx, m, k, n, act):

@@ -147,19 +147,30 @@ def test_pipelined_host_forward_is_cut_invariant(Model, model_dir, monkeypatch, 
         outs.append(got)
         assert np.array_equal(m(x), got)  # second call into the same arena
         m.close()
-    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
 
 
-def test_piece_count_tuning_keeps_results(Model, model_dir, monkeypatch):
+def test_piece_count_tuning_keeps_results(Model, libkx, model_dir, monkeypatch):
     """Without $KERNIX_PIPELINE the first calls at a chunk size try 1, 2, 3, 4, 6 and 8 pieces and keep the
-    fastest: every call, during and after the tuning, returns bitwise the same rows."""
+    fastest: every call, during and after the tuning, returns bitwise the same rows, into pageable memory (output
+    copies queued after a chunk's kernels) and into page-locked memory (each piece's copy queued after its own)."""
     from kernix_b200 import configs
     monkeypatch.delenv("KERNIX_PIPELINE", raising=False)
     x = configs.inputs("c2", 1000)
     m = Model(cfg_path("c2", model_dir))
     first = m(x)
-    for _ in range(9):
+    for _ in range(12):
         assert np.array_equal(m(x), first)
+    m.close()
+    xp = torch.from_numpy(x).pin_memory()
+    op = torch.empty(first.shape, dtype=torch.float32).pin_memory()
+    m = Model(cfg_path("c2", model_dir))
+    fwd = libkx.kernix_capi_forward
+    fwd.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    fwd.restype = ctypes.c_int
+    for _ in range(13):
+        assert fwd(m._h, xp.data_ptr(), x.shape[0], op.data_ptr()) == 0
+        assert np.array_equal(op.numpy(), first)
     m.close()
 
 
