@@ -134,6 +134,16 @@ KERNIX_API int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo,
                 int W, int C, int Co, int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl,
                 int groups, int act, float alpha, int* status, void* stream);
 
+/* kx_conv_f32 with caller scratch ws of ws_floats floats (16-byte aligned): when the convolution has stride 1, a
+ * multiple of 32 input channels and at most 128 output channels per group, K <= 2048, and output images whose
+ * pixels cut into 256-pixel tiles of whole rows or whole images, x is split once into tf32 hi / lo planes in ws
+ * (2 * B*H*W*C floats) and the pixel operand is loaded by the TMA as 4-D boxes (zero fill = padding) instead of
+ * being gathered by threads; otherwise, or with too little scratch, it is kx_conv_f32. Same results within the
+ * 3xTF32 bound (the same products in another order). Same role as kx_conv_f32 (kernix_conv_run :662-771). */
+KERNIX_API int kx_conv_f32_ws(const float* x, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y, int B,
+                   int H, int W, int C, int Co, int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl,
+                   int groups, int act, float alpha, float* ws, size_t ws_floats, int* status, void* stream);
+
 /* scaled dot-product attention per (sample, head): ctx = softmax(scale * Q K^T [+ causal -inf]) V with
  * scale = 1/sqrt(dk) (kernix_attention_run :1015-1046). q: (B*Rq) rows of H*dk at leading dim ldq, k: (B*S) rows
  * of H*dk (ldk), v: (B*S) rows of H*dv (ldv), ctx: (B*Rq) rows of H*dv (ldc). Rq, S <= 128 with head dims <= 64

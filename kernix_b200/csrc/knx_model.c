@@ -195,6 +195,12 @@ static int conv_pointwise(const kx_step* s) {
 
 static int conv_depthwise(const kx_step* s) { return s->groups > 1 && s->in / s->groups == 1; }
 
+/* convolutions that kx_conv_f32_ws may run from tf32 planes of their input (scratch: two copies of the input) */
+static int conv_planes(const kx_step* s) {
+    return s->kind == KERNIX_OP_CONV && !conv_depthwise(s) && !(s->groups == 1 && conv_pointwise(s)) && s->sh == 1 &&
+           s->sw == 1 && s->groups >= 1 && (s->in / s->groups) % 32 == 0 && s->out / s->groups <= 128;
+}
+
 /* device copies of one step's parameters, in the layouts the kernels want */
 static int step_upload(kx_graph* g, kx_step* s, cudaStream_t st) {
     switch (s->kind) {
@@ -287,6 +293,8 @@ static size_t step_scratch(const kx_graph* g, const kx_step* s, size_t* per_samp
         const size_t T = (size_t)vi->r, u = (size_t)s->out, gu = rnn_gates(s->kind) * u;
         *per_sample = (T * gu + 3 * u + (s->dirs == 2 && s->merge != 0 ? (s->ret_seq ? T : 1) * u : 0)) * sizeof(float) +
                       4 * KX_ALIGN;
+    } else if (conv_planes(s)) { /* tf32 hi / lo planes of the input */
+        *per_sample = 2 * (size_t)vi->r * (size_t)vi->c * sizeof(float) + KX_ALIGN;
     } else if (s->kind == KERNIX_OP_ATTENTION) {
         const kx_val* vv = &g->vals[s->inp[s->n_in > 1 ? 1 : 0]];
         const size_t hk = (size_t)s->heads * s->dk, hv = (size_t)s->heads * s->dv;
@@ -429,6 +437,10 @@ static int step_run(kernix_model* m, int i, int B) {
         if (conv_depthwise(s))
             return kx_conv_depthwise(a, s->w.d_raw, s->d_bias, y, B, H, W, vi->c, vo->c, Ho, Wo, s->kh, s->kw, s->sh, s->sw,
                                      s->dh, s->dw, s->pt, s->pl, s->act, s->alpha, st);
+        if (conv_planes(s))
+            return kx_conv_f32_ws(a, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, B, H, W, vi->c, vo->c, Ho, Wo, s->kh, s->kw,
+                                  s->sh, s->sw, s->dh, s->dw, s->pt, s->pl, s->groups, s->act, s->alpha,
+                                  (float*)align_ptr(im->scratch), 2 * (size_t)rin * (size_t)vi->c, im->status, st);
         return kx_conv_f32(a, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, B, H, W, vi->c, vo->c, Ho, Wo, s->kh, s->kw, s->sh,
                            s->sw, s->dh, s->dw, s->pt, s->pl, s->groups, s->act, s->alpha, im->status, st);
     }

@@ -74,7 +74,7 @@ __device__ __forceinline__ bool at_wait(AtCtl* ctl, uint32_t parity, int* status
 __global__ void __launch_bounds__(AT_THREADS, 1)
 k_attention_tc(const float* __restrict__ q, int ldq, const float* __restrict__ k, int ldk, const float* __restrict__ v,
                int ldv, float* __restrict__ ctx, int ldc, int Rq, int S, int dk, int dv, int causal, float scale,
-               int* status) {
+               int ahead, int* status) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     AtCtl* ctl = reinterpret_cast<AtCtl*>(smem + AT_QK_BYTES + AT_V_BYTES);
@@ -116,6 +116,28 @@ k_attention_tc(const float* __restrict__ q, int ldq, const float* __restrict__ k
 #pragma unroll
     for (int u = 0; u < 4; u++)
         xv[u] = vj < S ? load_row4(vb + static_cast<long>(vj) * ldv, vd0 + 4 * u, dv, vv) : make_float4(0.f, 0.f, 0.f, 0.f);
+    // While these loads are in flight, ask L2 for the rows of the (sample, head) that will most likely run on this
+    // SM next (`ahead` CTAs later in launch order: one CTA per SM at a time), so that its loads hit L2 instead of
+    // paying a full DRAM round trip at its start. One 128-byte line per thread and row segment, rows of Q, K, V.
+    if (ahead > 0) {
+        const long nxt = static_cast<long>(b) * gridDim.x + h + ahead;
+        if (nxt < static_cast<long>(gridDim.x) * gridDim.y) {
+            const int hn = static_cast<int>(nxt % gridDim.x), bn = static_cast<int>(nxt / gridDim.x);
+            const int lq = (dk * 4 + 127) / 128, lv = (dv * 4 + 127) / 128;  // lines per row segment
+            for (int i = tid; i < Rq * lq + S * lq + S * lv; i += AT_THREADS) {
+                const float* p;
+                if (i < Rq * lq) p = q + (static_cast<long>(bn) * Rq + i / lq) * ldq + hn * dk + 32 * (i % lq);
+                else if (i < Rq * lq + S * lq) {
+                    const int j = i - Rq * lq;
+                    p = k + (static_cast<long>(bn) * S + j / lq) * ldk + hn * dk + 32 * (j % lq);
+                } else {
+                    const int j = i - Rq * lq - S * lq;
+                    p = v + (static_cast<long>(bn) * S + j / lv) * ldv + hn * dv + 32 * (j % lv);
+                }
+                kx::prefetch_l2(p);
+            }
+        }
+    }
 #pragma unroll
     for (int u = 0; u < NQ; u++) {
         const int i = u * AT_THREADS + tid, row = i >> 4, d4 = i & 15;
@@ -302,7 +324,10 @@ int kx_attention_tc(const float* q, int ldq, const float* k, int ldk, const floa
             return -1;
         __atomic_fetch_or(&devs_set, bit, __ATOMIC_RELEASE);
     }
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 0;
     dim3 grid(H, B);
-    k_attention_tc<<<grid, AT_THREADS, AT_SMEM, st>>>(q, ldq, k, ldk, v, ldv, ctx, ldc, Rq, S, dk, dv, causal, scale, status);
+    k_attention_tc<<<grid, AT_THREADS, AT_SMEM, st>>>(q, ldq, k, ldk, v, ldv, ctx, ldc, Rq, S, dk, dv, causal, scale, sms,
+                                                      status);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

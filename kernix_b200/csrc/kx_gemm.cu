@@ -1324,6 +1324,166 @@ k_conv_tf32x3_cm(const float* __restrict__ X, const __grid_constant__ CUtensorMa
     }
 }
 
+// ------------------------------------------------- 3xTF32 convolution, channel-major tiles fed by TMA
+// The channel-major convolution with its pixel operand loaded by the TMA instead of gathered by converter warps
+// (whose ~13 GB/s of gathered rows per SM bound the kernel above at ~2.4 us per K block against ~1.1 us of MMAs).
+// The activations are first split once into tf32 hi / lo planes (k_split_planes, into caller-provided scratch); a
+// K block is one tap (ky, kx) and 32 channels, and its 256 output pixels (whole output rows of one image, or whole
+// images) read a 4-D box {32 channels, Wo columns, rows, images} of each plane at (c0, kx dw - pl, oy0 + ky dh - pt,
+// b0): stride 1 makes the box's pixels the tile's pixels in order, and the TMA's zero fill outside the tensor is the
+// convolution's zero padding. The box lands in the canonical K-major 128-byte-swizzle layout of the B operand. 320
+// threads: warp 0 TMA (weights and both planes), warp 1 MMA, warps 2-9 the epilogue of the kernel above after the
+// last MMA. Conditions (checked by the host): stride 1, channels per group a multiple of 32, at most 128 output
+// channels per group, K <= DRAIN_MIN_K, and 256 a multiple of the image's output pixels or of its output width.
+struct CmtGeom {
+    int cg, kw, dh, dw, pt, pl;  // channels per group, kernel width, dilation, padding (top, left)
+    int Ho, Wo, rows, imgs;      // output size; output rows and images per 256-pixel tile
+};
+
+__global__ void __launch_bounds__(256) k_split_planes(const float* __restrict__ x, float* __restrict__ hi,
+                                                      float* __restrict__ lo, long n) {
+    const long n4 = n >> 2;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n4; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+        float4 h, l;
+        tf32_split(v.x, h.x, l.x);
+        tf32_split(v.y, h.y, l.y);
+        tf32_split(v.z, h.z, l.z);
+        tf32_split(v.w, h.w, l.w);
+        reinterpret_cast<float4*>(hi)[i] = h;
+        reinterpret_cast<float4*>(lo)[i] = l;
+    }
+    for (long i = 4 * n4 + blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long>(gridDim.x) * blockDim.x)
+        tf32_split(x[i], hi[i], lo[i]);
+}
+
+template <int ACTC>
+__global__ void __launch_bounds__(CM_THREADS, 1)
+k_conv_tf32x3_cmt(const __grid_constant__ CUtensorMap tmXhi, const __grid_constant__ CUtensorMap tmXlo,
+                  const __grid_constant__ CUtensorMap tmWhi, const __grid_constant__ CUtensorMap tmWlo,
+                  const float* __restrict__ bias, float* __restrict__ y, int ldy, int cog, int M, int K, int act,
+                  float alpha, int* status, const CmtGeom gm) {
+    using C = CmCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + C::STAGES * C::STAGE_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    auto sWhi = [&](int s) { return smem + s * C::STAGE_BYTES; };
+    auto sWlo = [&](int s) { return smem + s * C::STAGE_BYTES + C::W_BYTES; };
+    auto sXhi = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::W_BYTES; };
+    auto sXlo = [&](int s) { return smem + s * C::STAGE_BYTES + 2 * C::W_BYTES + C::X_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * CM_NP;
+    const int nk = (K + C::BK - 1) / C::BK;
+    const int grp = static_cast<int>(blockIdx.y);
+    const int wrow0 = grp * cog;
+    y += wrow0;
+    if (bias) bias += wrow0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1);
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        kx::tmem_alloc(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish();
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            kx::tma_prefetch_desc(&tmXhi);
+            kx::tma_prefetch_desc(&tmXlo);
+            kx::tma_prefetch_desc(&tmWhi);
+            kx::tma_prefetch_desc(&tmWlo);
+            const int hw = gm.Ho * gm.Wo;
+            const int b0 = m0 / hw, oy0 = (m0 - b0 * hw) / gm.Wo;  // the tile's first image and output row
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % C::STAGES;
+                if (!kx::mbar_wait(&ctl->empty[s], ((kb / C::STAGES) & 1) ^ 1, abort_flag, status)) break;
+                kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * C::W_BYTES + 2 * C::X_BYTES);
+                const int k0 = kb * C::BK, tap = k0 / gm.cg, ky = tap / gm.kw, kxx = tap - ky * gm.kw;
+                const int c0 = grp * gm.cg + (k0 - tap * gm.cg);
+                const int ix = kxx * gm.dw - gm.pl, iy = oy0 + ky * gm.dh - gm.pt;
+                kx::tma_load_2d(sWhi(s), &tmWhi, k0, wrow0, &ctl->full[s]);
+                kx::tma_load_2d(sWlo(s), &tmWlo, k0, wrow0, &ctl->full[s]);
+                kx::tma_load_4d(sXhi(s), &tmXhi, c0, ix, iy, b0, &ctl->full[s]);
+                kx::tma_load_4d(sXlo(s), &tmXlo, c0, ix, iy, b0, &ctl->full[s]);
+                issued = kb + 1;
+            }
+            if (*abort_flag)
+                for (int kb = issued > C::STAGES ? issued - C::STAGES : 0; kb < issued; kb++)
+                    drain_wait(&ctl->full[kb % C::STAGES], (kb / C::STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = kx::idesc_tf32(BM, CM_NP);
+            const uint32_t d = tmem + C::MAIN0, dx = tmem + C::CROSS;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % C::STAGES;
+                if (!kx::mbar_wait(&ctl->full[s], (kb / C::STAGES) & 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t wh = kx::smem_u32(sWhi(s)), wl = kx::smem_u32(sWlo(s));
+                const uint32_t xh = kx::smem_u32(sXhi(s)), xl = kx::smem_u32(sXlo(s));
+#pragma unroll
+                for (int kk = 0; kk < C::BK / 8; kk++) {
+                    const uint32_t o = kk * 32;
+                    kx::mma_tf32(dx, kx::desc_sw128_kmajor(wl + o), kx::desc_sw128_kmajor(xh + o), idesc, (kb | kk) != 0);
+                    kx::mma_tf32(dx, kx::desc_sw128_kmajor(wh + o), kx::desc_sw128_kmajor(xl + o), idesc, 1);
+                    kx::mma_tf32(d, kx::desc_sw128_kmajor(wh + o), kx::desc_sw128_kmajor(xh + o), idesc, (kb | kk) != 0);
+                }
+                kx::mma_commit(&ctl->empty[s]);
+            }
+            kx::mma_commit(&ctl->accf);
+        }
+        __syncwarp();
+    } else {
+        drain_wait(&ctl->accf, 0);
+        kx::tc_fence_after();
+        const int q = warp & 3, part = (warp - 2) >> 2;
+        const int ch = q * 32 + lane;
+        const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+        if (ok && q * 32 < cog) {
+            const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+            const bool live = ch < cog;
+            const float bch = (bias && live) ? __ldg(bias + ch) : 0.0f;
+#pragma unroll 1
+            for (int c0 = 32 * part; c0 < CM_NP; c0 += 64) {
+                if (m0 + c0 >= M) break;
+                uint32_t r[32], x[32];
+                kx::tmem_ld32(tmem + lanes + C::MAIN0 + c0, r);
+                kx::tmem_ld32(tmem + lanes + C::CROSS + c0, x);
+                kx::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    float t = __fadd_rn(__uint_as_float(r[j]), __uint_as_float(x[j]));
+                    if (bias) t = __fadd_rn(t, bch);
+                    const int pix = m0 + c0 + j;
+                    if (live && pix < M) y[static_cast<size_t>(pix) * ldy + ch] = epi_act<ACTC>(t, act, alpha);
+                }
+            }
+        }
+    }
+    kx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------------------------------------------ 3xTF32, CTA pairs
 // The same GEMM on 256 x BN output tiles computed by a cluster of two CTAs with M = 256 tcgen05.mma
 // (cta_group::2). CTA rank r converts A rows [m0 + 128 r, +128) of each K block into its own shared memory and
@@ -1752,6 +1912,57 @@ int launch_conv_cm(const float* x, const float* whi, const float* wlo, int ldw, 
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+// 4-D map of an NHWC fp32 activation tensor {C, W, H, B} (C innermost) with box {32, bw, bh, bn}, 128-byte swizzle
+int make_map_nhwc(CUtensorMap* out, const float* base, int B, int H, int W, int C, uint32_t bw, uint32_t bh, uint32_t bn) {
+    PFN_encodeTiled_t enc = encode_fn();
+    if (enc == nullptr) return -1;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (C & 3)) return -1;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(H),
+                          static_cast<cuuint64_t>(B)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 4, static_cast<cuuint64_t>(W) * C * 4,
+                             static_cast<cuuint64_t>(H) * W * C * 4};
+    cuuint32_t box[4] = {32, bw, bh, bn};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS ? 0 : -1;
+}
+
+// tile shape of the TMA-fed channel-major convolution: 0 and (rows, images) per 256-pixel tile, or -1 if the
+// output's geometry does not cut into whole rows / images
+int cmt_tiling(int Ho, int Wo, int& rows, int& imgs) {
+    const long P = static_cast<long>(Ho) * Wo;
+    if (P <= 0 || Wo > 256) return -1;
+    if (P <= CM_NP) {
+        if (CM_NP % P) return -1;
+        rows = Ho;
+        imgs = static_cast<int>(CM_NP / P);
+        return 0;
+    }
+    if (P % CM_NP || CM_NP % Wo) return -1;
+    rows = CM_NP / Wo;
+    imgs = 1;
+    return 0;
+}
+
+template <int ACTC>
+int launch_conv_cmt(const CUtensorMap& xh, const CUtensorMap& xl, const float* whi, const float* wlo, int ldw, int wrows,
+                    const float* bias, float* y, int ldy, int cog, int m, int k, int act, float alpha, int* status,
+                    cudaStream_t st, const CmtGeom& gm, int groups) {
+    using C = CmCfg;
+    CUtensorMap th, tl;
+    if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BM) != 0 ||
+        make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
+                    static_cast<uint64_t>(ldw) * 4, C::BK, BM) != 0)
+        return -1;
+    auto kern = k_conv_tf32x3_cmt<ACTC>;
+    if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+    dim3 grid((m + CM_NP - 1) / CM_NP, groups);
+    kern<<<grid, CM_THREADS, C::SMEM, st>>>(xh, xl, th, tl, bias, y, ldy, cog, m, k, act, alpha, status, gm);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 // ------------------------------------------------------------------- direct convolution, tiny K
 // For reductions of at most DC_MAXK with at most 64 output channels per group (the first 3x3 layer over RGB: K = 27,
 // 64 channels) a tensor-core tile spends its time on pipeline set-up and a whole epilogue per 32 K, so these layers run
@@ -2033,6 +2244,44 @@ int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, c
                                        st, cv, groups);
     return dispatch_f32<256, true>(x, C, w_hi, w_lo, ldw, Co, bias, y, Co, static_cast<int>(m), cog, k, act, alpha, status, st,
                                    cv, groups);
+}
+
+int kx_conv_f32_ws(const float* x, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y, int B, int H,
+                   int W, int C, int Co, int Ho, int Wo, int kh, int kw, int sh, int sw, int dh, int dw, int pt, int pl,
+                   int groups, int act, float alpha, float* ws, size_t ws_floats, int* status, void* stream) {
+    if (B <= 0) return 0;
+    if (groups < 1 || C % groups || Co % groups || (ldw & 3)) return -1;
+    const long m = static_cast<long>(B) * Ho * Wo, n = static_cast<long>(B) * H * W * C;
+    const int cg = C / groups, cog = Co / groups, k = kh * kw * cg;
+    int rows = 0, imgs = 0;
+    const bool tma = sh == 1 && sw == 1 && cg % 32 == 0 && cog <= 128 && m > BM && m <= INT32_MAX && k <= DRAIN_MIN_K &&
+                     k <= ldw && groups <= 65535 && cmt_tiling(Ho, Wo, rows, imgs) == 0 && ws != nullptr &&
+                     ws_floats >= static_cast<size_t>(2 * n) && (reinterpret_cast<uintptr_t>(ws) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (!tma)
+        return kx_conv_f32(x, w_hi, w_lo, ldw, bias, y, B, H, W, C, Co, Ho, Wo, kh, kw, sh, sw, dh, dw, pt, pl, groups, act,
+                           alpha, status, stream);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* xh = ws;
+    float* xl = ws + n;  // n is a multiple of 4: 16-byte aligned
+    const long blocks = (n / 4 + 255) / 256;
+    k_split_planes<<<static_cast<unsigned>(blocks < 4L * sm_count() ? (blocks > 0 ? blocks : 1) : 4L * sm_count()), 256, 0, st>>>(
+        x, xh, xl, n);
+    if (cudaGetLastError() != cudaSuccess) return -1;
+    CUtensorMap mh, ml;
+    if (make_map_nhwc(&mh, xh, B, H, W, C, static_cast<uint32_t>(Wo), static_cast<uint32_t>(rows), static_cast<uint32_t>(imgs)) != 0 ||
+        make_map_nhwc(&ml, xl, B, H, W, C, static_cast<uint32_t>(Wo), static_cast<uint32_t>(rows), static_cast<uint32_t>(imgs)) != 0)
+        return -1;
+    const CmtGeom gm{cg, kw, dh, dw, pt, pl, Ho, Wo, rows, imgs};
+    const int mi = static_cast<int>(m);
+    switch (act_class(act)) {
+    case -1: return launch_conv_cmt<-1>(mh, ml, w_hi, w_lo, ldw, Co, bias, y, Co, cog, mi, k, act, alpha, status, st, gm, groups);
+    case 0: return launch_conv_cmt<0>(mh, ml, w_hi, w_lo, ldw, Co, bias, y, Co, cog, mi, k, act, alpha, status, st, gm, groups);
+    case 1: return launch_conv_cmt<1>(mh, ml, w_hi, w_lo, ldw, Co, bias, y, Co, cog, mi, k, act, alpha, status, st, gm, groups);
+    default:
+        return launch_conv_cmt<ACT_GENERIC>(mh, ml, w_hi, w_lo, ldw, Co, bias, y, Co, cog, mi, k, act, alpha, status, st, gm,
+                                            groups);
+    }
 }
 
 int kx_prep_i8_weight(const int8_t* q_kn, int k, int n, int8_t* wq, int ldw, void* stream) {

@@ -31,6 +31,7 @@ SIGNATURES = {
     "kx_embedding": [_vp, _l, _vp, _i, _i, _vp, _vp],
     "kx_conv_depthwise": [_vp, _vp, _vp, _vp] + [_i] * 15 + [_i, _f, _vp],
     "kx_conv_f32": [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 16 + [_i, _f, _vp, _vp],
+    "kx_conv_f32_ws": [_vp, _vp, _vp, _i, _vp, _vp] + [_i] * 16 + [_i, _f, _vp, _sz, _vp, _vp],
     "kx_attention": [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp],
     "kx_fma_relu": [_vp, _vp, _vp, _vp, _sz, _vp],
     "kx_unshard_cols": [_vp, _i, _l, _i, _vp, _i, _vp],

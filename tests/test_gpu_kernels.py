@@ -294,6 +294,11 @@ def test_gemm_f32_skinny(kx, m, k, n, act):
     dict(B=1, H=30, W=30, C=16, Co=8, k=5, s=1, d=1, p=2, g=1),
     # K = 2304 > 2048 with 64 channels: drained CTA-pair tiles
     dict(B=3, H=8, W=8, C=256, Co=64, k=3, s=1, d=1, p=1, g=1),
+    # planes + TMA boxes (kx_conv_f32_ws): several images per tile, no padding, dilation, groups of 32 channels
+    dict(B=5, H=8, W=8, C=64, Co=64, k=3, s=1, d=1, p=1, g=1, a=1),
+    dict(B=2, H=18, W=18, C=32, Co=64, k=3, s=1, d=1, p=0, g=1),
+    dict(B=1, H=16, W=16, C=64, Co=48, k=3, s=1, d=2, p=2, g=1),
+    dict(B=3, H=16, W=16, C=64, Co=64, k=3, s=1, d=1, p=1, g=2, a=-1),
 ])
 def test_conv_implicit_gemm(kx, cfg):
     """implicit-GEMM conv (no im2col buffer) vs the oracle's im2col + sgemm restatement of kernix_conv_run."""
@@ -318,6 +323,13 @@ def test_conv_implicit_gemm(kx, cfg):
                 w=("f32", w), bias=b)
     want = ko.conv(step, ko._val([H, W, C]), ko._val([Ho, Wo, Co]), x)
     assert rel_err(got, want) <= 1e-5
+    # with scratch for the tf32 planes (TMA-fed tiles where the geometry allows, the same kernels otherwise)
+    ws = torch.full((2 * B * H * W * C + 64,), float("nan"), dtype=torch.float32, device="cuda")
+    y2 = torch.empty_like(y)
+    kx.call("kx_conv_f32_ws", dev(x).data_ptr(), hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y2.data_ptr(), B, H, W, C,
+            Co, Ho, Wo, kk, kk, s, s, d, d, p, p, g, act, 0.0, ws.data_ptr(), ws.numel(), st.data_ptr(), sp())
+    check_status(st)
+    assert rel_err(host(y2), want) <= 1e-5
 
 
 # ------------------------------------------------------------------------------------ memory-bound
