@@ -375,6 +375,23 @@ def test_binary_broadcast_and_inplace(kx):
     assert np.array_equal(host(da), a + a)
 
 
+@pytest.mark.parametrize("C", [8, 64])
+def test_pool2d_four_channels_at_a_time(kx, C):
+    """Channel counts that are multiples of 4 take the float4 pooling path: same windows, same per-element
+    combination as the reference (max keeps a NaN only where the reference's comparison does), with NaNs planted."""
+    rng = np.random.default_rng(C)
+    B, H, W = 3, 9, 10
+    x = rng.standard_normal((B * H * W, C)).astype(F32)
+    x[rng.integers(0, B * H * W, 7), rng.integers(0, C, 7)] = np.nan
+    dx = dev(x)
+    for ptype, k, s, p, cp in [(0, 2, 2, 0, 0), (1, 3, 2, 1, 0), (1, 3, 2, 1, 1), (0, 3, 1, 1, 0)]:
+        Ho, Wo = (H + 2 * p - k) // s + 1, (W + 2 * p - k) // s + 1
+        y = torch.empty((B * Ho * Wo, C), dtype=torch.float32, device="cuda")
+        kx.call("kx_pool2d", dx.data_ptr(), y.data_ptr(), B, H, W, C, Ho, Wo, k, k, s, s, p, p, ptype, cp, sp())
+        st = dict(ptype=ptype, kh=k, kw=k, sh=s, sw=s, pt=p, pb=p, pl=p, pr=p, count_pad=cp)
+        assert rel_err(host(y), ko.pool(st, ko._val([H, W, C]), ko._val([Ho, Wo, C]), x)) <= 1e-6
+
+
 def test_pool_gpool_permute_pad_upsample(kx):
     rng = np.random.default_rng(11)
     B, H, W, C = 2, 7, 6, 5
