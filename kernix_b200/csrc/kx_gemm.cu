@@ -1979,7 +1979,7 @@ __global__ void __launch_bounds__(256) k_conv_direct(const float* __restrict__ x
                                                       int act, float alpha) {
     __shared__ __align__(16) float xs[DC_PIX][DC_MAXK];
     __shared__ int kdy[DC_MAXK], kdx[DC_MAXK], kci[DC_MAXK];  // per reduction index: input row / column offset, channel
-    __shared__ int pb[DC_PIX], py[DC_PIX], px[DC_PIX];        // per pixel of the tile: image, top row, left column
+    __shared__ int pb[2][DC_PIX], py[2][DC_PIX], px[2][DC_PIX];  // per pixel of a tile: image, top row, left column
     const int g = blockIdx.y, cog = cv.cog, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int hw = cv.Ho * cv.Wo;
     if (threadIdx.x < DC_MAXK) {
@@ -2007,34 +2007,49 @@ __global__ void __launch_bounds__(256) k_conv_direct(const float* __restrict__ x
     }
     const float b0 = (bias && c0 < cog) ? __ldg(bias + g * cog + c0) : 0.0f;
     const float b1 = (bias && c1 < cog) ? __ldg(bias + g * cog + c1) : 0.0f;
-    for (int p0 = blockIdx.x * DC_PIX; p0 < M; p0 += gridDim.x * DC_PIX) {
-        __syncthreads();  // the previous tile's inputs have been read
+    // Tiles of DC_PIX pixels, software-pipelined: the next tile's inputs are requested into registers right after
+    // this tile's are stored to shared memory, so their latency hides behind this tile's fmas.
+    constexpr int PER = DC_PIX * DC_MAXK / 256;  // inputs gathered per thread
+    auto geom = [&](int buf, int t0) {  // pixel geometry of the tile at t0 (threads 0 .. DC_PIX - 1)
         if (threadIdx.x < DC_PIX) {
-            const int m = p0 + threadIdx.x;
+            const int m = t0 + threadIdx.x;
             const int b = m / hw, rem = m - b * hw, oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
-            pb[threadIdx.x] = b * cv.H;
-            py[threadIdx.x] = oy * cv.sh - cv.pt;
-            px[threadIdx.x] = ox * cv.sw - cv.pl;
+            pb[buf][threadIdx.x] = b * cv.H;
+            py[buf][threadIdx.x] = oy * cv.sh - cv.pt;
+            px[buf][threadIdx.x] = ox * cv.sw - cv.pl;
         }
-        __syncthreads();
-        constexpr int PER = DC_PIX * DC_MAXK / 256;  // inputs gathered per thread, all loads issued before the stores
-        float v[PER];
+    };
+    auto gather = [&](int buf, int t0, float (&v)[PER]) {  // all loads issued before any use
 #pragma unroll
         for (int u = 0; u < PER; u++) {
             const int i = u * 256 + threadIdx.x, p = i / DC_MAXK, k = i % DC_MAXK;
             v[u] = 0.0f;
-            if (k < K && p0 + p < M) {
-                const int iy = py[p] + kdy[k], ix = px[p] + kdx[k];
+            if (k < K && t0 + p < M) {
+                const int iy = py[buf][p] + kdy[k], ix = px[buf][p] + kdx[k];
                 if (iy >= 0 && iy < cv.H && ix >= 0 && ix < cv.W)
-                    v[u] = __ldg(x + ((static_cast<size_t>(pb[p]) + iy) * cv.W + ix) * cv.C + kci[k]);
+                    v[u] = __ldg(x + ((static_cast<size_t>(pb[buf][p]) + iy) * cv.W + ix) * cv.C + kci[k]);
             }
         }
+    };
+    const int stride = gridDim.x * DC_PIX;
+    float v[PER];
+    int p0 = blockIdx.x * DC_PIX, buf = 0;
+    if (p0 < M) {
+        geom(0, p0);
+        __syncthreads();  // also publishes kdy / kdx / kci
+        gather(0, p0, v);
+    }
+    for (; p0 < M; p0 += stride, buf ^= 1) {
+        __syncthreads();  // the previous tile's inputs and the other geometry buffer are no longer read
 #pragma unroll
         for (int u = 0; u < PER; u++) {
             const int i = u * 256 + threadIdx.x;
             xs[i / DC_MAXK][i % DC_MAXK] = v[u];
         }
+        const int pn = p0 + stride;
+        if (pn < M) geom(buf ^ 1, pn);
         __syncthreads();
+        if (pn < M) gather(buf ^ 1, pn, v);
         for (int p = warp; p < DC_PIX; p += 8) {
             const int m = p0 + p;
             if (m >= M) break;

@@ -294,6 +294,10 @@ def test_gemm_f32_skinny(kx, m, k, n, act):
     dict(B=1, H=30, W=30, C=16, Co=8, k=5, s=1, d=1, p=2, g=1),
     # K = 2304 > 2048 with 64 channels: drained CTA-pair tiles
     dict(B=3, H=8, W=8, C=256, Co=64, k=3, s=1, d=1, p=1, g=1),
+    # direct CUDA-core convolution (K <= 32, <= 64 channels): ragged tiles, stride 2, GELU
+    dict(B=3, H=13, W=11, C=3, Co=64, k=3, s=2, d=1, p=1, g=1),
+    dict(B=4, H=7, W=9, C=2, Co=40, k=3, s=1, d=1, p=1, g=1, a=1),
+    dict(B=7, H=32, W=32, C=3, Co=64, k=3, s=1, d=1, p=1, g=1),
     # planes + TMA boxes (kx_conv_f32_ws): several images per tile, no padding, dilation, groups of 32 channels
     dict(B=5, H=8, W=8, C=64, Co=64, k=3, s=1, d=1, p=1, g=1, a=1),
     dict(B=2, H=18, W=18, C=32, Co=64, k=3, s=1, d=1, p=0, g=1),
