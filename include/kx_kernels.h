@@ -70,6 +70,13 @@ KERNIX_API int kx_prep_i8_weight(const int8_t* q_kn, int k, int n, int8_t* wq, i
 KERNIX_API int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
                 int ldy, int m, int n, int k, int act, float alpha, int* status, void* stream);
 
+/* y = act(x . W + bias) + res (ldr >= n): a LINEAR step and the elementwise ADD that consumes it in one kernel
+ * (kernix_dense :544-550 followed by kernix_binary_run :877-906), each output written once. The add is the ADD
+ * step's round-to-nearest fp32 add on the activation's output, so results are bitwise those of the two steps run
+ * apart. y may be res (in place); neither may overlap x. */
+KERNIX_API int kx_gemm_f32_res(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
+                    int ldy, int m, int n, int k, int act, float alpha, const float* res, int ldr, int* status, void* stream);
+
 /* Load-time transpose + split of a float weight (k x n, in x out) into n x ldw K-major planes
  * hi = tf32(w), lo = w - hi (exact), zero padded. */
 KERNIX_API int kx_prep_f32_weight(const float* w_kn, int k, int n, float* w_hi, float* w_lo, int ldw, void* stream);

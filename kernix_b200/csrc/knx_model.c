@@ -382,15 +382,38 @@ static float* val_ptr(const struct kx_model_impl* im, int v) {
 
 static void* align_ptr(void* p) { return (void*)round_up((uintptr_t)p, KX_ALIGN); }
 
-/* one step over B samples */
-static int step_run(kernix_model* m, int i, int B) {
+/* Mark the fp32 LINEAR / ATTENTION steps whose output is read only by the next step, an ADD of two operands of the
+ * same shape: the GEMM that produces the output adds the ADD's other operand in its epilogue and writes the ADD's
+ * output (the same round-to-nearest add on the same values, so the same bits), and the ADD step is skipped. The
+ * ADD's output must not share storage with the LINEAR's input, which the GEMM is still reading. */
+static void plan_fusions(kx_graph* g) {
+    for (int i = 0; i + 1 < g->n_steps; i++) {
+        kx_step* s = &g->steps[i];
+        const kx_step* t = &g->steps[i + 1];
+        s->fuse_add = 0;
+        const int gemm = (s->kind == KERNIX_OP_LINEAR && !s->w.int8 && s->shard_n == 0) || s->kind == KERNIX_OP_ATTENTION;
+        if (!gemm || t->kind != KERNIX_OP_BINARY || t->bop != 0 || t->n_in != 2) continue;
+        const int out = i + 1, res = t->inp[0] == out ? t->inp[1] : t->inp[0];
+        if ((t->inp[0] == out) == (t->inp[1] == out)) continue; /* the output is not exactly one of the operands */
+        const kx_val *vo = &g->vals[out], *vr = &g->vals[res], *vy = &g->vals[i + 2];
+        if (vo->last != i + 1 || out == g->out_v) continue;
+        if (vo->r != vr->r || vo->c != vr->c || vo->r != vy->r || vo->c != vy->c) continue;
+        if (s->kind == KERNIX_OP_LINEAR && vy->st == g->vals[s->inp[0]].st) continue;
+        s->fuse_add = 1;
+        s->fuse_res = res;
+    }
+}
+
+/* one step over B samples; fused: the step's GEMM also performs the next step, an ADD (plan_fusions) */
+static int step_run(kernix_model* m, int i, int B, int fused) {
     struct kx_model_impl* im = m->impl;
     kx_graph* g = im->g;
     kx_step* s = &g->steps[i];
     const kx_val* vi = &g->vals[s->inp[0]];
     const kx_val* vo = &g->vals[i + 1];
     const float* a = val_ptr(im, s->inp[0]);
-    float* y = val_ptr(im, i + 1);
+    float* y = val_ptr(im, fused ? i + 2 : i + 1);
+    const float* res = fused ? val_ptr(im, s->fuse_res) : NULL;
     const long rin = (long)B * vi->r, rout = (long)B * vo->r;
     cudaStream_t st = im->stream;
     switch (s->kind) {
@@ -418,9 +441,12 @@ static int step_run(kernix_model* m, int i, int B) {
             }
             return kx_unshard_cols(yg, im->world, rin, s->shard_n, y, s->out, st);
         }
-        if (skinny) /* few rows: stream the fp32 weights on the CUDA cores, K split over the SMs */
+        if (skinny) /* few rows: stream the fp32 weights on the CUDA cores, K split over the SMs (never fused) */
             return kx_gemm_f32_skinny(a, s->in, s->w.d_raw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act, s->alpha,
                                       im->skinny_part, im->skinny_floats, st);
+        if (res)
+            return kx_gemm_f32_res(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in,
+                                   s->act, s->alpha, res, s->out, im->status, st);
         return kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act,
                            s->alpha, im->status, st);
     case KERNIX_OP_ACT:
@@ -525,6 +551,9 @@ static int step_run(kernix_model* m, int i, int B) {
                              st) != 0)
                 return -1;
         }
+        if (res)
+            return kx_gemm_f32_res(ctx, hv, s->wo.d_hi, s->wo.d_lo, s->wo.ldw, s->d_bo, y, s->out, (int)rin, s->out, hv,
+                                   KERNIX_ACT_NONE, 0.0f, res, s->out, im->status, st);
         return kx_gemm_f32(ctx, hv, s->wo.d_hi, s->wo.d_lo, s->wo.ldw, s->d_bo, y, s->out, (int)rin, s->out, hv,
                            KERNIX_ACT_NONE, 0.0f, im->status, st);
     }
@@ -577,12 +606,20 @@ static const char* kind_name(int k) {
 }
 
 static int chunk_run(kernix_model* m, int B) {
-    for (int i = 0; i < m->impl->g->n_steps; i++)
-        if (step_run(m, i, B) != 0) {
-            fprintf(stderr, "forward: step %d (%s) failed to launch: %s\n", i, kind_name(m->impl->g->steps[i].kind),
+    struct kx_model_impl* im = m->impl;
+    for (int i = 0; i < im->g->n_steps; i++) {
+        const kx_step* s = &im->g->steps[i];
+        /* a fused LINEAR must take the tensor-core path (the skinny path for few rows has no residual) */
+        const long rin = (long)B * im->g->vals[s->inp[0]].r;
+        const int fused = s->fuse_add && (s->kind == KERNIX_OP_ATTENTION || !(rin <= KX_SKINNY_MAX_ROWS && s->w.d_raw != NULL &&
+                                                                              im->skinny_part != NULL));
+        if (step_run(m, i, B, fused) != 0) {
+            fprintf(stderr, "forward: step %d (%s) failed to launch: %s\n", i, kind_name(s->kind),
                     cudaGetErrorString(cudaGetLastError()));
             return -1;
         }
+        if (fused) i++; /* the ADD is done */
+    }
     return 0;
 }
 
@@ -789,6 +826,7 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
                 s->shard_c0 = s->shard_n * rank;
             }
         }
+    plan_fusions(g);
     kernix_model* m = calloc(1, sizeof *m);
     struct kx_model_impl* im = calloc(1, sizeof *im);
     if (m == NULL || im == NULL) {
@@ -1011,7 +1049,7 @@ KERNIX_API int kx_model_forward_trace(kernix_model* m, const float* x, int rows,
     if (cudaMemcpyAsync(im->xin, x, (size_t)rows * m->in_dim * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess)
         goto done;
     for (int i = 0; i < im->g->n_steps; i++) {
-        if (step_run(m, i, B) != 0) goto done;
+        if (step_run(m, i, B, 0) != 0) goto done;
         if (outs[i] != NULL) {
             const kx_val* v = &im->g->vals[i + 1];
             if (cudaMemcpyAsync(outs[i], val_ptr(im, i + 1), (size_t)B * v->r * v->c * sizeof(float), cudaMemcpyDeviceToHost,

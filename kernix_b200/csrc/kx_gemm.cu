@@ -746,6 +746,33 @@ __device__ __forceinline__ void f32_stage_bias(float* sbias, const float* __rest
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+// The residual values of one 32 x 32 output block as the store loops below write it (lane: rows 4 p + lane / 8,
+// columns col0 + 4 (lane % 8) .. + 3), all eight loads issued at once so that their latency overlaps the block's
+// TMEM loads and activation math; zero where the block leaves the output.
+__device__ __forceinline__ void load_residual(const float* __restrict__ res, int ldr, bool rvec, int row0, int col0, int lane,
+                                              int M, int N, float4 (&rv)[8]) {
+    const int gcol = col0 + 4 * (lane & 7);
+#pragma unroll
+    for (int p = 0; p < 8; p++) {
+        const int grow = row0 + 4 * p + (lane >> 3);
+        rv[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (grow >= M || gcol >= N) continue;
+        const float* rp = res + static_cast<size_t>(grow) * ldr + gcol;
+        if (rvec && gcol + 3 < N) {
+            rv[p] = __ldg(reinterpret_cast<const float4*>(rp));
+        } else {
+            rv[p].x = __ldg(rp);
+            if (gcol + 1 < N) rv[p].y = __ldg(rp + 1);
+            if (gcol + 2 < N) rv[p].z = __ldg(rp + 2);
+            if (gcol + 3 < N) rv[p].w = __ldg(rp + 3);
+        }
+    }
+}
+// y = (activation output) + res with round-to-nearest adds (the separate ADD step's arithmetic)
+__device__ __forceinline__ float4 add4(float4 w, float4 r) {
+    return make_float4(__fadd_rn(w.x, r.x), __fadd_rn(w.y, r.y), __fadd_rn(w.z, r.z), __fadd_rn(w.w, r.w));
+}
+
 // Final epilogue of one warp's 32 rows (TMEM lanes; thread = row row0 + lane), 32-column blocks part, part + 3, ...
 // (the three warps of a TMEM lane quarter share a tile's blocks): (Ah.Bh sum + cross terms) rounded
 // to nearest, bias (from the shared-memory copy), activation. Each 32-column block is staged through one of the
@@ -756,15 +783,19 @@ __device__ __forceinline__ void f32_stage_bias(float* sbias, const float* __rest
 template <int BN, int ACTC>
 __device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross, bool ok, int row0, int lane, int n0,
                                                const float* sbias, bool has_bias, float* __restrict__ y, int ldy,
-                                               int M, int N, int act, float alpha, float4* stg, int part) {
+                                               int M, int N, int act, float alpha, float4* stg, int part,
+                                               const float* __restrict__ res, int ldr, bool add_cross) {
     const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+    const bool rvec = ((ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(res) & 15) == 0);
 #pragma unroll 1
     for (int c0 = 32 * part; c0 < BN; c0 += 32 * F32_EPI_PARTS) {
         uint32_t r[32], x[32];
         kx::tmem_ld32(t_sum + c0, r);
-        kx::tmem_ld32(t_cross + c0, x);
-        kx::tmem_ld_wait();
+        if (add_cross) kx::tmem_ld32(t_cross + c0, x);
         const int col0 = n0 + c0;
+        float4 rv[8];
+        if (res && ok) load_residual(res, ldr, rvec, row0, col0, lane, M, N, rv);
+        kx::tmem_ld_wait();
         if (!ok || col0 >= N) continue;
         float4* buf = stg + ((c0 >> 5) & 1) * 256;
 #pragma unroll
@@ -774,7 +805,8 @@ __device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross,
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                float t = __fadd_rn(__uint_as_float(r[4 * j4 + e]), __uint_as_float(x[4 * j4 + e]));
+                float t = __uint_as_float(r[4 * j4 + e]);
+                if (add_cross) t = __fadd_rn(t, __uint_as_float(x[4 * j4 + e]));
                 if (has_bias) t = __fadd_rn(t, bb[e]);
                 v[e] = epi_act<ACTC>(t, act, alpha);
             }
@@ -785,8 +817,9 @@ __device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross,
 #pragma unroll
         for (int p = 0; p < 8; p++) {
             const int rr = 4 * p + (lane >> 3), grow = row0 + rr;
-            const float4 w = buf[rr * 8 + (q ^ (rr & 7))];
+            float4 w = buf[rr * 8 + (q ^ (rr & 7))];
             if (grow >= M || gcol >= N) continue;
+            if (res) w = add4(w, rv[p]);
             float* dst = y + static_cast<size_t>(grow) * ldy + gcol;
             if (vec && gcol + 3 < N) {
                 *reinterpret_cast<float4*>(dst) = w;
@@ -804,7 +837,8 @@ template <int BN, int STAGES, bool CONV, int ACTC, bool DRAIN>
 __global__ void __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
               const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
-              int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv) {
+              int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv, const float* __restrict__ res,
+              int ldr, int combine) {
     using C = F32Cfg<BN, STAGES, DRAIN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
@@ -884,6 +918,12 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
 #pragma unroll
                 for (int kk = 0; kk < C::BK / 8; kk++) {
                     const uint32_t o = kk * 32;  // 8 tf32 = 32 bytes of K per MMA
+                    if (!DRAIN && combine) {  // the three products in one accumulator, in k_gemm_tf32x3_pp's order
+                        kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
+                        kx::mma_tf32(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
+                        kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                        continue;
+                    }
                     kx::mma_tf32(dx, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
                     kx::mma_tf32(dx, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
                     kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
@@ -927,7 +967,7 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
         f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
                                  n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
-                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part);
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part, res, ldr, DRAIN || !combine);
     }
     kx::tc_fence_before();
     __syncthreads();
@@ -966,15 +1006,19 @@ struct PpCfg {
 // staged through the warp's 4 KB buffer `stg` and written as full 128-byte row segments
 template <int ACTC>
 __device__ __forceinline__ void pp_store_tile(uint32_t t_acc, int row0, int lane, int n0, const float* sbias, bool has_bias,
-                                              float* __restrict__ y, int ldy, int M, int N, int act, float alpha, float4* stg) {
+                                              float* __restrict__ y, int ldy, int M, int N, int act, float alpha, float4* stg,
+                                              const float* __restrict__ res, int ldr) {
     constexpr int BN = PpCfg::BN;
     const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+    const bool rvec = ((ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(res) & 15) == 0);
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         kx::tmem_ld32(t_acc + c0, r);
-        kx::tmem_ld_wait();
         const int col0 = n0 + c0;
+        float4 rv[8];
+        if (res) load_residual(res, ldr, rvec, row0, col0, lane, M, N, rv);
+        kx::tmem_ld_wait();
         if (col0 >= N) break;
         __syncwarp();  // the previous block's reads of stg are done
 #pragma unroll
@@ -995,8 +1039,9 @@ __device__ __forceinline__ void pp_store_tile(uint32_t t_acc, int row0, int lane
 #pragma unroll
         for (int p = 0; p < 8; p++) {
             const int rr = 4 * p + (lane >> 3), grow = row0 + rr;
-            const float4 w = stg[rr * 8 + (q ^ (rr & 7))];
+            float4 w = stg[rr * 8 + (q ^ (rr & 7))];
             if (grow >= M || gcol >= N) continue;
+            if (res) w = add4(w, rv[p]);
             float* dst = y + static_cast<size_t>(grow) * ldy + gcol;
             if (vec && gcol + 3 < N) {
                 *reinterpret_cast<float4*>(dst) = w;
@@ -1014,7 +1059,7 @@ template <int ACTC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3_pp(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
                  const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
-                 int M, int N, int K, int act, float alpha, int* status) {
+                 int M, int N, int K, int act, float alpha, int* status, const float* __restrict__ res, int ldr) {
     using C = PpCfg;
     constexpr int BN = C::BN, STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -1150,7 +1195,7 @@ k_gemm_tf32x3_pp(const float* __restrict__ A, int lda, const __grid_constant__ C
             if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
             kx::tc_fence_after();
             pp_store_tile<ACTC>(tmem + lanes + b * BN, mt * 2 * BM + static_cast<int>(rank) * BM + q * 32, lane, nt * BN, sb,
-                                bias != nullptr, y, ldy, M, N, act, alpha, stg);
+                                bias != nullptr, y, ldy, M, N, act, alpha, stg, res, ldr);
 #pragma unroll
             for (int e = 0; e < 8; e++) bcur[e] = bnext[e];
             kx::tc_fence_before();
@@ -1516,7 +1561,8 @@ template <int BN, bool CONV, int ACTC, bool DRAIN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
                    const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y,
-                   int ldy, int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv) {
+                   int ldy, int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv,
+                   const float* __restrict__ res, int ldr, int combine) {
     using C = F32PairCfg<BN, DRAIN>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -1601,6 +1647,12 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
 #pragma unroll
                 for (int kk = 0; kk < C::BK / 8; kk++) {
                     const uint32_t o = kk * 32;
+                    if (!DRAIN && combine) {  // the three products in one accumulator, in k_gemm_tf32x3_pp's order
+                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
+                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
+                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
+                        continue;
+                    }
                     kx::mma_tf32_pair(dx, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
                     kx::mma_tf32_pair(dx, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
                     kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
@@ -1653,7 +1705,7 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
         const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
         f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
                                  n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
-                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part);
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part, res, ldr, DRAIN || !combine);
     }
     kx::tc_fence_before();
     kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
@@ -1839,7 +1891,7 @@ int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq,
 template <int BN, bool CONV, int ACTC, bool DRAIN>
 int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
-               int groups) {
+               int groups, const float* res, int ldr) {
     constexpr int STAGES = BN == 256 ? 2 : 3;
     using C = F32Cfg<BN, STAGES, DRAIN>;
     CUtensorMap th, tl;
@@ -1851,14 +1903,15 @@ int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int 
     auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
-    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr,
+                                             !CONV && k <= PP_MAX_K ? 1 : 0);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 template <int BN, bool CONV, int ACTC, bool DRAIN>
 int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias,
                     float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st,
-                    const ConvGeom& cv, int groups) {
+                    const ConvGeom& cv, int groups, const float* res, int ldr) {
     using C = F32PairCfg<BN, DRAIN>;
     CUtensorMap th, tl;
     if (make_map_2d(&th, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, whi, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
@@ -1869,7 +1922,8 @@ int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo,
     auto kern = k_gemm_tf32x3_pair<BN, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid(2 * ((n + BN - 1) / BN), (m + 2 * BM - 1) / (2 * BM), groups);
-    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr,
+                                             !CONV && k <= PP_MAX_K ? 1 : 0);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -1877,7 +1931,7 @@ int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo,
 // one-tile-per-cluster kernel (with its separate cross-term accumulator) costs the same
 template <int ACTC>
 int launch_f32_pp(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
-                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st) {
+                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const float* res, int ldr) {
     using C = PpCfg;
     auto kern = k_gemm_tf32x3_pp<ACTC>;
     const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + C::BN - 1) / C::BN);
@@ -1891,7 +1945,7 @@ int launch_f32_pp(const float* x, int ldx, const float* whi, const float* wlo, i
         make_map_2d(&tl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wlo, static_cast<uint64_t>(ldw), static_cast<uint64_t>(wrows),
                     static_cast<uint64_t>(ldw) * 4, C::BK, C::BN / 2) != 0)
         return -1;
-    kern<<<2 * clusters, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status);
+    kern<<<2 * clusters, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, res, ldr);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -2144,11 +2198,11 @@ int dispatch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, in
     }
 }
 
-#define KX_F32_ARGS x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups
+#define KX_F32_ARGS x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, cv, groups, res, ldr
 template <int BN, bool CONV, bool DRAIN, bool PAIR>
 int launch_f32_act(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias,
                    float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st,
-                   const ConvGeom& cv, int groups) {
+                   const ConvGeom& cv, int groups, const float* res, int ldr) {
     if constexpr (PAIR) {
         switch (act_class(act)) {
         case -1: return launch_f32_pair<BN, CONV, -1, DRAIN>(KX_F32_ARGS);
@@ -2171,15 +2225,15 @@ int launch_f32_act(const float* x, int ldx, const float* whi, const float* wlo, 
 template <int BN, bool CONV>
 int dispatch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                  int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
-                 int groups) {
+                 int groups, const float* res = nullptr, int ldr = 0) {
     const bool pair = m > BM;
     if (!CONV && BN == 256 && pair && k <= PP_MAX_K) {  // persistent CTA pairs when there is more than one wave
         int r;
         switch (act_class(act)) {
-        case -1: r = launch_f32_pp<-1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st); break;
-        case 0: r = launch_f32_pp<0>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st); break;
-        case 1: r = launch_f32_pp<1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st); break;
-        default: r = launch_f32_pp<ACT_GENERIC>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st);
+        case -1: r = launch_f32_pp<-1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, res, ldr); break;
+        case 0: r = launch_f32_pp<0>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, res, ldr); break;
+        case 1: r = launch_f32_pp<1>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, res, ldr); break;
+        default: r = launch_f32_pp<ACT_GENERIC>(x, ldx, whi, wlo, ldw, wrows, bias, y, ldy, m, n, k, act, alpha, status, st, res, ldr);
         }
         if (r <= 0) return r;
     }
@@ -2231,6 +2285,17 @@ int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, i
     const ConvGeom cv{};
     if (n <= 128) return dispatch_f32<128, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
     return dispatch_f32<256, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
+}
+
+int kx_gemm_f32_res(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
+                    int ldy, int m, int n, int k, int act, float alpha, const float* res, int ldr, int* status, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldx || k > ldw || (ldw & 3) || res == nullptr || ldr < n) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const ConvGeom cv{};
+    if (n <= 128)
+        return dispatch_f32<128, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1, res, ldr);
+    return dispatch_f32<256, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1, res, ldr);
 }
 
 int kx_conv_f32(const float* x, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y, int B, int H,

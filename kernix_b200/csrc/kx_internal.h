@@ -60,6 +60,8 @@ typedef struct {
     float* d_bqkv;
     size_t scratch_per_row; /* bytes of scratch per input row this step needs */
     int shard_c0, shard_n;  /* sharded LINEAR: this rank keeps output columns [shard_c0, shard_c0 + shard_n); 0 = whole */
+    int fuse_add, fuse_res; /* fp32 LINEAR / ATTENTION whose output only feeds the next step, an elementwise ADD: the
+                             * GEMM writes that ADD's output, adding value fuse_res (the ADD's other operand) */
 } kx_step;
 
 /* Parsed graph (host side), the output of kx_graph_load */

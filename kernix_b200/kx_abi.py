@@ -15,6 +15,7 @@ SIGNATURES = {
     "kx_gemm_i8_acc": [_vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _vp, _vp],
     "kx_prep_i8_weight": [_vp, _i, _i, _vp, _i, _vp],
     "kx_gemm_f32": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp],
+    "kx_gemm_f32_res": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _i, _vp, _vp],
     "kx_prep_f32_weight": [_vp, _i, _i, _vp, _vp, _i, _vp],
     "kx_bias_act": [_vp, _vp, _l, _i, _vp, _i, _f, _vp],
     "kx_softmax_rows": [_vp, _vp, _l, _i, _vp],

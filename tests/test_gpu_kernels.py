@@ -227,6 +227,32 @@ def test_gemm_f32_3xtf32(kx, m, k, n, act):
     assert rel_err(got, ref) <= 1e-5
 
 
+@pytest.mark.parametrize("m,k,n,act,inplace", [(100, 300, 200, 0, False), (300, 512, 512, -1, True), (4096, 512, 1536, 1, False),
+                                               (700, 2500, 130, -1, False), (5000, 1000, 520, 0, True)])
+def test_gemm_f32_residual_is_gemm_then_add(kx, m, k, n, act, inplace):
+    """kx_gemm_f32_res (a LINEAR step and the ADD that consumes it, in one kernel) gives bitwise what kx_gemm_f32
+    followed by the elementwise add gives, on every tile kind (one CTA, CTA pairs, persistent pairs, drained K),
+    also in place (y = res)."""
+    rng = np.random.default_rng(m + n)
+    x = rng.standard_normal((m, k)).astype(F32)
+    w = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(F32)
+    b = rng.standard_normal(n).astype(F32)
+    r = rng.standard_normal((m, n)).astype(F32)
+    hi, lo, ldw = _prep_f32(kx, w)
+    st = status()
+    dx, db = dev(x), dev(b)
+    y0 = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    kx.call("kx_gemm_f32", dx.data_ptr(), k, hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y0.data_ptr(), n, m, n, k, act,
+            0.0, st.data_ptr(), sp())
+    want = (host(y0) + r).astype(F32)
+    dr = dev(r)
+    y = dr if inplace else torch.empty((m, n), dtype=torch.float32, device="cuda")
+    kx.call("kx_gemm_f32_res", dx.data_ptr(), k, hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y.data_ptr(), n, m, n, k,
+            act, 0.0, dr.data_ptr(), n, st.data_ptr(), sp())
+    check_status(st)
+    assert np.array_equal(host(y), want)
+
+
 @pytest.mark.parametrize("m,k,n,act", [(4096, 512, 1536, 0), (5000, 1000, 2500, -1), (20000, 100, 1024, 0),
                                        (4352, 1024, 2304, -1)])
 def test_gemm_f32_persistent_pairs(kx, m, k, n, act):

@@ -49,3 +49,27 @@ def test_every_value_matches_oracle(libkx, model_dir, cfg, batch, tol):
     x = configs.inputs(cfg, batch)
     rep = trace_compare(p, x, batch, tol)
     print(cfg, [(f, k, round(e, 9)) for f, k, _, e in rep])
+
+
+@pytest.mark.parametrize("cfg,batch", [("c4", 3), ("c4", 40)])
+def test_fused_forward_equals_step_by_step(libkx, model_dir, cfg, batch):
+    """The forward runs a LINEAR / ATTENTION step and the ADD that consumes its output as one GEMM (the residual added
+    in the epilogue); the trace hook runs every step on its own. Their final outputs are bitwise equal (c4 has one
+    such pair per encoder block for the attention output and one for the feed-forward output; 40 x 128 rows take
+    the persistent tiles)."""
+    from kernix_b200 import Model, configs, kx_abi
+    L = kx_abi.lib()
+    L.kx_model_forward_trace.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    L.kx_model_forward_trace.restype = ctypes.c_int
+    p = configs.model_path(cfg, model_dir)
+    x = configs.inputs(cfg, batch)
+    m = Model(p, workspace_mb=0)
+    got = m(x)
+    xr = np.ascontiguousarray(x.reshape(-1, m.in_dim), np.float32)
+    mod = ko.load(p)
+    n = mod["n_fused_steps"]
+    last = np.empty(got.size, np.float32)
+    ptrs = (ctypes.c_void_p * n)(*([None] * (n - 1) + [last.ctypes.data]))
+    assert L.kx_model_forward_trace(m._h, xr.ctypes.data, xr.shape[0], ptrs) == 0
+    m.close()
+    assert np.array_equal(last.reshape(got.shape), got)
