@@ -528,7 +528,10 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // KC_BLOCKS K blocks (256 K) into two alternating TMEM buffers, and the epilogue warps add every chunk into an fp32
 // running sum in a third region with round-to-nearest adds (((P0 + P1) + P2) + ..., a fixed order), which bounds
 // the truncated accumulation length by 32 MMAs: about 5e-7 per layer at any K. The result is running sum (or
-// Ah.Bh sum) + cross terms, rounded to nearest.
+// Ah.Bh sum) + cross terms, rounded to nearest. Dense products with K <= PP_MAX_K (1024) instead sum all three
+// products in one accumulator (Ah.Bh, Al.Bh, Ah.Bl per 8 K; ~6e-6 of the output scale at K = 1024) in every tile
+// kind, because the persistent kernel has no TMEM left for a separate one and a row's result must not depend on
+// which tile kind its GEMM's row count selects.
 // shared-memory bytes of the control block; the tile's bias (BN floats) follows it
 constexpr int F32_CTL_BYTES = (static_cast<int>(sizeof(SmemCtl)) + 15) & ~15;
 // warps per TMEM lane quarter in the final epilogue: the epilogue warp and the two converter warps of that quarter
