@@ -682,7 +682,8 @@ static int host_page_locked(const void* p) {
  * the two copy directions overlap each other. Piece p of every chunk reuses arena region p: its input copy waits
  * until the last user of region p has been computed and copied out, and its kernels wait for that copy-out too.
  * Rows never mix across pieces, so the result is the same for any cut (the chunking invariance of
- * include/kernix_model.h:1691-1694). Into page-locked memory a piece's output copy is queued right after its
+ * include/kernix_model.h:1691-1694): bit for bit, except that a piece too small for the persistent 3xTF32 tiles
+ * (which sum their three products in one accumulator) differs from a whole run by at most ~6e-6 of the scale. Into page-locked memory a piece's output copy is queued right after its
  * kernels, so that it never waits for the host to queue the later pieces; into pageable memory (a copy that returns
  * only when done) the copies of a chunk are queued after all of its kernels, so that they do not hold back the
  * later pieces' launches. */
@@ -749,7 +750,8 @@ static int forward_enqueue_host(kernix_model* m, const float* x, int rows, float
  * the kernels) run with 1, 2, 3, 4, 6 and 8 pieces in turn, each timed on the device from its last chunk's first
  * input copy to its last output copy, and the fastest count is kept from then on. How many pieces pay depends on
  * the model (kernels that are much longer than the copies want one, kernels that lose efficiency on small pieces
- * want few) and on the link, so it is measured rather than guessed. The result does not depend on the count. */
+ * want few) and on the link, so it is measured rather than guessed. The result does not depend on the count (to
+ * the bit, or within ~6e-6 where the persistent tiles apply to the whole but not to a piece). */
 static const int kx_pipe_cand[] = {1, 2, 3, 4, 6, 8};
 #define KX_PIPE_NCAND ((int)(sizeof kx_pipe_cand / sizeof kx_pipe_cand[0]))
 static void pipe_tune(struct kx_model_impl* im) {

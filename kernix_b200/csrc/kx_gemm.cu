@@ -528,10 +528,8 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // KC_BLOCKS K blocks (256 K) into two alternating TMEM buffers, and the epilogue warps add every chunk into an fp32
 // running sum in a third region with round-to-nearest adds (((P0 + P1) + P2) + ..., a fixed order), which bounds
 // the truncated accumulation length by 32 MMAs: about 5e-7 per layer at any K. The result is running sum (or
-// Ah.Bh sum) + cross terms, rounded to nearest. Dense products with K <= PP_MAX_K (1024) instead sum all three
-// products in one accumulator (Ah.Bh, Al.Bh, Ah.Bl per 8 K; ~6e-6 of the output scale at K = 1024) in every tile
-// kind, because the persistent kernel has no TMEM left for a separate one and a row's result must not depend on
-// which tile kind its GEMM's row count selects.
+// Ah.Bh sum) + cross terms, rounded to nearest. The persistent kernel (k_gemm_tf32x3_pp) alone sums all three
+// products in one accumulator (no TMEM left for a separate one): ~6e-6 of the output scale at K = 1024.
 // shared-memory bytes of the control block; the tile's bias (BN floats) follows it
 constexpr int F32_CTL_BYTES = (static_cast<int>(sizeof(SmemCtl)) + 15) & ~15;
 // warps per TMEM lane quarter in the final epilogue: the epilogue warp and the two converter warps of that quarter
@@ -787,14 +785,14 @@ template <int BN, int ACTC>
 __device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross, bool ok, int row0, int lane, int n0,
                                                const float* sbias, bool has_bias, float* __restrict__ y, int ldy,
                                                int M, int N, int act, float alpha, float4* stg, int part,
-                                               const float* __restrict__ res, int ldr, bool add_cross) {
+                                               const float* __restrict__ res, int ldr) {
     const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
     const bool rvec = ((ldr & 3) == 0) && ((reinterpret_cast<uintptr_t>(res) & 15) == 0);
 #pragma unroll 1
     for (int c0 = 32 * part; c0 < BN; c0 += 32 * F32_EPI_PARTS) {
         uint32_t r[32], x[32];
         kx::tmem_ld32(t_sum + c0, r);
-        if (add_cross) kx::tmem_ld32(t_cross + c0, x);
+        kx::tmem_ld32(t_cross + c0, x);
         const int col0 = n0 + c0;
         float4 rv[8];
         if (res && ok) load_residual(res, ldr, rvec, row0, col0, lane, M, N, rv);
@@ -808,8 +806,7 @@ __device__ __forceinline__ void f32_store_tile(uint32_t t_sum, uint32_t t_cross,
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                float t = __uint_as_float(r[4 * j4 + e]);
-                if (add_cross) t = __fadd_rn(t, __uint_as_float(x[4 * j4 + e]));
+                float t = __fadd_rn(__uint_as_float(r[4 * j4 + e]), __uint_as_float(x[4 * j4 + e]));
                 if (has_bias) t = __fadd_rn(t, bb[e]);
                 v[e] = epi_act<ACTC>(t, act, alpha);
             }
@@ -841,7 +838,7 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
               const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
               int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv, const float* __restrict__ res,
-              int ldr, int combine) {
+              int ldr) {
     using C = F32Cfg<BN, STAGES, DRAIN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
@@ -921,12 +918,6 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
 #pragma unroll
                 for (int kk = 0; kk < C::BK / 8; kk++) {
                     const uint32_t o = kk * 32;  // 8 tf32 = 32 bytes of K per MMA
-                    if (!DRAIN && combine) {  // the three products in one accumulator, in k_gemm_tf32x3_pp's order
-                        kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
-                        kx::mma_tf32(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
-                        kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
-                        continue;
-                    }
                     kx::mma_tf32(dx, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
                     kx::mma_tf32(dx, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
                     kx::mma_tf32(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
@@ -970,7 +961,7 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
         const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
         f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
                                  n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
-                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part, res, ldr, DRAIN || !combine);
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part, res, ldr);
     }
     kx::tc_fence_before();
     __syncthreads();
@@ -1565,7 +1556,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
                    const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y,
                    int ldy, int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv,
-                   const float* __restrict__ res, int ldr, int combine) {
+                   const float* __restrict__ res, int ldr) {
     using C = F32PairCfg<BN, DRAIN>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -1650,12 +1641,6 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
 #pragma unroll
                 for (int kk = 0; kk < C::BK / 8; kk++) {
                     const uint32_t o = kk * 32;
-                    if (!DRAIN && combine) {  // the three products in one accumulator, in k_gemm_tf32x3_pp's order
-                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
-                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, 1);
-                        kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
-                        continue;
-                    }
                     kx::mma_tf32_pair(dx, kx::desc_sw128_kmajor(al + o), kx::desc_sw128_kmajor(bh + o), idesc, (kb | kk) != 0);
                     kx::mma_tf32_pair(dx, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bl + o), idesc, 1);
                     kx::mma_tf32_pair(d, kx::desc_sw128_kmajor(ah + o), kx::desc_sw128_kmajor(bh + o), idesc, (kc | kk) != 0);
@@ -1708,7 +1693,7 @@ k_gemm_tf32x3_pair(const float* __restrict__ A, int lda, const __grid_constant__
         const bool ok = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
         f32_store_tile<BN, ACTC>(tmem + lanes + (DRAIN ? C::RUN : C::MAIN0), tmem + lanes + C::CROSS, ok, m0 + q * 32, lane,
                                  n0, sbias, bias != nullptr, y, ldy, M, N, act, alpha,
-                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part, res, ldr, DRAIN || !combine);
+                                 reinterpret_cast<float4*>(smem + (warp - 2) * 8192), part, res, ldr);
     }
     kx::tc_fence_before();
     kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
@@ -1906,8 +1891,7 @@ int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int 
     auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
-    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr,
-                                             !CONV && k <= PP_MAX_K ? 1 : 0);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -1925,8 +1909,7 @@ int launch_f32_pair(const float* x, int ldx, const float* whi, const float* wlo,
     auto kern = k_gemm_tf32x3_pair<BN, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
     dim3 grid(2 * ((n + BN - 1) / BN), (m + 2 * BM - 1) / (2 * BM), groups);
-    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr,
-                                             !CONV && k <= PP_MAX_K ? 1 : 0);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -52,11 +52,12 @@ def test_every_value_matches_oracle(libkx, model_dir, cfg, batch, tol):
 
 
 @pytest.mark.parametrize("cfg,batch", [("c4", 3), ("c4", 40)])
-def test_fused_forward_equals_step_by_step(libkx, model_dir, cfg, batch):
+def test_fused_forward_equals_step_by_step(libkx, model_dir, monkeypatch, cfg, batch):
     """The forward runs a LINEAR / ATTENTION step and the ADD that consumes its output as one GEMM (the residual added
-    in the epilogue); the trace hook runs every step on its own. Their final outputs are bitwise equal (c4 has one
-    such pair per encoder block for the attention output and one for the feed-forward output; 40 x 128 rows take
-    the persistent tiles)."""
+    in the epilogue); the trace hook runs every step on its own. With the same rows per GEMM (one piece) their final
+    outputs are bitwise equal (c4 has one such pair per encoder block for the attention output and one for the
+    feed-forward output; 40 x 128 rows take the persistent tiles)."""
+    monkeypatch.setenv("KERNIX_PIPELINE", "1")
     from kernix_b200 import Model, configs, kx_abi
     L = kx_abi.lib()
     L.kx_model_forward_trace.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
