@@ -50,7 +50,9 @@ def parse():
                     help="profiling case: only run the int8 GEMM of c2's 4096x4096 layer with M rows, 3 launches, then exit")
     ap.add_argument("--kernel-k", type=int, default=4096, help="K of the profiling case (1024: c2's first layer)")
     ap.add_argument("--kernel-act", type=int, default=1, help="activation of the profiling case (1 GELU, -1 none)")
-    ap.add_argument("--kernel-dtype", choices=["i8", "f32"], default="i8", help="GEMM of the profiling case")
+    ap.add_argument("--kernel-dtype", choices=["i8", "f32", "attn"], default="i8",
+                    help="kernel of the profiling case: int8 or 3xTF32 GEMM, or (attn) the attention core on c4's shape "
+                         "(M samples x 128 positions, 8 heads of 64)")
     ap.add_argument("--workload", choices=["c2", "c5-rows", "c1", "c3", "c4", "c5"], default="c2",
                     help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
                          "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling). c1, c3, c4, "
@@ -73,6 +75,18 @@ def kernel_case(m_rows, k=4096, act=1, dtype="i8"):
     L = kx_abi.lib()
     n = 4096
     rng = np.random.default_rng(0)
+    if dtype == "attn":  # c4's attention core: S = 128, 8 heads, d = 64, Q / K / V packed in one row as the model does
+        S, H, d = 128, 8, 64
+        qkv = torch.from_numpy(rng.standard_normal((m_rows * S, 3 * H * d)).astype(np.float32)).cuda()
+        ctx = torch.empty((m_rows * S, H * d), device="cuda")
+        ld, base = 3 * H * d, qkv.data_ptr()
+        for _ in range(3):
+            kx_abi.call("kx_attention", base, ld, base + 4 * H * d, ld, base + 8 * H * d, ld, ctx.data_ptr(), H * d, m_rows, S, S,
+                        H, d, d, 0, None, None)
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel_case": "k_attention_tc", "samples": m_rows, "seq": S, "heads": H, "head_dim": d,
+                          "launches": 3}))
+        return
     if dtype == "f32":
         ldw = (k + 31) // 32 * 32
         w = torch.from_numpy((rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)).cuda()
