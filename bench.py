@@ -12,6 +12,10 @@ the path has no cross-sample exchange, so there is no collective in the data pat
   roofline     the dominant kernel (tcgen05 kind::i8 GEMM, all three layers), algorithmic int8 ops / CUDA-event time
   cpu_baseline the reference's own CPU forward (oracle/_ref, compiled from the reference sources) on a bounded
                sample, all host threads (one model instance per thread; the reference's forward is per-model serial)
+  per_config   (N = 1) every other configuration at its benchmark batch -- c1 256, c2 32, c3 1024, c4 512, c5 1 and
+               256 -- device-resident samples/s with the achieved rate and its fraction of the bound at that batch
+
+  --impl reference times the reference's CPU forward on the same 4096-sample c2 batch per step, all host threads.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kernix|reference]
 """
@@ -34,8 +38,9 @@ DIMS = [1024, 4096, 4096, 1024]
 METRIC = "samples/s, int8 MLP 1024-4096-4096-1024 (config c2), batch 4096 per GPU"
 WORKLOAD = "c2: int8-quantised MLP 1024-4096-4096-1024, GELU hidden, I8_COL per-output-channel weights, batch 4096"
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) per int8-GEMM op from the ncu capture in profiles/k_gemm_i8_pair_8192x4096x4096_full.md:
-# 167.3 MB for 274.9 GOP; the roofline's traffic per launch is this ratio times the launch's ops.
+# DRAM bytes (read + write) per int8-GEMM op from an ncu capture of the int8 GEMM at M = 8192, K = N = 4096 with GELU
+# (dram__bytes_read.sum + dram__bytes_write.sum): 167.3 MB for 274.9 GOP; the roofline's traffic per launch is this
+# ratio times the launch's ops.
 GEMM_DRAM_BYTES_PER_OP = 167.3e6 / 274.9e9
 
 
@@ -57,6 +62,8 @@ def parse():
                     help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
                          "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling). c1, c3, c4, "
                          "c5: the device-resident forward of that configuration at --batch samples per GPU")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per_config object (the other configurations at their benchmark batch sizes)")
     ap.add_argument("--batch", type=int, default=0,
                     help="samples per step: global batch of c5-rows (default 64), per-GPU batch of c1/c3/c4/c5 "
                          "(default: the configuration's own, 256 / 1024 / 512 / 256)")
@@ -159,7 +166,23 @@ def reference_throughput(path, seconds, samples_per_call=8, threads=None):
     return n / dt, threads, n, dt
 
 
+def cpu_model():
+    """The host CPU's model name (first 'model name' of /proc/cpuinfo), or the platform's processor string."""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.lower().startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def run_reference(args):
+    """The reference arm: the reference's own CPU forward (oracle/_ref, include/kernix_model.h compiled from its
+    sources) on the same workload as the GPU arm -- config c2, 4096 samples per step -- with every host thread:
+    the 4096 samples are split over one reference model per thread (kernix_model_forward is serial per model and
+    models may run concurrently), each at the reference's default workspace limit."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -169,12 +192,13 @@ def run_reference(args):
         return
     path = model_file(0)
     threads = os.cpu_count() or 1
-    per_step = max(8, threads * 2)  # samples per step: a bounded sample of the workload
+    per_step = BATCH  # the GPU arm's batch: same configuration, same samples per step
     from oracle import ref_lib as rl
     from kernix_b200 import configs
     models = [rl.RefModel(path) for _ in range(threads)]
-    x = configs.inputs(CFG, per_step, seed=7)
-    chunks = [x[i::threads] for i in range(threads)]
+    x = configs.inputs(CFG, per_step, seed=100)
+    bounds = [per_step * i // threads for i in range(threads + 1)]
+    chunks = [x[bounds[i]:bounds[i + 1]] for i in range(threads)]
 
     def step():
         ts = [threading.Thread(target=models[i].forward, args=(chunks[i],)) for i in range(threads) if len(chunks[i])]
@@ -192,11 +216,16 @@ def run_reference(args):
     v = per_step * args.steps / dt
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_step": per_step},
-            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "kind": "reference",
-                             "sample": f"{per_step} samples per step, split over {threads} threads, one reference model each"},
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic: inputs ~N(0,1) seed 100, random-init weights ~N(0,0.02)",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "global_batch": per_step,
+                       "parallelism": f"{threads} host threads, one reference model each"},
+            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": threads, "cpu": cpu_model(), "kind": "reference",
+                             "sample": f"the full {per_step}-sample batch per step, split over {threads} threads with one "
+                                       "reference model each (default workspace: the int8 layers run the reference's "
+                                       "kernix_qmatmul scalar loop on x86)"},
             "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    for m in models:
+        m.close()
     print(json.dumps(line), flush=True)
 
 
@@ -375,11 +404,16 @@ def run_kernix(args):
         from oracle import ref_lib
         if ref_lib.available():
             v, thr, n, dt = reference_throughput(path, args.cpu_seconds)
-            cpu = {"value": v, "unit": "samples/s", "cores": thr, "kind": "reference",
+            cpu = {"value": v, "unit": "samples/s", "cores": thr, "cpu": cpu_model(), "kind": "reference",
                    "sample": f"{n} samples of the c2 workload in {dt:.1f} s, {thr} threads with one reference model each "
                              "(default workspace: int8 layers run the reference's kernix_qmatmul scalar loop on x86)"}
         else:
             cpu = {"value": None, "unit": "samples/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
+
+    # ---- the other configurations at their benchmark batch sizes (rank 0 at N = 1 only)
+    per_config = None
+    if rank == 0 and world == 1 and not args.no_per_config:
+        per_config = measure_configs(L, torch, flush, stream, max(5, args.steps // 2), 3)
 
     if rank == 0:
         peaks = {}
@@ -398,6 +432,7 @@ def run_kernix(args):
                     "d2h_bytes_per_step": BATCH * DIMS[-1] * 4, "api": "kernix_capi_forward, page-locked host buffers"},
             "roofline": roof,
             "cpu_baseline": cpu,
+            "per_config": per_config,
             "clocks": clk.summary(),
             "gpu_launches": 6 * args.steps,
             "peaks_file": bool(peaks),
@@ -457,6 +492,80 @@ def gemm_roofline(L, torch, np, steps, flush):
             "traffic": GEMM_DRAM_BYTES_PER_OP * tot_ops / len(per),
             "traffic_note": "bytes per launch, scaled by ops from the ncu capture of M=8192 (profiles/)", "per_layer": per,
             "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
+
+
+def _peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured (MEASURED_PEAKS.json)"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# (configuration, batch) of the per_config object: every configuration at the batch its benchmark names
+PER_CONFIG = [("c1", 256), ("c2", 32), ("c3", 1024), ("c4", 512), ("c5", 1), ("c5", 256)]
+# algorithmic bytes one forward must move when it is bound by weight streaming: c2's int8 weights (+ scales and
+# biases), c5's fp32 weights (+ biases)
+WEIGHT_BYTES = {"c2": 1024 * 4096 + 4096 * 4096 + 4096 * 1024 + 8 * (4096 + 4096 + 1024),
+                "c5": 4 * (8192 * 16384 + 16384 * 16384 + 16384 * 8192) + 4 * (16384 + 16384 + 8192)}
+DOMINANT = {"c1": "k_gemm_tf32x3 (3xTF32 tcgen05, one CTA per 128-row tile)",
+            "c2": "k_gemm_i8 / k_gemm_i8_pair (tcgen05 kind::i8) streaming the int8 weights",
+            "c3": "k_conv_tf32x3_cmt (3xTF32 tcgen05 implicit-GEMM convolution fed by TMA)",
+            "c4": "k_gemm_tf32x3_pp / k_gemm_tf32x3_pair (3xTF32 tcgen05 GEMMs)",
+            "c5@1": "k_skinny (fp32 weight streaming on the CUDA cores)",
+            "c5@256": "k_gemm_tf32x3_pair (3xTF32 tcgen05, drained long reductions)"}
+
+
+def measure_configs(L, torch, flush, stream, steps, warmup):
+    """Device-resident forward (kernix_model_forward_device, inputs in HBM) of every configuration at its benchmark
+    batch: CUDA events on the launching stream per step, L2 flushed (256 MB write) before each, the mean over the
+    steps. Each entry gives samples/s, the achieved algorithmic rate and its fraction of the bound the
+    configuration has at that batch: the 3xTF32 rate (measured dense bf16 burst / 2 for tf32, / 3 for the three
+    products) for the tensor-bound ones, measured HBM bandwidth on the weight bytes for the weight-streaming ones
+    (c2 at 32 rows, c5 at 1 row). The fraction is of the whole forward, so it bounds its dominant kernel's from below."""
+    from kernix_b200 import Model, configs
+    peaks, basis = _peaks()
+    tf32x3 = float(peaks["bf16_tflops"]) / 2 / 3
+    hbm = float(peaks["hbm_gbs"])
+    out = {}
+    model_dir = os.environ.get("KERNIX_MODEL_DIR", "/tmp/kernix_models_r0")
+    for cfg, B in PER_CONFIG:
+        m = Model(configs.model_path(cfg, model_dir), workspace_mb=0)
+        x = torch.from_numpy(configs.inputs(cfg, B, seed=100)).cuda()
+        y = torch.empty((B, m.out_dim), dtype=torch.float32, device="cuda")
+
+        def step():
+            if L.kernix_model_forward_device(m._h, x.data_ptr(), x.shape[0], y.data_ptr(), stream.cuda_stream) != 0:
+                raise RuntimeError(f"forward_device failed on {cfg}")
+
+        for _ in range(warmup):
+            step()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        if L.kernix_model_check(m._h) != 0:
+            raise RuntimeError(f"a kernel reported a failure on {cfg}")
+        t = sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3 / steps
+        m.close()
+        del x, y
+        key = f"{cfg}@{B}"
+        e = {"batch": B, "samples_per_s": B / t, "ms_per_forward": t * 1e3,
+             "dominant_kernel": DOMINANT.get(key, DOMINANT.get(cfg))}
+        if cfg == "c2":  # 32 rows: weight streaming (the 25 MB of int8 weights leave L2 with the flush)
+            gbs = WEIGHT_BYTES["c2"] / t / 1e9
+            e.update(bound="hbm", achieved=gbs, unit="GB/s", frac=gbs / hbm, achieved_tops=2 * 25165824 * B / t / 1e12)
+        elif cfg == "c5" and B <= 16:
+            gbs = WEIGHT_BYTES["c5"] / t / 1e9
+            e.update(bound="hbm", achieved=gbs, unit="GB/s", frac=gbs / hbm, achieved_tflops=CONFIG_FLOPS[cfg] * B / t / 1e12)
+        else:
+            tf = CONFIG_FLOPS[cfg] * B / t / 1e12
+            e.update(bound="tensor (3xTF32)", achieved=tf, unit="TFLOP/s", frac=tf / tf32x3)
+        out[key] = e
+    out["peaks"] = {"basis": basis, "hbm_gbs": hbm, "tf32x3_tflops": tf32x3}
+    return out
 
 
 # algorithmic FLOPs per sample (2 per MAC) of the configurations, and their default batch

@@ -47,8 +47,10 @@ KERNIX_API int kx_linear_i8(const float* x, int ldx, int rows, int k, const int8
  * reference. Same arguments and result as kx_linear_i8 minus the two scratch buffers: they come from one
  * KX_NOALLOC_SCRATCH_BYTES array compiled into the library (held on every GPU that loads it until exit), so
  * rows * (k rounded up to 16) + 4 * rows (+ alignment) must fit, else it returns -1 with a message. The first call on
- * a device looks the array up (cudaGetSymbolAddress); make it before any stream capture. Calls share the array:
- * calls whose work overlaps on the GPU race, so order them on one stream. Allocates nothing. */
+ * a device (per CUDA context) loads the module that holds the array, which reserves its 16 MiB there, and looks
+ * the array up (cudaGetSymbolAddress): make that call in initialisation code, before any stream capture. Later
+ * calls in the same context allocate nothing; after cudaDeviceReset the next call looks the array up again.
+ * Calls share the array: calls whose work overlaps on the GPU race, so order them on one stream. */
 #define KX_NOALLOC_SCRATCH_BYTES (16 << 20)
 KERNIX_API int kx_linear_i8_noalloc(const float* x, int ldx, int rows, int k, const int8_t* wq, int ldw, const float* scale,
                                     const float* bias, float* y, int ldy, int n, int act, float alpha, int* status,

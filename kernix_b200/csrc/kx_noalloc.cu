@@ -5,15 +5,23 @@
 // not allow extra allocations. kx_linear_i8 needs two scratch buffers (the int8 activations and the per-row
 // scales); this variant takes them from one fixed array compiled into the library instead of from the caller.
 //
-// The array below is a file-scope __device__ object: every GPU that loads the library holds its
-// KX_NOALLOC_SCRATCH_BYTES until the process exits. Host code cannot use the array's name as a device address, so
-// the first call on each device looks the address up with cudaGetSymbolAddress (with that device current) and
-// caches it; make that first call before any stream capture. Nothing here calls cudaMalloc or cudaFree.
+// The array below is a file-scope __device__ object of KX_NOALLOC_SCRATCH_BYTES. With CUDA's default lazy module
+// loading it comes into existence on a device the first time this file's module is needed there: the first call
+// of this entry point on each device (in its CUDA context) loads the module, which reserves the array, and looks
+// the array's device address up with cudaGetSymbolAddress, with that device current. So that first call is the
+// one that may take device memory and synchronise; make it in initialisation code, before any stream capture.
+// Later calls in the same context reuse the cached address and allocate nothing; the array then stays reserved
+// until the process exits (or the context is destroyed). Host code cannot use the array's name as a device
+// address, which is why the address is looked up rather than taken. Nothing here calls cudaMalloc or cudaFree.
 //
-// All calls on a device share the one array. Every byte a call reads is written earlier in the same call (the
+// The cached address belongs to one CUDA context: it is keyed by device and by the context current at the call,
+// so after cudaDeviceReset (a new primary context) or under a different driver context it is looked up again.
+//
+// All calls in a context share the one array. Every byte a call reads is written earlier in the same call (the
 // quantiser writes all rows, including the zero padding up to the 16-byte row pitch, and every row scale), so no
 // state carries over between calls and nothing needs clearing. Two calls whose work overlaps on the GPU (different
 // streams, or other threads) race on the array and corrupt each other's results: order them on one stream.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -27,25 +35,57 @@ namespace {
 static __device__ __align__(256) uint8_t g_noalloc_scratch[KX_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-uint8_t* g_scratch_ptr[kMaxDevices] = {nullptr};
+struct Cached {
+    CUcontext ctx;
+    uint8_t* ptr;
+};
+Cached g_cache[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
-// device address of the array on the current device, looked up once per device
-uint8_t* scratch_on_current_device() {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links no libcuda stub)
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return static_cast<CtxGetCurrentFn>(nullptr);
+        }
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    return fn;
+}
+
+// device address of the array in the current context, looked up once per (device, context)
+uint8_t* scratch_in_current_context() {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    CUcontext ctx = nullptr;
+    CtxGetCurrentFn get = ctx_get_current();
+    if (get != nullptr) get(&ctx);  // NULL before the runtime made its context current: then the lookup below does
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (g_scratch_ptr[dev] == nullptr) {
+    Cached& c = g_cache[dev];
+    if (c.ptr == nullptr || ctx == nullptr || c.ctx != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) {
+            cudaGetLastError();  // leave no error behind for the next, unrelated launch check
             std::fprintf(stderr, "kx_linear_i8_noalloc: cannot locate the scratch array on device %d: %s\n", dev,
                          cudaGetErrorString(e));
+            c.ptr = nullptr;
             return nullptr;
         }
-        g_scratch_ptr[dev] = static_cast<uint8_t*>(p);
+        if (ctx == nullptr && get != nullptr) get(&ctx);  // the lookup made the primary context current
+        c.ctx = ctx;
+        c.ptr = static_cast<uint8_t*>(p);
     }
-    return g_scratch_ptr[dev];
+    return c.ptr;
 }
 
 }  // namespace
@@ -66,7 +106,7 @@ extern "C" int kx_linear_i8_noalloc(const float* x, int ldx, int rows, int k, co
                      rows, k, need, KX_NOALLOC_SCRATCH_BYTES);
         return -1;
     }
-    uint8_t* base = scratch_on_current_device();
+    uint8_t* base = scratch_in_current_context();
     if (base == nullptr) return -1;
     int8_t* xq = reinterpret_cast<int8_t*>(base);
     float* sx = reinterpret_cast<float*>(base + sx_off);

@@ -30,6 +30,37 @@ std::unordered_map<const void*, size_t> g_live;  // backend storage -> bytes
 std::vector<std::pair<void*, size_t>> g_cache;   // freed storage, oldest first
 size_t g_cache_bytes = 0;
 
+// scratch of kernix_matmul_ep_into: one buffer per device, grown to the largest product seen, released by
+// kernix_metal_release_cache; callers hold g_mm_mu for the whole product
+constexpr int TB_MAX_DEVICES = 64;
+std::mutex g_mm_mu;
+struct MmScratch {
+    void* p;
+    size_t cap;
+};
+MmScratch g_mm[TB_MAX_DEVICES] = {};
+
+uint8_t* mm_scratch(size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= TB_MAX_DEVICES) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    MmScratch& s = g_mm[dev];
+    if (s.cap < bytes) {
+        if (s.p != nullptr) cudaFree(s.p);
+        s.p = nullptr;
+        s.cap = 0;
+        if (cudaMalloc(&s.p, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            s.p = nullptr;
+            return nullptr;
+        }
+        s.cap = bytes;
+    }
+    return static_cast<uint8_t*>(s.p);
+}
+
 bool is_backend(const void* p, size_t bytes) {
     std::lock_guard<std::mutex> g(g_mu);
     const auto it = g_live.find(p);
@@ -273,6 +304,17 @@ void kernix_metal_release_cache(void) {
         g_cache_bytes = 0;
     }
     for (auto& e : drop) cudaFreeHost(e.first);
+    std::lock_guard<std::mutex> lock(g_mm_mu);
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (int d = 0; d < TB_MAX_DEVICES; ++d) {
+        if (g_mm[d].p == nullptr) continue;
+        cudaSetDevice(d);
+        cudaFree(g_mm[d].p);
+        g_mm[d] = MmScratch{};
+    }
+    cudaSetDevice(cur);
+    cudaGetLastError();
 }
 
 size_t kernix_metal_map(int op, const float* x, const float* b, size_t bcols, float* y, size_t n, float p0, float p1) {
@@ -348,36 +390,40 @@ int kernix_matmul_ep_into(const float_tensor* a, const float_tensor* b, float_te
         if (cpu_ep != nullptr) cpu_ep(0, static_cast<size_t>(m));
         return 0;
     }
-    // device copies: A (m x k), B (k x n) split into the tf32 planes (n x ldw), bias, C
+    // device copies: A (m x k), B (k x n) split into the tf32 planes (n x ldw), bias, C, status word; all carved
+    // from one per-device scratch buffer that only grows, so repeated products allocate nothing
     const int ldw = (k + 31) / 32 * 32;
-    float *da = nullptr, *dw = nullptr, *dhi = nullptr, *dlo = nullptr, *dbias = nullptr, *dc = nullptr;
-    int* dst = nullptr;
     const size_t sa = static_cast<size_t>(m) * k, sw = static_cast<size_t>(k) * n, sp = static_cast<size_t>(n) * ldw,
                  sc = static_cast<size_t>(m) * n;
-    bool ok = cudaMalloc(reinterpret_cast<void**>(&da), sa * 4) == cudaSuccess &&
-              cudaMalloc(reinterpret_cast<void**>(&dw), sw * 4) == cudaSuccess &&
-              cudaMalloc(reinterpret_cast<void**>(&dhi), sp * 4) == cudaSuccess &&
-              cudaMalloc(reinterpret_cast<void**>(&dlo), sp * 4) == cudaSuccess &&
-              cudaMalloc(reinterpret_cast<void**>(&dc), sc * 4) == cudaSuccess &&
-              cudaMalloc(reinterpret_cast<void**>(&dst), sizeof(int)) == cudaSuccess &&
-              (bias == nullptr || cudaMalloc(reinterpret_cast<void**>(&dbias), static_cast<size_t>(n) * 4) == cudaSuccess);
-    ok = ok && cudaMemset(dst, 0, sizeof(int)) == cudaSuccess &&
-         cudaMemcpy(da, a->tensor, sa * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemcpy(dw, b->tensor, sw * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
-         (bias == nullptr || cudaMemcpy(dbias, bias, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice) == cudaSuccess);
+    const size_t parts[7] = {sa * 4, sw * 4, sp * 4, sp * 4, sc * 4, static_cast<size_t>(n) * 4, sizeof(int)};
+    size_t offs[7], total = 0;
+    for (int i = 0; i < 7; ++i) {
+        offs[i] = total;
+        total += (parts[i] + 255) / 256 * 256;
+    }
+    std::lock_guard<std::mutex> lock(g_mm_mu);
+    uint8_t* base = mm_scratch(total);
+    if (base == nullptr) {
+        std::fprintf(stderr, "matmul: no device memory for a %dx%dx%d product\n", m, k, n);
+        return -1;
+    }
+    float* da = reinterpret_cast<float*>(base + offs[0]);
+    float* dw = reinterpret_cast<float*>(base + offs[1]);
+    float* dhi = reinterpret_cast<float*>(base + offs[2]);
+    float* dlo = reinterpret_cast<float*>(base + offs[3]);
+    float* dc = reinterpret_cast<float*>(base + offs[4]);
+    float* dbias = bias ? reinterpret_cast<float*>(base + offs[5]) : nullptr;
+    int* dst = reinterpret_cast<int*>(base + offs[6]);
+    bool ok = cudaMemsetAsync(dst, 0, sizeof(int), nullptr) == cudaSuccess &&
+              cudaMemcpy(da, a->tensor, sa * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              cudaMemcpy(dw, b->tensor, sw * 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+              (bias == nullptr || cudaMemcpy(dbias, bias, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice) == cudaSuccess);
     ok = ok && kx_prep_f32_weight(dw, k, n, dhi, dlo, ldw, nullptr) == 0 &&
          kx_gemm_f32(da, k, dhi, dlo, ldw, dbias, dc, n, m, n, k, act, alpha, dst, nullptr) == 0 &&
          cudaDeviceSynchronize() == cudaSuccess;
     int status = 1;
     ok = ok && cudaMemcpy(&status, dst, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && status == 0 &&
          cudaMemcpy(c->tensor, dc, sc * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
-    cudaFree(da);
-    cudaFree(dw);
-    cudaFree(dhi);
-    cudaFree(dlo);
-    cudaFree(dbias);
-    cudaFree(dc);
-    cudaFree(dst);
     if (!ok) {
         cudaGetLastError();
         std::fprintf(stderr, "matmul: the GPU product failed\n");

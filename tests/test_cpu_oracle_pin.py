@@ -96,7 +96,7 @@ def test_int8_int32_edge():
 
 @pytest.mark.reference
 @pytest.mark.skipif(not ref_lib.available(), reason="compiled reference (oracle/_ref) not built here")
-@pytest.mark.parametrize("cfg,batch", [("c1", 16), ("c2", 3), ("c3", 2), ("c4", 1)])
+@pytest.mark.parametrize("cfg,batch", [("c1", 16), ("c2", 3), ("c3", 2), ("c4", 1), ("c5", 3)])
 def test_oracle_matches_reference_on_configs(cfg, batch, tmp_path):
     from kernix_b200 import configs
     p = configs.model_path(cfg, str(tmp_path))
@@ -105,6 +105,7 @@ def test_oracle_matches_reference_on_configs(cfg, batch, tmp_path):
         m.set_workspace_limit(1)
     x = configs.inputs(cfg, batch)
     assert rel_err(ko.forward(ko.load(p), x), m.forward(x)) <= (1e-4 if cfg == "c2" else 1e-5)
+    m.close()
 
 
 def rnn_model(path, kind, T, cin, u, dirs, merge, ret_seq, act, int8, rng):

@@ -43,6 +43,60 @@ def test_config_matches_oracle(Model, model_dir, cfg, batch):
     assert rel_err(got.reshape(want.shape), want) <= TOL[cfg]
 
 
+_ORACLE_MODELS = {}
+
+
+def _oracle_model(p):
+    if p not in _ORACLE_MODELS:
+        _ORACLE_MODELS.clear()  # one at a time: c5's oracle copy is 2 GB
+        _ORACLE_MODELS[p] = ko.load(p)
+    return _ORACLE_MODELS[p]
+
+
+def _sample_ids(batch):
+    """First and last samples, both sides of the 128- and 256-row tile and piece boundaries, the middle."""
+    ids = {0, 1, batch // 2 - 1, batch // 2, batch - 2, batch - 1, 127, 128, 255, 256, 511, 512, 1023}
+    return np.array(sorted(i for i in ids if 0 <= i < batch))
+
+
+@pytest.mark.parametrize("cfg,batch", [("c2", 32), ("c3", 1024), ("c4", 512), ("c5", 1), ("c5", 64), ("c5", 256),
+                                       ("c5", 1024)])
+def test_config_at_its_benchmark_batch(Model, libkx, model_dir, cfg, batch):
+    """Every configuration at the batch sizes the benchmark names (c2 at 32 besides 4096, c3 at 1024, c4 at 512,
+    c5 over its sweep), through the public host API (kernix_capi_forward via the binding) and through the
+    device-resident forward the benchmark times (kernix_model_forward_device, one launch sequence over the whole
+    batch, so the same tile kinds as the bench): sampled samples against the oracle run on those samples only
+    (samples are independent), within the north star's bound for the configuration (c2 end to end 1e-4, c3 / c4
+    1e-4, c5 1e-5 of the output scale); the two paths agree with each other bit for bit or within the bound."""
+    from kernix_b200 import configs
+    tol = dict(c2=1e-4, c3=1e-4, c4=1e-4, c5=1e-5)[cfg]
+    p = cfg_path(cfg, model_dir)
+    m = Model(p, workspace_mb=0)
+    x = configs.inputs(cfg, batch)
+    per = x.shape[0] // batch
+    host = m(x.reshape(-1, m.in_dim)).reshape(batch, -1)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((batch, m.out_dim), dtype=torch.float32, device="cuda")
+    libkx.kernix_model_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    libkx.kernix_model_forward_device.restype = ctypes.c_int
+    libkx.kernix_model_check.argtypes = [ctypes.c_void_p]
+    libkx.kernix_model_check.restype = ctypes.c_int
+    s = torch.cuda.current_stream()
+    assert libkx.kernix_model_forward_device(m._h, dx.data_ptr(), x.shape[0], dy.data_ptr(), s.cuda_stream) == 0
+    s.synchronize()
+    assert libkx.kernix_model_check(m._h) == 0
+    dev = dy.cpu().numpy()
+    m.close()
+    del dx, dy
+    ids = _sample_ids(batch)
+    xs = x.reshape(batch, per, -1)[ids].reshape(len(ids) * per, -1)
+    want = ko.forward(_oracle_model(p), xs).reshape(len(ids), -1)
+    e_host, e_dev = rel_err(host[ids], want), rel_err(dev[ids], want)
+    print(f"{cfg} batch {batch}: host API {e_host:.2e}, device forward {e_dev:.2e} (bound {tol:g}, samples {list(ids)})")
+    assert e_host <= tol and e_dev <= tol
+    assert rel_err(host, dev) <= tol
+
+
 def test_c2_int8_end_to_end(Model, model_dir):
     """int8 MLP end to end: within 1e-4 of the output scale; requantisation flips after GELU (device expf vs
     glibc expf moving a value across a rounding tie) are allowed and counted."""
