@@ -56,6 +56,15 @@ KERNIX_API int kx_linear_i8_noalloc(const float* x, int ldx, int rows, int k, co
                                     const float* bias, float* y, int ldy, int n, int act, float alpha, int* status,
                                     void* stream);
 
+/* Failure-detection check of the bounded waits every tcgen05 kernel here uses (the counterpart of the reference's
+ * command-buffer error handling, src/kernix_metal.m:259-263, which turns a failed GPU command into -1): one warp
+ * waits on an mbarrier with the library's wait helper and a limit of limit_ns (at most 2 s). arrive = 1: the
+ * barrier completes and *status is left as it was; arrive = 0: nothing arrives, the wait gives up after limit_ns
+ * and writes KX_STATUS_TIMEOUT (1) to *status, and the launch ends normally. *waited_ns: time spent waiting.
+ * Device pointers; returns -1 on bad arguments or a launch error. */
+KERNIX_API int kx_probe_bounded_wait(int arrive, unsigned long long limit_ns, int* status, unsigned long long* waited_ns,
+                                     void* stream);
+
 /* int32 accumulators only (acc[row][col], leading dimension ldacc): exposes the integer result for tests. */
 KERNIX_API int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
                    int* status, void* stream);

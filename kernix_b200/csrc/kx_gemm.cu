@@ -2229,9 +2229,35 @@ int dispatch_f32(const float* x, int ldx, const float* whi, const float* wlo, in
 }
 #undef KX_F32_ARGS
 
+// One warp waits, with the library's bounded wait (mbar_wait_for), on an mbarrier of arrival count 1. With
+// arrive = 1 lane 0 arrives first and the wait completes; with arrive = 0 nothing ever arrives, so the wait gives
+// up after limit_ns and records KX_STATUS_TIMEOUT in *status. Nothing asynchronous (TMA, MMA) is in flight.
+// waited[0] receives the nanoseconds lane 0 spent in the wait.
+__global__ void k_probe_wait(int arrive, uint64_t limit_ns, int* status, unsigned long long* waited) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        kx::mbar_init(&bar, 1);
+        abort_flag = 0;
+        kx::fence_mbar_init();
+    }
+    __syncwarp();
+    if (arrive && threadIdx.x == 0) kx::mbar_arrive(&bar);
+    __syncwarp();
+    const uint64_t t0 = kx::globaltimer();
+    kx::mbar_wait_for(&bar, 0, &abort_flag, status, limit_ns);
+    if (threadIdx.x == 0) waited[0] = kx::globaltimer() - t0;
+}
+
 }  // namespace
 
 extern "C" {
+
+int kx_probe_bounded_wait(int arrive, unsigned long long limit_ns, int* status, unsigned long long* waited_ns, void* stream) {
+    if (status == nullptr || waited_ns == nullptr || limit_ns > 2000000000ull) return -1;
+    k_probe_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(arrive, limit_ns, status, waited_ns);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
 
 int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
                const float* bias, float* y, int ldy, int m, int n, int k, int act, float alpha, int* status,

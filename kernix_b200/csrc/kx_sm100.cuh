@@ -57,16 +57,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for completion of the phase with the given parity. Returns false (after recording a timeout in
-// *status and setting *abort) if it does not complete within KX_WAIT_NS, or if another thread of the CTA
+// *status and setting *abort) if it does not complete within limit_ns, or if another thread of the CTA
 // has already raised *abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                              uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t spin = 0;; spin++) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
         if ((spin & 63) == 63) {
-            if (globaltimer() - t0 > KX_WAIT_NS) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort = 1;
                 if (status) atomicExch(status, KX_STATUS_TIMEOUT);
                 return false;
@@ -74,6 +75,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             __nanosleep(64);
         }
     }
+}
+
+// the library's waits: KX_WAIT_NS
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
+    return mbar_wait_for(bar, parity, abort, status, KX_WAIT_NS);
 }
 
 // ---- TMA ----

@@ -115,10 +115,29 @@ def _mutations(data, n, rng):
             yield bytes(b) + bytes(rng.integers(0, 256, rng.integers(1, 9)).astype(np.uint8))
 
 
-@pytest.mark.parametrize("name", ["g_cnn", "g_attn", "g_rnn", "inplace_first"])
+def legacy_lstm_file():
+    """A KNX1 file with the legacy LSTM record (in, units, act, ret_seq, sequence length; float weights W, U, bias)
+    followed by a Linear and a softmax: the version-1/2 header rules of ACT and LSTM."""
+    rng = np.random.default_rng(3)
+    cin, u, T = 3, 4, 5
+    rec = struct.pack("<6I", 4, cin, u, 4, 0, T)  # LSTM, tanh, last state only
+    rec += rng.standard_normal(cin * 4 * u).astype("<f4").tobytes() + rng.standard_normal(u * 4 * u).astype("<f4").tobytes()
+    rec += rng.standard_normal(4 * u).astype("<f4").tobytes()
+    lin = struct.pack("<4I", 0, u, 2, 1) + rng.standard_normal(u * 2 + 2).astype("<f4").tobytes()
+    return b"KNX1" + struct.pack("<I", 4) + rec + lin + struct.pack("<2I", 1, 0) + struct.pack("<I", 3)
+
+
+@pytest.mark.parametrize("name", ["g_cnn", "g_attn", "g_rnn", "inplace_first", "cnn_s", "tfm_s", "small_int8",
+                                  "legacy_lstm"])
 def test_fuzzed_files_agree_with_reference(kx, name, tmp_path):
+    """Every op kind's header and data rules (the golden graphs hold all 21 kinds; small_int8 and legacy_lstm the
+    KNX2 / KNX1 variants)."""
     rng = np.random.default_rng(len(name))
-    data = open(os.path.join(GOLD, f"{name}.knx"), "rb").read()
+    if name == "legacy_lstm":
+        data = legacy_lstm_file()
+        assert accepts(kx, write(tmp_path, "legacy_lstm.knx", data))
+    else:
+        data = open(os.path.join(GOLD, f"{name}.knx"), "rb").read()
     n_acc = 0
     for i, mdata in enumerate(_mutations(data, 240, rng)):
         p = write(tmp_path, f"m{i}.knx", mdata)
@@ -139,7 +158,7 @@ def test_fuzzed_files_agree_with_reference(kx, name, tmp_path):
                 assert r.plan() == kx.plan(p) and r.steps() == kx.inspect(p)["steps"]
                 r.close()
         if oracle_ok != mine:  # the oracle's reader skips a few of the loader's range checks on RNN fields
-            assert name == "g_rnn", f"mutation {i}: oracle {'accepts' if oracle_ok else 'rejects'}, runtime does not"
+            assert name in ("g_rnn", "legacy_lstm"), f"mutation {i}: oracle {'accepts' if oracle_ok else 'rejects'}, runtime does not"
         n_acc += mine
         os.remove(p)
     assert 0 < n_acc < 240

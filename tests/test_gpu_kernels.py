@@ -518,3 +518,23 @@ def test_attention_core(kx, Rq, S, H, dk, dv, causal, packed):
     want = (P @ V).transpose(0, 2, 1, 3).reshape(B * Rq, H * dv)
     check_status(st)
     assert rel_err(host(ctx), want) <= 1e-5
+
+
+@pytest.mark.parametrize("arrive", [1, 0])
+def test_bounded_wait_reports_timeout(libkx, arrive):
+    """Failure detection without a fault: the bounded mbarrier wait every tcgen05 kernel here uses gives up after its
+    limit and reports KX_STATUS_TIMEOUT through the status word (a barrier nothing arrives at, 20 ms limit), while a
+    barrier that completes leaves the status alone; either way the launch ends and the context stays usable."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from kernix_b200 import kx_abi as kx
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    waited = torch.zeros(1, dtype=torch.int64, device="cuda")
+    kx.call("kx_probe_bounded_wait", arrive, 20_000_000, status.data_ptr(), waited.data_ptr(), None)
+    torch.cuda.synchronize()
+    ns = int(waited.item())
+    if arrive:
+        assert int(status.item()) == 0 and ns < 20_000_000
+    else:
+        assert int(status.item()) == 1 and 20_000_000 <= ns < 1_000_000_000
+    assert torch.ones(4, device="cuda").sum().item() == 4.0  # the context is still usable
