@@ -14,6 +14,8 @@ the path has no cross-sample exchange, so there is no collective in the data pat
                sample, all host threads (one model instance per thread; the reference's forward is per-model serial)
   per_config   (N = 1) every other configuration at its benchmark batch -- c1 256, c2 32, c3 1024, c4 512, c5 1 and
                256 -- device-resident samples/s with the achieved rate and its fraction of the bound at that batch
+  strong_scaling  c5 at batch 1 / 64 / 256 with every layer's output columns split over all N GPUs (the runtime's
+               own ncclAllGather per layer), ms per forward, max over ranks: the strong-scaling companion of value
 
   --impl reference times the reference's CPU forward on the same 4096-sample c2 batch per step, all host threads.
 
@@ -62,6 +64,8 @@ def parse():
                     help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
                          "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling). c1, c3, c4, "
                          "c5: the device-resident forward of that configuration at --batch samples per GPU")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the strong_scaling object (c5 column-sharded over all ranks at batch 1 / 64 / 256)")
     ap.add_argument("--no-per-config", action="store_true",
                     help="skip the per_config object (the other configurations at their benchmark batch sizes)")
     ap.add_argument("--batch", type=int, default=0,
@@ -410,6 +414,11 @@ def run_kernix(args):
         else:
             cpu = {"value": None, "unit": "samples/s", "cores": 0, "kind": "reference", "sample": "oracle/_ref not built"}
 
+    # ---- strong scaling beside the weak-scaling value: c5 column-sharded over all ranks (every N, every rank)
+    strong = None
+    if not args.no_strong:
+        strong = c5_sharded_times(L, torch, dist, rank, world, local, [1, 64, 256], max(5, args.steps // 2), 3)
+
     # ---- the other configurations at their benchmark batch sizes (rank 0 at N = 1 only)
     per_config = None
     if rank == 0 and world == 1 and not args.no_per_config:
@@ -433,6 +442,7 @@ def run_kernix(args):
             "roofline": roof,
             "cpu_baseline": cpu,
             "per_config": per_config,
+            "strong_scaling": strong,
             "clocks": clk.summary(),
             "gpu_launches": 6 * args.steps,
             "peaks_file": bool(peaks),
@@ -494,6 +504,51 @@ def gemm_roofline(L, torch, np, steps, flush):
             "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
 
 
+def c5_sharded_times(L, torch, dist, rank, world, local, batches, steps, warmup):
+    """Strong scaling of config c5 (fp32 MLP 8192-16384-16384-8192): its layers split by output columns over all
+    `world` ranks (kernix_model_load_sharded_nccl; the runtime calls ncclAllGather per layer on the model's stream;
+    one rank = the whole model), each batch timed as `steps` back-to-back device-resident forwards with CUDA events
+    on the model's stream, max over ranks. The weights (2.15 GB / world per rank) stream from HBM every forward."""
+    from kernix_b200 import Model, configs, shard
+    model_dir = os.environ.get("KERNIX_MODEL_DIR_SHARED", "/tmp/kernix_models_shared")
+    if rank == 0:
+        configs.model_path("c5", model_dir)
+    if dist is not None:
+        dist.barrier()
+    path = configs.model_path("c5", model_dir)
+    uid = shard.share_nccl_id() if world > 1 else None
+    m = Model(path, workspace_mb=0, shard=(rank, world, uid) if world > 1 else None)
+    stream = torch.cuda.current_stream()
+    out = {}
+    for B in batches:
+        x = torch.from_numpy(configs.inputs("c5", B, seed=100)).cuda()
+        y = torch.empty((B, 8192), dtype=torch.float32, device="cuda")
+
+        def step():
+            if L.kernix_model_forward_device(m._h, x.data_ptr(), B, y.data_ptr(), stream.cuda_stream) != 0:
+                raise RuntimeError("forward_device failed (c5 sharded)")
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if L.kernix_model_check(m._h) != 0:
+            raise RuntimeError("a kernel reported a failure (c5 sharded)")
+        t = reduce_max(dist, e0.elapsed_time(e1) / 1e3 / steps, "cuda")
+        out[str(B)] = {"ms_per_forward": t * 1e3, "samples_per_s": B / t, "achieved_tflops": 2.0 * 536870912 * B / t / 1e12}
+    m.close()
+    return {"workload": "c5 fp32 MLP 8192-16384-16384-8192, every layer's output columns split over all GPUs",
+            "scaling": "strong", "n_gpus": world, "by_batch": out,
+            "collective": "ncclAllGather per layer, called by the runtime on the model's stream" if world > 1 else "none (1 GPU)"}
+
+
 def _peaks():
     try:
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured (MEASURED_PEAKS.json)"
@@ -527,7 +582,7 @@ def measure_configs(L, torch, flush, stream, steps, warmup):
     tf32x3 = float(peaks["bf16_tflops"]) / 2 / 3
     hbm = float(peaks["hbm_gbs"])
     out = {}
-    model_dir = os.environ.get("KERNIX_MODEL_DIR", "/tmp/kernix_models_r0")
+    model_dir = os.environ.get("KERNIX_MODEL_DIR_SHARED", "/tmp/kernix_models_shared")
     for cfg, B in PER_CONFIG:
         m = Model(configs.model_path(cfg, model_dir), workspace_mb=0)
         x = torch.from_numpy(configs.inputs(cfg, B, seed=100)).cuda()
@@ -649,7 +704,7 @@ def run_config(args):
 
 def run_c5_rows(args):
     """Config c5 (fp32 MLP 8192-16384-16384-8192, ReLU) at a small batch, its three layers split by output columns
-    over the ranks (kernix_model_load_sharded + NCCL all-gather on the model's stream). value: batch * steps / (max
+    over the ranks (kernix_model_load_sharded_nccl: the runtime calls ncclAllGather on the model's stream). value: batch * steps / (max
     over ranks of the CUDA-event time of the timed steps); the weights (2.15 GB, 1/N per rank) stream from HBM every
     step, larger than L2, so no flush is needed. e2e: kernix_capi_forward with page-locked host buffers."""
     import datetime
@@ -678,7 +733,7 @@ def run_c5_rows(args):
         dist.barrier()
     path = configs.model_path("c5")
     os.environ["KERNIX_DEVICE"] = str(local)
-    m = Model(path, workspace_mb=0, shard=(rank, world, shard.torch_allgather()) if world > 1 else None)
+    m = Model(path, workspace_mb=0, shard=(rank, world, shard.share_nccl_id()) if world > 1 else None)
     B = args.batch or 64
     x_pin = torch.from_numpy(configs.inputs("c5", B, seed=100)).pin_memory()
     out_pin = torch.empty((B, 8192), dtype=torch.float32).pin_memory()
@@ -728,7 +783,7 @@ def run_c5_rows(args):
             "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic: inputs U[-1,1) seed 100, weights N(0, sqrt(2/fan_in)), b = 0.01",
             "config": {"workload": f"c5-rows: c5 at batch {B}, every layer's output columns split over {world} GPU(s)",
-                       "global_batch": B, "parallelism": f"column-parallel x{world}, NCCL all-gather per layer",
+                       "global_batch": B, "parallelism": f"column-parallel x{world}, ncclAllGather per layer from the runtime",
                        "l2": "no flush: 2.15 GB of weights stream from HBM every step"},
             "e2e": {"value": B * args.steps / t_e2e, "unit": "samples/s", "h2d_bytes_per_step": B * 8192 * 4,
                     "d2h_bytes_per_step": B * 8192 * 4, "api": "kernix_capi_forward, page-locked host buffers"},

@@ -48,6 +48,24 @@ typedef int (*kernix_allgather_fn)(void* ctx, const float* send, float* recv, si
 KERNIX_API kernix_model* kernix_model_load_sharded(const char* path, int rank, int world, kernix_allgather_fn gather,
                                                    void* ctx);
 
+/* The same sharded load with the all-gather done by the runtime itself: every rank calls it with the same 128-byte
+ * NCCL unique id (kernix_nccl_unique_id on one rank, then shared by the host program), the model creates its NCCL
+ * communicator on its device (collective: all ranks must call concurrently) and each sharded step calls
+ * ncclAllGather on the model's stream -- no host callback, so a C program can shard. NCCL (libnccl.so.2) is
+ * loaded on first use. The communicator is destroyed by kernix_model_free. world = 1 loads the whole model. */
+KERNIX_API kernix_model* kernix_model_load_sharded_nccl(const char* path, int rank, int world, const void* nccl_id);
+
+/* A new NCCL unique id (128 bytes into id) for kernix_model_load_sharded_nccl. 0, or -1 if NCCL is unavailable. */
+KERNIX_API int kernix_nccl_unique_id(void* id);
+
+/* ------------------------------------------------------------------ batch sharding across GPUs
+ * (extension; the reference's chunk loop over one batch, include/kernix_model.h:2036-2063, spread over devices).
+ * With $KERNIX_GPUS naming two or more devices ("0,1,2,3" or "all") when kernix_model_load runs, the model is
+ * loaded whole onto each of them; every host-memory forward (kernix_model_forward, kernix_capi_forward) then gives
+ * each device a contiguous share of the samples, run concurrently (one host thread per extra device), each
+ * share's rows read from and written to the caller's buffers at their offsets -- the same rows as one device
+ * computes. kernix_model_forward_device runs on the first device only. Unset or one device: one device. */
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,11 +28,27 @@ extern "C" {
  * (their GEMM output becomes NaN, as the reference's NaN rows). xq columns k..ldq-1 are zeroed. */
 KERNIX_API int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream);
 
+/* kx_quant_rows that also clears zero[0 .. zero_words) once the kernel before it has completed: the row maxima
+ * and counters of the kx_gemm_i8_q launch that follows (an internal step of the model runtime). */
+KERNIX_API int kx_quant_rows_z(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, uint32_t* zero,
+                               int zero_words, void* stream);
+
 /* y = act(((float)acc * sx[row]) * scale[col] + bias[col]) with acc = sum_t xq[row][t] * wq[col][t] in int32
  * on tcgen05 kind::i8 (kernix_qmatmul :143-177 and the step's activation :1854-1856). wq: n x ldw int8,
  * K-major (see kx_prep_i8_weight). ldq, ldw multiples of 16. bias may be NULL (adds 0). */
 KERNIX_API int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
                const float* bias, float* y, int ldy, int m, int n, int k, int act, float alpha, int* status, void* stream);
+
+/* A hidden int8 layer whose output feeds only the next int8 layer (kernix_qmatmul :99-182 twice, :1854-1856):
+ * the int8 GEMM of kx_gemm_i8 whose epilogue quantises its own output rows for the next layer, as kx_quant_rows
+ * would from y, and writes q_out (m x ldq_out int8; ldq_out >= n, a multiple of 16; columns n .. ldq_out-1 zero;
+ * 16-byte aligned) and sx_out (m floats) instead of y: bit for bit the kx_quant_rows result of y. ctl: m + ceil(m/128)
+ * words of device memory that must be zero at launch (row maxima and row-group counters); the launch clears
+ * zero_next[0 .. zero_words) for the next one. n > 128 (CTA-pair tiles) and at most as many 256-column tiles as
+ * CTA pairs resident at once, else -1. */
+KERNIX_API int kx_gemm_i8_q(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
+                            const float* bias, int m, int n, int k, int act, float alpha, int8_t* q_out, int ldq_out,
+                            float* sx_out, uint32_t* ctl, uint32_t* zero_next, int zero_words, int* status, void* stream);
 
 /* One int8 LINEAR step from fp32 activations, the whole of kernix_qmatmul plus the step's activation
  * (include/kernix_model.h:99-182, :1854-1856): quantise x's rows into xq_scratch (rows x ldq int8, ldq =

@@ -28,8 +28,8 @@ CC_FLAGS = ["-std=gnu11", "-O2", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wext
             "-I" + INCLUDE, "-I" + CSRC, "-I" + os.path.join(CUDA_HOME, "include")]
 
 CU_SOURCES = ["kx_gemm.cu", "kx_ops.cu", "kx_noalloc.cu", "kx_attn.cu", "kx_tensor.cu"]
-C_SOURCES = ["knx_load.c", "knx_model.c"]
-HEADERS = ["kx_sm100.cuh", "kx_act.cuh", "kx_internal.h"]
+C_SOURCES = ["knx_load.c", "knx_model.c", "knx_nccl.c"]
+HEADERS = ["kx_sm100.cuh", "kx_act.cuh", "kx_pdl.cuh", "kx_internal.h"]
 
 
 def _newer(src_list, dst):

@@ -12,6 +12,7 @@
 #include <limits.h>
 #include <math.h>
 #include <stdint.h>
+#include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -27,6 +28,8 @@
 #define KX_ALIGN 256
 #define KX_PIPE_MAX 8             /* pieces a chunk of host rows is split into, at most */
 #define KX_PIPE_MIN_BYTES (1 << 20) /* input bytes of one piece, at least */
+
+#define KX_MAX_REPLICAS 15
 
 struct kx_model_impl {
     kx_graph* g;
@@ -58,6 +61,12 @@ struct kx_model_impl {
     size_t skinny_floats;
     int* status_h;        /* pinned host copy */
     size_t scratch_per_row_max;
+    int no_qchain;        /* 1 while tracing: every int8 step writes its fp32 output (int8 chains off) */
+    void* nccl_comm;      /* the communicator of kernix_model_load_sharded_nccl (owned), else NULL */
+    /* batch sharding over the devices of $KERNIX_GPUS: whole-model replicas on the other devices; a host-memory
+     * forward gives each device a contiguous share of the samples */
+    int n_rep;
+    kernix_model* rep[KX_MAX_REPLICAS];
     /* output-column sharding (kernix_model_load_sharded) */
     int rank, world;
     kernix_allgather_fn gather;
@@ -279,15 +288,26 @@ static void step_dev_free(kx_step* s) {
     s->d_bias = s->d_bk = s->d_bv = s->d_bo = s->d_gamma = s->d_beta = s->d_cst = s->d_bqkv = NULL;
 }
 
+/* row pitch of the int8 activation slots: the largest quantised row any int8 LINEAR step reads or writes */
+static size_t int8_pitch(const kx_graph* g) {
+    size_t q = 16;
+    for (int i = 0; i < g->n_steps; i++) {
+        const kx_step* s = &g->steps[i];
+        if (s->kind != KERNIX_OP_LINEAR || !s->w.int8) continue;
+        if (round_up((size_t)s->in, 16) > q) q = round_up((size_t)s->in, 16);
+        if (round_up((size_t)s->out, 16) > q) q = round_up((size_t)s->out, 16);
+    }
+    return q;
+}
+
 /* scratch bytes per input row (per sample for attention) that a step needs during its launch */
 static size_t step_scratch(const kx_graph* g, const kx_step* s, size_t* per_sample) {
     *per_sample = 0;
     const kx_val* vi = &g->vals[s->inp[0]];
     if (s->kind == KERNIX_OP_LINEAR && s->shard_n > 0) { /* local slice, then the gathered [world][rows][slice] */
         *per_sample = (size_t)vi->r * ((size_t)s->shard_n + (size_t)s->out) * sizeof(float) + 2 * KX_ALIGN;
-    } else if (s->kind == KERNIX_OP_LINEAR && s->w.int8) {
-        const size_t ldq = round_up((size_t)s->in, 16);
-        *per_sample = (size_t)vi->r * (round_up(ldq, 16) + 4 * 4);
+    } else if (s->kind == KERNIX_OP_LINEAR && s->w.int8) { /* two int8 slots (rows x pitch + row scales), two ctl arrays */
+        *per_sample = (size_t)vi->r * (2 * (int8_pitch(g) + 4) + 2 * 8) + 8 * KX_ALIGN;
     } else if (s->kind == KERNIX_OP_LSTM || s->kind == KERNIX_OP_GRU || s->kind == KERNIX_OP_RNN) {
         /* input projections of all steps, two state buffers, the cell state, the second direction's output */
         const size_t T = (size_t)vi->r, u = (size_t)s->out, gu = rnn_gates(s->kind) * u;
@@ -404,6 +424,25 @@ static void plan_fusions(kx_graph* g) {
     }
 }
 
+/* Chains of int8 LINEAR steps: a step whose output is read only by the next step, itself an int8 LINEAR taking that
+ * output as its input, runs kx_gemm_i8_q: its epilogue writes the next step's quantised rows and row scales (the
+ * kernix_qmatmul quantisation, bit for bit) instead of fp32 rows, so neither the fp32 intermediate nor a separate
+ * quantiser pass exists. The quantised rows alternate between two scratch slots along the chain. Needs CTA-pair
+ * tiles (more than 128 columns) and at most 64 tiles of 256 columns (a row group's tiles are resident at once). */
+static void plan_qchain(kx_graph* g) {
+    for (int i = 0; i < g->n_steps; i++) g->steps[i].qout = g->steps[i].qin = g->steps[i].qpar = 0;
+    for (int i = 0; i + 1 < g->n_steps; i++) {
+        kx_step* s = &g->steps[i];
+        kx_step* t = &g->steps[i + 1];
+        const int int8_pair = s->kind == KERNIX_OP_LINEAR && s->w.int8 && s->out > 128 && (s->out + 255) / 256 <= 64;
+        if (!int8_pair || t->kind != KERNIX_OP_LINEAR || !t->w.int8 || t->n_in != 1 || t->inp[0] != i + 1) continue;
+        if (g->vals[i + 1].last != i + 1 || g->out_v == i + 1 || t->in != s->out) continue;
+        s->qout = 1;
+        t->qin = 1;
+        t->qpar = 1 - s->qpar;
+    }
+}
+
 /* one step over B samples; fused: the step's GEMM also performs the next step, an ADD (plan_fusions) */
 static int step_run(kernix_model* m, int i, int B, int fused) {
     struct kx_model_impl* im = m->impl;
@@ -418,13 +457,28 @@ static int step_run(kernix_model* m, int i, int B, int fused) {
     cudaStream_t st = im->stream;
     switch (s->kind) {
     case KERNIX_OP_LINEAR:
-        if (s->w.int8) {
+        if (s->w.int8) { /* scratch: int8 slots 0 and 1 (rows x pitch, then the row scales), ctl arrays 0 and 1 */
             const int ldq = (int)round_up((size_t)s->in, 16);
-            int8_t* xq = (int8_t*)im->scratch;
-            float* sx = (float*)align_ptr(xq + (size_t)rin * ldq);
-            if (kx_quant_rows(a, s->in, (int)rin, s->in, xq, ldq, sx, st) != 0) return -1;
-            return kx_gemm_i8(xq, ldq, sx, s->w.d_q, s->w.ldw, s->w.d_scale, s->d_bias, y, s->out, (int)rin, s->out, s->in,
-                              s->act, s->alpha, im->status, st);
+            const size_t pitch = int8_pitch(g), q_bytes = round_up((size_t)rin * pitch, KX_ALIGN);
+            const size_t slot = q_bytes + round_up((size_t)rin * sizeof(float), KX_ALIGN);
+            const size_t cw = (size_t)rin + ((size_t)rin + 127) / 128;
+            uint8_t* sc = (uint8_t*)align_ptr(im->scratch);
+            int8_t* xq_slot[2] = {(int8_t*)sc, (int8_t*)(sc + slot)};
+            float* sx_slot[2] = {(float*)(sc + q_bytes), (float*)(sc + slot + q_bytes)};
+            uint32_t* ctl[2] = {(uint32_t*)(sc + 2 * slot), (uint32_t*)(sc + 2 * slot + round_up(cw * 4, KX_ALIGN))};
+            const int chain = !im->no_qchain, p = s->qpar;
+            const int qin = chain && s->qin, qout = chain && s->qout;
+            if (!qin && kx_quant_rows_z(a, s->in, (int)rin, s->in, xq_slot[p], ldq, sx_slot[p], qout ? ctl[p] : NULL,
+                                        qout ? (int)cw : 0, st) != 0)
+                return -1;
+            if (qout) { /* this GEMM's ctl[p] was cleared by the kernel before it; it clears the next one's */
+                const int zn = g->steps[i + 1].qout;
+                return kx_gemm_i8_q(xq_slot[p], ldq, sx_slot[p], s->w.d_q, s->w.ldw, s->w.d_scale, s->d_bias, (int)rin, s->out,
+                                    s->in, s->act, s->alpha, xq_slot[1 - p], (int)round_up((size_t)s->out, 16), sx_slot[1 - p],
+                                    ctl[p], zn ? ctl[1 - p] : NULL, zn ? (int)cw : 0, im->status, st);
+            }
+            return kx_gemm_i8(xq_slot[p], ldq, sx_slot[p], s->w.d_q, s->w.ldw, s->w.d_scale, s->d_bias, y, s->out, (int)rin,
+                              s->out, s->in, s->act, s->alpha, im->status, st);
         }
         const int skinny = rin <= KX_SKINNY_MAX_ROWS && s->w.d_raw != NULL && im->skinny_part != NULL;
         if (s->shard_n > 0) { /* this rank's columns, all-gather across ranks, re-interleave into full rows */
@@ -770,7 +824,57 @@ static void pipe_tune(struct kx_model_impl* im) {
 }
 
 /* host-memory forward: enqueue, then wait for every stream and check the status word */
+static int forward_one(kernix_model* m, const float* x, int rows, float* out);
+
+/* one device's share of a batch-sharded host forward, run on its own host thread */
+typedef struct {
+    kernix_model* m;
+    const float* x;
+    int rows;
+    float* out;
+    int rc;
+} kx_share;
+
+static void* share_run(void* arg) {
+    kx_share* sh = (kx_share*)arg;
+    int prev;
+    sh->rc = dev_guard_enter(sh->m, &prev) == 0 ? forward_one(sh->m, sh->x, sh->rows, sh->out) : -1;
+    dev_guard_leave(sh->m, prev);
+    return NULL;
+}
+
+/* host-memory forward of a model with replicas: samples split in contiguous shares, one per device, each share's
+ * input read and output written in place in the caller's buffers; every share must succeed */
+static int forward_sharded_batch(kernix_model* m, const float* x, int rows, float* out) {
+    struct kx_model_impl* im = m->impl;
+    const int samples = rows / m->seq_len, parts = im->n_rep + 1 < samples ? im->n_rep + 1 : samples;
+    kx_share sh[KX_MAX_REPLICAS + 1];
+    pthread_t th[KX_MAX_REPLICAS + 1];
+    int started[KX_MAX_REPLICAS + 1] = {0};
+    for (int k = 0; k < parts; k++) {
+        const int a = (int)((long)samples * k / parts), b = (int)((long)samples * (k + 1) / parts);
+        sh[k] = (kx_share){k == 0 ? m : im->rep[k - 1], x + (size_t)a * m->seq_len * m->in_dim, (b - a) * m->seq_len,
+                           out + (size_t)a * m->out_dim, -1};
+    }
+    for (int k = 1; k < parts; k++) started[k] = pthread_create(&th[k], NULL, share_run, &sh[k]) == 0;
+    sh[0].rc = forward_one(m, sh[0].x, sh[0].rows, sh[0].out);
+    int rc = sh[0].rc;
+    for (int k = 1; k < parts; k++) {
+        if (started[k]) pthread_join(th[k], NULL);
+        else share_run(&sh[k]); /* no thread: run the share here */
+        rc |= sh[k].rc;
+    }
+    return rc ? -1 : 0;
+}
+
+/* host-memory forward on the model's device(s) (the caller made the model's device current) */
 static int forward_into(kernix_model* m, const float* x, int rows, float* out) {
+    if (m->impl->n_rep > 0 && rows / m->seq_len > 1) return forward_sharded_batch(m, x, rows, out);
+    return forward_one(m, x, rows, out);
+}
+
+/* host-memory forward on the model's own device */
+static int forward_one(kernix_model* m, const float* x, int rows, float* out) {
     struct kx_model_impl* im = m->impl;
     if (rows / m->seq_len == 0) return 0;
     cudaStream_t st = im->stream;
@@ -809,7 +913,16 @@ static size_t ws_count(kernix_model* m) {
 }
 
 /* ------------------------------------------------------------------------------------ public API */
-static kernix_model* model_load(const char* path, int rank, int world, kernix_allgather_fn gather, void* ctx) {
+/* the device a model loads onto: `device` if >= 0, else $KERNIX_DEVICE, else the caller's current device */
+static int pick_device(int device) {
+    if (device >= 0) return device;
+    const char* env = getenv("KERNIX_DEVICE");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    return env && *env ? atoi(env) : (cur >= 0 ? cur : 0);
+}
+
+static kernix_model* model_load(const char* path, int rank, int world, kernix_allgather_fn gather, void* ctx, int device) {
     const char* err = NULL;
     if (world < 1 || rank < 0 || rank >= world || (world > 1 && gather == NULL)) {
         fprintf(stderr, "model load failed (%s): bad shard arguments (rank %d of %d)\n", path ? path : "NULL", rank, world);
@@ -829,6 +942,7 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
             }
         }
     plan_fusions(g);
+    plan_qchain(g);
     kernix_model* m = calloc(1, sizeof *m);
     struct kx_model_impl* im = calloc(1, sizeof *im);
     if (m == NULL || im == NULL) {
@@ -860,10 +974,9 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
     m->ws_fixed = 0;
     m->ws_per_sample = ws_count(m);
 
-    const char* env = getenv("KERNIX_DEVICE");
     int prev = -1;
     cudaGetDevice(&prev);
-    im->device = env && *env ? atoi(env) : (prev >= 0 ? prev : 0);
+    im->device = pick_device(device);
     const char* why = NULL;
     if (cudaSetDevice(im->device) != cudaSuccess) why = "no CUDA device";
     else if (cudaStreamCreateWithFlags(&im->stream, cudaStreamNonBlocking) != cudaSuccess ||
@@ -922,17 +1035,84 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
     return m;
 }
 
-KERNIX_API kernix_model* kernix_model_load(const char* path) { return model_load(path, 0, 1, NULL, NULL); }
+/* devices named by $KERNIX_GPUS ("0,1,2,3" or "all"): the count, at most KX_MAX_REPLICAS + 1, or 0 if unset */
+static int gpus_from_env(int* dev) {
+    const char* env = getenv("KERNIX_GPUS");
+    if (env == NULL || *env == 0) return 0;
+    int n = 0;
+    if (strcmp(env, "all") == 0) {
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        for (int d = 0; d < count && n <= KX_MAX_REPLICAS; d++) dev[n++] = d;
+        return n;
+    }
+    for (const char* p = env; *p && n <= KX_MAX_REPLICAS;) {
+        char* end = NULL;
+        const long v = strtol(p, &end, 10);
+        if (end == p || v < 0) break;
+        dev[n++] = (int)v;
+        p = *end == ',' ? end + 1 : end;
+        if (*end != ',' && *end != 0) break;
+    }
+    return n;
+}
+
+KERNIX_API kernix_model* kernix_model_load(const char* path) {
+    int dev[KX_MAX_REPLICAS + 1];
+    const int n = gpus_from_env(dev);
+    kernix_model* m = model_load(path, 0, 1, NULL, NULL, n >= 2 ? dev[0] : -1);
+    if (m == NULL || n < 2) return m;
+    for (int k = 1; k < n; k++) { /* whole-model replicas; the load fails if any device cannot hold one */
+        kernix_model* r = model_load(path, 0, 1, NULL, NULL, dev[k]);
+        if (r == NULL) {
+            fprintf(stderr, "model load failed (%s): no replica on device %d of $KERNIX_GPUS\n", path, dev[k]);
+            kernix_model_free(m);
+            return NULL;
+        }
+        m->impl->rep[m->impl->n_rep++] = r;
+    }
+    return m;
+}
 
 KERNIX_API kernix_model* kernix_model_load_sharded(const char* path, int rank, int world, kernix_allgather_fn gather,
                                                    void* ctx) {
-    return model_load(path, rank, world, gather, ctx);
+    return model_load(path, rank, world, gather, ctx, -1);
+}
+
+KERNIX_API kernix_model* kernix_model_load_sharded_nccl(const char* path, int rank, int world, const void* nccl_id) {
+    if (world == 1) return model_load(path, 0, 1, NULL, NULL, -1);
+    if (world < 1 || rank < 0 || rank >= world || nccl_id == NULL) {
+        fprintf(stderr, "model load failed (%s): bad shard arguments (rank %d of %d)\n", path ? path : "NULL", rank, world);
+        return NULL;
+    }
+    const int device = pick_device(-1);
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) {
+        fprintf(stderr, "model load failed (%s): no CUDA device %d\n", path ? path : "NULL", device);
+        return NULL;
+    }
+    void* comm = kx_nccl_comm_init(rank, world, nccl_id); /* collective: every rank of the group is here */
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    if (comm == NULL) return NULL;
+    kernix_model* m = model_load(path, rank, world, kx_nccl_gather, comm, device);
+    if (m == NULL) {
+        kx_nccl_comm_free(comm);
+        return NULL;
+    }
+    m->impl->nccl_comm = comm;
+    return m;
 }
 
 KERNIX_API void kernix_model_free(kernix_model* m) {
     if (m == NULL) return;
     struct kx_model_impl* im = m->impl;
     if (im != NULL) {
+        for (int k = 0; k < im->n_rep; k++) kernix_model_free(im->rep[k]);
+        im->n_rep = 0;
         int prev = -1;
         cudaGetDevice(&prev);
         cudaSetDevice(im->device);
@@ -953,6 +1133,7 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
         if (im->s_out) cudaStreamDestroy(im->s_out);
         if (im->stream) cudaStreamDestroy(im->stream);
         kx_graph_free(im->g);
+        if (im->nccl_comm) kx_nccl_comm_free(im->nccl_comm);
         if (prev >= 0) cudaSetDevice(prev);
         free(im);
     }
@@ -961,6 +1142,7 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
 
 KERNIX_API void kernix_model_trim(kernix_model* m) {
     if (m == NULL) return;
+    for (int k = 0; k < m->impl->n_rep; k++) kernix_model_trim(m->impl->rep[k]);
     int prev;
     if (dev_guard_enter(m, &prev) != 0) return;
     sync_all(m->impl);
@@ -969,7 +1151,9 @@ KERNIX_API void kernix_model_trim(kernix_model* m) {
 }
 
 KERNIX_API void kernix_model_set_workspace_limit(kernix_model* m, size_t bytes) {
-    if (m != NULL) m->ws_limit = bytes;
+    if (m == NULL) return;
+    m->ws_limit = bytes;
+    for (int k = 0; k < m->impl->n_rep; k++) m->impl->rep[k]->ws_limit = bytes;
 }
 
 KERNIX_API int kernix_model_set_ane(kernix_model* m, int on) {
@@ -998,7 +1182,7 @@ KERNIX_API const float_tensor* kernix_model_forward(kernix_model* m, const float
         if (im->out_host) cudaFreeHost(im->out_host);
         im->out_host = NULL;
         im->out_host_floats = 0;
-        if (cudaHostAlloc((void**)&im->out_host, need ? need * sizeof(float) : 4, cudaHostAllocDefault) != cudaSuccess) {
+        if (cudaHostAlloc((void**)&im->out_host, need ? need * sizeof(float) : 4, cudaHostAllocPortable) != cudaSuccess) {
             im->out_host = NULL;
             dev_guard_leave(m, prev);
             return NULL;
@@ -1050,8 +1234,12 @@ KERNIX_API int kx_model_forward_trace(kernix_model* m, const float* x, int rows,
     cudaStream_t st = im->stream;
     if (cudaMemcpyAsync(im->xin, x, (size_t)rows * m->in_dim * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess)
         goto done;
+    im->no_qchain = 1; /* every intermediate value is materialised */
     for (int i = 0; i < im->g->n_steps; i++) {
-        if (step_run(m, i, B, 0) != 0) goto done;
+        if (step_run(m, i, B, 0) != 0) {
+            im->no_qchain = 0;
+            goto done;
+        }
         if (outs[i] != NULL) {
             const kx_val* v = &im->g->vals[i + 1];
             if (cudaMemcpyAsync(outs[i], val_ptr(im, i + 1), (size_t)B * v->r * v->c * sizeof(float), cudaMemcpyDeviceToHost,
@@ -1061,6 +1249,7 @@ KERNIX_API int kx_model_forward_trace(kernix_model* m, const float* x, int rows,
     }
     rc = cudaStreamSynchronize(st) == cudaSuccess ? 0 : -1;
 done:
+    im->no_qchain = 0;
     dev_guard_leave(m, prev);
     return rc;
 }

@@ -57,40 +57,39 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 
 // GELU with the Abramowitz-Stegun 7.1.26 erf approximation (reference :485-496): the same formula and
 // constants, GELU(x) = x/2 (1 + sign(x) e) with e = 1 - k p(k) exp(-z^2), z = x/sqrt(2), k = 1/(1 + 0.3275911|z|),
-// evaluated with fused multiply-adds, exp(-z^2) = 2^(-z^2 log2 e) on the hardware exp2 unit and the hardware
-// reciprocal -- about 20 instructions instead of about 50 with correctly rounded steps. The result differs
-// from a step-by-step IEEE evaluation by at most about 1e-6 relative (GELU runs in the epilogue of every
-// hidden layer of the int8 and Transformer configurations, where it bounds the epilogue's issue rate); the
-// parity tests bound the end-to-end effect. gelu_as2 computes two GELUs with packed f32x2 arithmetic: the same
-// steps as gelu_as (the polynomial in negated coefficients gives -k p(k) exactly), within about an ulp of it where
-// the code generator contracts a packed mul and add.
+// evaluated with fused multiply-adds, exp(-z^2) = 2^(-x^2 log2(e) / 2) on the hardware exp2 unit and the hardware
+// reciprocal -- about 10 instructions per value instead of about 50 with correctly rounded steps. The constants
+// of z are folded into the two uses of x (-x^2 log2(e)/2 and 0.3275911/sqrt(2) |x|), and sign(x) e is e with x's sign
+// bit. The result differs from a step-by-step IEEE evaluation by at most about 1e-6 relative (GELU runs in the
+// epilogue of every hidden layer of the int8 and Transformer configurations, where it bounds the epilogue's issue
+// rate); the parity tests bound the end-to-end effect. +inf gives +inf and -inf NaN, as the reference's formula.
+// gelu_as2 computes two GELUs with packed f32x2 arithmetic, the same steps as gelu_as.
+__device__ __forceinline__ float sign_of(float v, float x) {  // |v| with the sign bit of x (v >= 0)
+    return __int_as_float(__float_as_int(v) ^ (__float_as_int(x) & 0x80000000));
+}
 __device__ __forceinline__ float gelu_as(float x) {
-    const float z = __fmul_rn(x, 0.70710678f);
-    const float t = ex2_approx(__fmul_rn(__fmul_rn(z, z), -1.44269504f));
-    const float k = rcp_approx(__fmaf_rn(0.3275911f, fabsf(z), 1.0f));
+    const float h = __fmul_rn(0.5f, x);
+    const float t = ex2_approx(__fmul_rn(__fmul_rn(x, -0.72134752f), x));
+    const float k = rcp_approx(__fmaf_rn(fabsf(x), 0.23164189f, 1.0f));
     float q = __fmaf_rn(k, -1.061405429f, 1.453152027f);
     q = __fmaf_rn(k, q, -1.421413741f);
     q = __fmaf_rn(k, q, 0.284496736f);
     q = __fmaf_rn(k, q, -0.254829592f);
-    q = __fmul_rn(k, q);                        // -k p(k)
-    const float e = __fmaf_rn(q, t, 1.0f);
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, x < 0.0f ? -e : e));
+    const float e = __fmaf_rn(__fmul_rn(k, q), t, 1.0f);  // 1 - k p(k) exp(-z^2), in [0, 1]
+    return __fmul_rn(h, __fadd_rn(1.0f, sign_of(e, x)));
 }
 __device__ __forceinline__ float2 gelu_as2(float2 x) {
-    const float2 z = mul2(x, f2(0.70710678f));
-    const float2 a = mul2(mul2(z, z), f2(-1.44269504f));
+    const float2 h = mul2(x, f2(0.5f));
+    const float2 a = mul2(mul2(x, f2(-0.72134752f)), x);
     const float2 t = make_float2(ex2_approx(a.x), ex2_approx(a.y));
-    const float2 d = fma2(f2(0.3275911f), make_float2(fabsf(z.x), fabsf(z.y)), f2(1.0f));
+    const float2 d = fma2(make_float2(fabsf(x.x), fabsf(x.y)), f2(0.23164189f), f2(1.0f));
     const float2 k = make_float2(rcp_approx(d.x), rcp_approx(d.y));
     float2 q = fma2(k, f2(-1.061405429f), f2(1.453152027f));
     q = fma2(k, q, f2(-1.421413741f));
     q = fma2(k, q, f2(0.284496736f));
     q = fma2(k, q, f2(-0.254829592f));
-    q = mul2(k, q);
-    float2 e = fma2(q, t, f2(1.0f));
-    e.x = x.x < 0.0f ? -e.x : e.x;
-    e.y = x.y < 0.0f ? -e.y : e.y;
-    return mul2(mul2(f2(0.5f), x), add2(f2(1.0f), e));
+    const float2 e = fma2(mul2(k, q), t, f2(1.0f));
+    return mul2(h, add2(f2(1.0f), make_float2(sign_of(e.x, x.x), sign_of(e.y, x.y))));
 }
 
 __device__ __forceinline__ float sigmoidf_ref(float x) {

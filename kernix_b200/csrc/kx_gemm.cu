@@ -101,11 +101,17 @@ struct I8Cfg {
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // double-buffered accumulator
 };
 
-struct TileMap {  // tile t -> (m-tile, n-tile), M-tile fastest
+struct TileMap {  // tile t -> (m-tile, n-tile): M-tile fastest, or N-tile fastest (row blocks in order) if n_fast
     int m_tiles, n_tiles;
+    bool n_fast;
     __device__ __forceinline__ void at(int t, int& mt, int& nt) const {
-        nt = t / m_tiles;
-        mt = t - nt * m_tiles;
+        if (n_fast) {
+            mt = t / n_tiles;
+            nt = t - mt * n_tiles;
+        } else {
+            nt = t / m_tiles;
+            mt = t - nt * m_tiles;
+        }
     }
 };
 
@@ -130,41 +136,72 @@ __device__ __forceinline__ void epi_prefetch(EpiPre& p, int r0, int col0, int la
     p.bi.y = bias && c + 1 < N ? __ldg(bias + c + 1) : 0.0f;
 }
 
-// Dequantise, activate and store one 16x256b.x4 block: rows ra and ra + 8, columns gc, gc + 1 (per k block).
-template <bool ACC_ONLY, int ACTC>
-__device__ __forceinline__ void epi_block(const uint32_t (&r)[16], int ra, int gc0, float sxa, float sxb,
-                                          const float2* __restrict__ scs, const float2* __restrict__ bis,
-                                          float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N,
-                                          bool vec, int act, float alpha) {
+// Raw int32 sums of one 16x256b.x4 block (rows ra and ra + 8, columns gc0 + 8k, +1): the accumulator test path.
+__device__ __forceinline__ void epi_block_acc(const uint32_t (&r)[16], int ra, int gc0, int32_t* __restrict__ acc_out, int ldy,
+                                              int M, int N) {
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int gc = gc0 + 8 * k;
         if (gc >= N) continue;
-        const float2 sc = scs[4 * k], bi = bis[4 * k];
 #pragma unroll
         for (int e = 0; e < 2; e++) {
             const int gr = ra + 8 * e;
             if (gr >= M) continue;
-            const uint32_t v0 = r[4 * k + 2 * e], v1 = r[4 * k + 2 * e + 1];
-            if (ACC_ONLY) {
-                int32_t* dst = acc_out + static_cast<size_t>(gr) * ldy + gc;
-                dst[0] = static_cast<int32_t>(v0);
-                if (gc + 1 < N) dst[1] = static_cast<int32_t>(v1);
+            int32_t* dst = acc_out + static_cast<size_t>(gr) * ldy + gc;
+            dst[0] = static_cast<int32_t>(r[4 * k + 2 * e]);
+            if (gc + 1 < N) dst[1] = static_cast<int32_t>(r[4 * k + 2 * e + 1]);
+        }
+    }
+}
+
+// Dequantise and activate one 16x256b.x4 block: o[2k + e] = the thread's two values in row ra + 8e at columns
+// gc0 + 8k, +1. ((float)acc * sx) * scale + bias keeps the reference's IEEE step order: the two products are packed
+// (mul.rn.f32x2) and the add is scalar, so no product is contracted into an fma with the add. All 16 values are
+// dequantised, then all activated, before anything is stored, so the eight independent chains interleave.
+// cf[4k] = (scale, scale, bias, bias) of the thread's two columns in block k.
+template <int ACTC>
+__device__ __forceinline__ void epi_math(const uint32_t (&r)[16], float sxa, float sxb, const float4* __restrict__ cf,
+                                         float2 (&o)[8], int act, float alpha) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float4 f = cf[4 * k];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float2 a = make_float2(static_cast<float>(static_cast<int32_t>(r[4 * k + 2 * e])),
+                                         static_cast<float>(static_cast<int32_t>(r[4 * k + 2 * e + 1])));
+            const float2 p = kx::mul2(kx::mul2(a, kx::f2(e ? sxb : sxa)), make_float2(f.x, f.y));
+            o[2 * k + e] = make_float2(__fadd_rn(p.x, f.z), __fadd_rn(p.y, f.w));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) o[i] = epi_act2<ACTC>(o[i], act, alpha);
+}
+
+// store a block's values: rows ra (o[2k]) and ra + 8 (o[2k + 1]), columns gc0 + 8k, +1
+__device__ __forceinline__ void epi_store_full(const float2 (&o)[8], float* __restrict__ rowa, float* __restrict__ rowb) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        *reinterpret_cast<float2*>(rowa + 8 * k) = o[2 * k];
+        *reinterpret_cast<float2*>(rowb + 8 * k) = o[2 * k + 1];
+    }
+}
+__device__ __forceinline__ void epi_store_checked(const float2 (&o)[8], float* __restrict__ y, int ra, int gc0, int ldy, int M,
+                                                  int N, bool vec) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int gc = gc0 + 8 * k;
+        if (gc >= N) continue;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int gr = ra + 8 * e;
+            if (gr >= M) continue;
+            float* dst = y + static_cast<size_t>(gr) * ldy + gc;
+            const float2 v = o[2 * k + e];
+            if (vec && gc + 1 < N) {
+                *reinterpret_cast<float2*>(dst) = v;
             } else {
-                const float s = e ? sxb : sxa;
-                // ((float)acc * sx) * scale + bias in scalar IEEE steps (the compiler may contract packed
-                // mul + add chains into fma, which would change the bits), the activation on the pair
-                const float d0 = __fadd_rn(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v0)), s), sc.x), bi.x);
-                const float d1 = __fadd_rn(__fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(v1)), s), sc.y), bi.y);
-                const float2 o = epi_act2<ACTC>(make_float2(d0, d1), act, alpha);
-                const float o0 = o.x, o1 = o.y;
-                float* dst = y + static_cast<size_t>(gr) * ldy + gc;
-                if (vec && gc + 1 < N) {
-                    *reinterpret_cast<float2*>(dst) = make_float2(o0, o1);
-                } else {
-                    dst[0] = o0;
-                    if (gc + 1 < N) dst[1] = o1;
-                }
+                dst[0] = v.x;
+                if (gc + 1 < N) dst[1] = v.y;
             }
         }
     }
@@ -175,31 +212,42 @@ __device__ __forceinline__ void epi_block(const uint32_t (&r)[16], int ra, int g
 // tcgen05.ld 16x256b: four consecutive threads hold 8 consecutive columns of one row, so every store writes
 // whole 32-byte sectors straight from registers (no shared-memory transpose); the loads are double-buffered so
 // each block's load is in flight while the previous block is processed. The warp's column factors sit in
-// its shared-memory slot (written from the prefetched registers) and are read as broadcasts.
-// ACC_ONLY writes the raw int32 sums.
+// its shared-memory slot (written from the prefetched registers) as (scale, scale, bias, bias) per column pair
+// and are read as broadcasts. Tiles entirely inside the output store without bounds checks. ACC_ONLY writes the
+// raw int32 sums.
 template <int BN, bool ACC_ONLY, int ACTC>
 __device__ __forceinline__ void epi_tile_i8(uint32_t tbase, int r0, int n0, int c_lo, float* slot, int lane, const EpiPre& f,
                                             float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N,
                                             int act, float alpha) {
     constexpr int EPI_COLS = BN / 4;  // 64 or 32 columns: 2 or 1 column halves of 32
     constexpr int NB = 2 * (EPI_COLS / 32);  // 16x256b.x4 blocks per warp: (row half, column half)
-    float2* scs = reinterpret_cast<float2*>(slot);
-    float2* bis = scs + 32;
+    float4* cf = reinterpret_cast<float4*>(slot);
     if (!ACC_ONLY) {
         __syncwarp();
-        scs[lane] = f.sc;  // columns c_lo + 2 lane, +1
-        bis[lane] = f.bi;
+        cf[lane] = make_float4(f.sc.x, f.sc.y, f.bi.x, f.bi.y);  // columns c_lo + 2 lane, +1
         __syncwarp();
     }
     const int t4 = lane & 3, row = lane >> 2;
     const bool vec = (ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(y) & 7) == 0;
+    const bool full = vec && r0 + 32 <= M && n0 + c_lo + EPI_COLS <= N;
     uint32_t ra[16], rb[16];
     // block i: row half h = i % 2, column half cc = i / 2
     auto taddr = [&](int i) { return tbase + (static_cast<uint32_t>(16 * (i & 1)) << 16) + c_lo + 32 * (i >> 1); };
     auto run = [&](const uint32_t (&r)[16], int i) {
         const int h = i & 1, cc = i >> 1;
-        epi_block<ACC_ONLY, ACTC>(r, r0 + 16 * h + row, n0 + c_lo + 32 * cc + 2 * t4, f.sx[2 * h], f.sx[2 * h + 1],
-                                  scs + 16 * cc + t4, bis + 16 * cc + t4, y, acc_out, ldy, M, N, vec, act, alpha);
+        const int gr = r0 + 16 * h + row, gc = n0 + c_lo + 32 * cc + 2 * t4;
+        if (ACC_ONLY) {
+            epi_block_acc(r, gr, gc, acc_out, ldy, M, N);
+        } else {
+            float2 o[8];
+            epi_math<ACTC>(r, f.sx[2 * h], f.sx[2 * h + 1], cf + 16 * cc + t4, o, act, alpha);
+            if (full) {
+                float* rowa = y + static_cast<size_t>(gr) * ldy + gc;
+                epi_store_full(o, rowa, rowa + 8 * static_cast<size_t>(ldy));
+            } else {
+                epi_store_checked(o, y, gr, gc, ldy, M, N, vec);
+            }
+        }
     };
     kx::tmem_ld16x256b_x4(taddr(0), ra);
     kx::tmem_ld16_wait(ra);
@@ -214,6 +262,125 @@ __device__ __forceinline__ void epi_tile_i8(uint32_t tbase, int r0, int n0, int 
         run(ra, 2);
         kx::tmem_ld16_wait(rb);
         run(rb, 3);
+    }
+}
+
+// ------------------------------------------------------------------ int8 with a quantised output (QOUT)
+// The output of a hidden int8 layer is read only by the next int8 layer, and only quantised: row by row as
+// q = clamp(rint(y * (1 / sx)), +-127) with sx = max|y| / 127 over the whole row (kernix_qmatmul :110-142, the
+// next step's quantisation). A QOUT launch of the CTA-pair kernel writes q and sx instead of y, so there is no fp32
+// intermediate and no separate quantiser pass. Tiles are walked row-block-major, so the CTA tiles of one 128-row
+// group run at the same time on different clusters. Per CTA tile, once its accumulator is complete:
+//   pass 1: dequantise and activate exactly as the fp32 epilogue, write the fp32 values back over the accumulator
+//           in TMEM, and publish each row's max|y| (atomicMax on the IEEE bits of |y|, so NaN wins, as the
+//           quantiser's max) into rowmax; after a barrier of the CTA's 16 epilogue warps one thread counts the tile
+//           in the row group's counter;
+//   wait:   until every N-tile of the row group has been counted (bounded; a timeout sets the status word);
+//   pass 2: read the values back (one thread per row), scale by 1 / sx in the quantiser's IEEE steps, round to
+//           nearest even with the 1.5 * 2^23 addition (exact for |v| < 2^22; here |v| <= 127.0001), clamp, and store
+//           32 bytes of a row per 16-byte pair of stores; rows whose max is inf or NaN get sx = NaN and q = 0, as
+//           the quantiser gives them.
+// The same values, the same max and the same IEEE steps as the quantiser kernel on the fp32 output: q and sx are
+// bit for bit what kx_quant_rows would produce from y. The grid is a whole number of row groups' worth of clusters,
+// so a round of the round-robin walk covers whole row groups and a tile's wait is only for the tiles of the same
+// round (no deadlock either way: a tile's wait depends only on pass 1 of the tiles of its row group, which sit at
+// the same or the next round, and pass 1 of a round needs only the accumulator buffer freed two rounds earlier).
+struct QOut {
+    int8_t* q;         // M x ldq, the next layer's A operand; columns N .. ldq-1 are written as 0
+    float* sx;         // M row scales
+    uint32_t* rowmax;  // M, zero at launch
+    uint32_t* cnt;     // ceil(M / 128), zero at launch
+    uint32_t* zero;    // words this launch clears after its dependency wait (the next QOUT launch's rowmax and cnt)
+    int ldq, zero_words;
+};
+
+// pass 1 of one warp's part of a CTA tile (32 rows x 64 columns): rows r0 + 16h + lane/4 + 8e -> mx[2h + e]
+template <int ACTC>
+__device__ __forceinline__ void q_pass1(uint32_t tbase, int c_lo, const float4* __restrict__ cf, int lane, const EpiPre& f,
+                                        int act, float alpha, uint32_t (&mx)[4]) {
+    const int t4 = lane & 3;
+    uint32_t ra[16], rb[16];
+    auto taddr = [&](int i) { return tbase + (static_cast<uint32_t>(16 * (i & 1)) << 16) + c_lo + 32 * (i >> 1); };
+    auto run = [&](uint32_t (&r)[16], int i) {
+        const int h = i & 1, cc = i >> 1;
+        float2 o[8];
+        epi_math<ACTC>(r, f.sx[2 * h], f.sx[2 * h + 1], cf + 16 * cc + t4, o, act, alpha);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t bx = __float_as_uint(o[2 * k + e].x), by = __float_as_uint(o[2 * k + e].y);
+                mx[2 * h + e] = max(mx[2 * h + e], max(bx & 0x7FFFFFFFu, by & 0x7FFFFFFFu));
+                r[4 * k + 2 * e] = bx;
+                r[4 * k + 2 * e + 1] = by;
+            }
+        kx::tmem_st16x256b_x4(taddr(i), r);
+    };
+    kx::tmem_ld16x256b_x4(taddr(0), ra);
+    kx::tmem_ld16_wait(ra);
+    kx::tmem_ld16x256b_x4(taddr(1), rb);
+    run(ra, 0);
+    kx::tmem_ld16_wait(rb);
+    kx::tmem_ld16x256b_x4(taddr(2), ra);
+    run(rb, 1);
+    kx::tmem_ld16_wait(ra);
+    kx::tmem_ld16x256b_x4(taddr(3), rb);
+    run(ra, 2);
+    kx::tmem_ld16_wait(rb);
+    run(rb, 3);
+    kx::tmem_st_wait();
+}
+
+// one quantised byte of v (the quantiser's steps: rint(v * inv), clamp to +-127); inv is finite here
+__device__ __forceinline__ uint32_t q_byte(uint32_t vbits, float inv) {
+    const float t = __fadd_rn(__fmul_rn(__uint_as_float(vbits), inv), 12582912.0f);  // 1.5 * 2^23: rounds to an integer
+    const int qi = min(max(static_cast<int>(__float_as_uint(t)) - 0x4B400000, -127), 127);
+    return static_cast<uint32_t>(qi) & 0xFFu;
+}
+
+// pass 2 of one warp: thread = row r0 + lane (TMEM lane quarter), columns c_lo .. c_lo + 63 of the tile
+__device__ __forceinline__ void q_pass2(uint32_t tbase, int c_lo, int lane, float inv, bool nan_row, int gr, int gc0,
+                                        const QOut& qo, int M, int N) {
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        uint32_t v[32];
+        kx::tmem_ld32(tbase + c_lo + 32 * half, v);
+        kx::tmem_ld_wait();
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            w[j] = nan_row ? 0u
+                           : q_byte(v[4 * j], inv) | (q_byte(v[4 * j + 1], inv) << 8) | (q_byte(v[4 * j + 2], inv) << 16) |
+                                 (q_byte(v[4 * j + 3], inv) << 24);
+        const int gc = gc0 + 32 * half;
+        if (gr >= M || gc >= qo.ldq) continue;
+        if (gc + 32 > N) {  // the last columns: bytes at N and beyond are the zero padding up to ldq
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+#pragma unroll
+                for (int b = 0; b < 4; b++)
+                    if (gc + 4 * j + b >= N) w[j] &= ~(0xFFu << (8 * b));
+        }
+        uint4* dst = reinterpret_cast<uint4*>(qo.q + static_cast<size_t>(gr) * qo.ldq + gc);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        if (gc + 16 < qo.ldq) dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+}
+
+// wait (bounded) until the counter reaches target; false on a timeout (status set, abort raised) or abort
+__device__ __forceinline__ bool q_wait_count(const uint32_t* cnt, uint32_t target, volatile int* abort, int* status) {
+    const uint64_t t0 = kx::globaltimer();
+    for (uint32_t spin = 0;; spin++) {
+        if (kx::ld_acquire_gpu(cnt) >= target) return true;
+        if (*abort) return false;
+        if ((spin & 15) == 15) {
+            if (kx::globaltimer() - t0 > KX_WAIT_NS) {
+                *abort = 1;
+                if (status) atomicExch(status, KX_STATUS_TIMEOUT);
+                return false;
+            }
+            __nanosleep(128);
+        }
     }
 }
 
@@ -234,7 +401,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk = (K + C::BK - 1) / C::BK;
-    const TileMap tm{(M + BM - 1) / BM, (N + BN - 1) / BN};
+    const TileMap tm{(M + BM - 1) / BM, (N + BN - 1) / BN, false};
     const int n_tiles = tm.m_tiles * tm.n_tiles;
 
     if (threadIdx.x == 0) {
@@ -375,12 +542,12 @@ struct I8PairCfg {
     static constexpr uint32_t TMEM_COLS = 2 * BN;
 };
 
-template <int STAGES, bool ACC_ONLY, int ACTC>
+template <int STAGES, bool ACC_ONLY, int ACTC, bool QOUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(I8PairCfg<STAGES>::THREADS, 1)
 k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const float* __restrict__ sx, const float* __restrict__ scale, const float* __restrict__ bias,
                float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N, int K, int act, float alpha,
-               int* status) {
+               int* status, const QOut qo) {
     using C = I8PairCfg<STAGES>;
     constexpr int BN = C::BN;
     extern __shared__ uint8_t smem_raw[];
@@ -395,7 +562,7 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t rank = kx::cluster_ctarank();
     const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
     const int nk = (K + C::BK - 1) / C::BK;
-    const TileMap tm{(M + 2 * BM - 1) / (2 * BM), (N + BN - 1) / BN};  // pair tiles: 256 rows x 256 columns
+    const TileMap tm{(M + 2 * BM - 1) / (2 * BM), (N + BN - 1) / BN, QOUT};  // pair tiles: 256 rows x 256 columns
     const int n_tiles = tm.m_tiles * tm.n_tiles;
 
     if (threadIdx.x == 0) {
@@ -492,6 +659,10 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             epi_prefetch(cur, mt * 2 * BM + row_off, nt * BN + c_lo, lane, M, N, sx, scale, bias);
         }
         const uint32_t acc_empty0 = kx::mapa(kx::smem_u32(&ctl->acc_empty[0]), 0);
+        if constexpr (QOUT) {  // clear the next QOUT launch's row maxima and counters (this launch's dependency is met)
+            const int et = ew * 32 + lane, estride = static_cast<int>(gridDim.x) * C::EPI_WARPS * 32;
+            for (int i = static_cast<int>(blockIdx.x) * C::EPI_WARPS * 32 + et; i < qo.zero_words; i += estride) qo.zero[i] = 0;
+        }
         int j = 0;
         for (int t = cluster; t < n_tiles; t += n_clusters, j++) {
             int mt, nt;
@@ -502,10 +673,63 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tm.at(t + n_clusters, mt2, nt2);
                 epi_prefetch(nxt, mt2 * 2 * BM + row_off, nt2 * BN + c_lo, lane, M, N, sx, scale, bias);
             }
-            if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
-            kx::tc_fence_after();
-            epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), mt * 2 * BM + row_off,
-                                            nt * BN, c_lo, stg, lane, cur, y, acc_out, ldy, M, N, act, alpha);
+            const bool full_ok = __all_sync(0xffffffffu, kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status));
+            if constexpr (!QOUT) {
+                if (!full_ok) break;
+                kx::tc_fence_after();
+                epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), mt * 2 * BM + row_off,
+                                                nt * BN, c_lo, stg, lane, cur, y, acc_out, ldy, M, N, act, alpha);
+            } else {
+                // every epilogue warp of the CTA passes the same two barriers per tile, whatever happens, and leaves
+                // only on the OR of their abort states taken at the second one
+                const uint32_t tb = tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16);
+                const int r0 = mt * 2 * BM + row_off;       // this warp's first row
+                const int rg = mt * 2 + static_cast<int>(rank);  // this CTA's 128-row group
+                const bool live = rg * BM < M;              // the CTA has rows in the output
+                bool ok = full_ok;
+                if (ok) {
+                    kx::tc_fence_after();
+                    float4* cf = reinterpret_cast<float4*>(stg);
+                    __syncwarp();
+                    cf[lane] = make_float4(cur.sc.x, cur.sc.y, cur.bi.x, cur.bi.y);
+                    __syncwarp();
+                    uint32_t mx[4] = {0u, 0u, 0u, 0u};
+                    q_pass1<ACTC>(tb, c_lo, cf, lane, cur, act, alpha, mx);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        mx[i] = max(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+                        mx[i] = max(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+                    }
+                    if ((lane & 3) == 0)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int gr = r0 + 16 * (i >> 1) + (lane >> 2) + 8 * (i & 1);
+                            if (gr < M) atomicMax(qo.rowmax + gr, mx[i]);
+                        }
+                    __threadfence();
+                }
+                kx::named_bar(1, C::EPI_WARPS * 32);  // every warp of this CTA tile has published its rows
+                if (ok && live && ew == 0 && lane == 0) atomicAdd(qo.cnt + rg, 1u);
+                if (ok && live) {
+                    if (lane == 0) ok = q_wait_count(qo.cnt + rg, static_cast<uint32_t>(tm.n_tiles), abort_flag, status);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                }
+                if (ok) {
+                    const int gr = r0 + lane;
+                    const uint32_t m = gr < M ? kx::ld_relaxed_gpu(qo.rowmax + gr) : 0u;
+                    const bool nan_row = m >= 0x7F800000u;  // inf or NaN in the row: sx = NaN, q = 0
+                    float sxv = 1.0f, inv = 1.0f;
+                    if (nan_row) {
+                        sxv = __uint_as_float(0x7FC00000u);
+                    } else if (m != 0u) {
+                        sxv = __fdiv_rn(__uint_as_float(m), 127.0f);
+                        inv = __fdiv_rn(1.0f, sxv);
+                    }
+                    if (nt == 0 && c_lo == 0 && gr < M) qo.sx[gr] = sxv;
+                    q_pass2(tb, c_lo, lane, inv, nan_row, gr, nt * BN + c_lo, qo, M, N);
+                }
+                if (kx::named_bar_or(1, C::EPI_WARPS * 32, !ok || *abort_flag)) break;
+            }
             cur = nxt;
             kx::tc_fence_before();
             __syncwarp();
@@ -1854,10 +2078,10 @@ int max_pair_clusters(const void* kern, int threads, int smem) {
     return c;
 }
 
-template <bool ACC_ONLY, int ACTC>
+template <bool ACC_ONLY, int ACTC, bool QOUT = false>
 int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
                    const float* bias, float* y, int32_t* acc, int ldy, int m, int n, int k, int act, float alpha, int* status,
-                   cudaStream_t st) {
+                   cudaStream_t st, const QOut& qo = QOut{}) {
     constexpr int STAGES = 6;
     using C = I8PairCfg<STAGES>;
     CUtensorMap ta, tb;
@@ -1866,14 +2090,19 @@ int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq,
         make_map_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq, static_cast<uint64_t>(ldw), static_cast<uint64_t>(n),
                     static_cast<uint64_t>(ldw), C::BK, C::BN / 2) != 0)
         return -1;
-    auto kern = k_gemm_i8_pair<STAGES, ACC_ONLY, ACTC>;
+    auto kern = k_gemm_i8_pair<STAGES, ACC_ONLY, ACTC, QOUT>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
-    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + C::BN - 1) / C::BN);
+    const int n_tiles_n = (n + C::BN - 1) / C::BN;
+    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * n_tiles_n;
     int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
     if (clusters <= 0) clusters = sm_count() / 2;
+    if (QOUT) {  // a row group's tiles must all be resident at once, and a round of the walk covers whole row groups
+        if (n_tiles_n > clusters) return -1;
+        clusters = clusters / n_tiles_n * n_tiles_n;
+    }
     if (clusters > tiles) clusters = tiles;
     return kx::launch_pdl(kern, dim3(2 * clusters), dim3(C::THREADS), C::SMEM, st, ta, tb, sx, scale, bias, y, acc, ldy, m, n,
-                          k, act, alpha, status);
+                          k, act, alpha, status, qo);
 }
 
 template <int BN, bool CONV, int ACTC, bool DRAIN>
@@ -2267,6 +2496,26 @@ int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (n <= 128) return dispatch_i8<128>(xq, ldq, sx, wq, ldw, scale, bias, y, ldy, m, n, k, act, alpha, status, st);
     return dispatch_i8<256>(xq, ldq, sx, wq, ldw, scale, bias, y, ldy, m, n, k, act, alpha, status, st);
+}
+
+int kx_gemm_i8_q(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale, const float* bias,
+                 int m, int n, int k, int act, float alpha, int8_t* q_out, int ldq_out, float* sx_out, uint32_t* ctl,
+                 uint32_t* zero_next, int zero_words, int* status, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15) || n <= 128 || ldq_out < n || (ldq_out & 15) ||
+        q_out == nullptr || sx_out == nullptr || ctl == nullptr || (reinterpret_cast<uintptr_t>(q_out) & 15) ||
+        (zero_words > 0 && zero_next == nullptr))
+        return -1;
+    const QOut qo{q_out, sx_out, ctl, ctl + m, zero_next, ldq_out, zero_words};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (act_class(act)) {
+    case -1: return launch_i8_pair<false, -1, true>(xq, ldq, sx, wq, ldw, scale, bias, nullptr, nullptr, n, m, n, k, act, alpha, status, st, qo);
+    case 0: return launch_i8_pair<false, 0, true>(xq, ldq, sx, wq, ldw, scale, bias, nullptr, nullptr, n, m, n, k, act, alpha, status, st, qo);
+    case 1: return launch_i8_pair<false, 1, true>(xq, ldq, sx, wq, ldw, scale, bias, nullptr, nullptr, n, m, n, k, act, alpha, status, st, qo);
+    default:
+        return launch_i8_pair<false, ACT_GENERIC, true>(xq, ldq, sx, wq, ldw, scale, bias, nullptr, nullptr, n, m, n, k, act, alpha,
+                                                        status, st, qo);
+    }
 }
 
 int kx_linear_i8(const float* x, int ldx, int rows, int k, const int8_t* wq, int ldw, const float* scale, const float* bias,

@@ -62,6 +62,9 @@ typedef struct {
     int shard_c0, shard_n;  /* sharded LINEAR: this rank keeps output columns [shard_c0, shard_c0 + shard_n); 0 = whole */
     int fuse_add, fuse_res; /* fp32 LINEAR / ATTENTION whose output only feeds the next step, an elementwise ADD: the
                              * GEMM writes that ADD's output, adding value fuse_res (the ADD's other operand) */
+    int qout, qin, qpar;    /* int8 LINEAR chains: qout = the GEMM writes the next int8 step's quantised input (its
+                             * fp32 output is never materialised); qin = the input arrives quantised from the step
+                             * before; qpar = which of the two scratch slots holds this step's quantised input */
 } kx_step;
 
 /* Parsed graph (host side), the output of kx_graph_load */
@@ -81,6 +84,12 @@ typedef struct {
  * (include/kernix_model.h:1448-1601). Returns NULL and sets *err (static string) on failure. */
 kx_graph* kx_graph_load(const char* path, const char** err);
 void kx_graph_free(kx_graph* g);
+
+/* NCCL data plane (knx_nccl.c): a communicator on the current device, its release, and the all-gather of the
+ * column-sharded forward over it (a kernix_allgather_fn with the communicator as its context) */
+void* kx_nccl_comm_init(int rank, int world, const void* id);
+void kx_nccl_comm_free(void* comm);
+int kx_nccl_gather(void* ctx, const float* send, float* recv, size_t count, void* stream);
 
 /* in-place capable kinds (include/kernix_model.h:1397-1401) */
 int kx_inplace_ok(int kind);

@@ -48,9 +48,11 @@ constexpr int QT = 128;
 constexpr int QV = 8;  // float4 per thread kept in registers (rows up to 4096 columns in one read)
 
 __global__ void __launch_bounds__(QT) k_quant_rows(const float* __restrict__ x, int ldx, int k, int8_t* __restrict__ xq,
-                                                   int ldq, float* __restrict__ sx) {
+                                                   int ldq, float* __restrict__ sx, uint32_t* __restrict__ zero,
+                                                   int zero_words) {
     kx::griddep_wait();  // launched as a dependent of the kernel before it: x is its output
     kx::griddep_launch_dependents();
+    for (int i = blockIdx.x * QT + threadIdx.x; i < zero_words; i += gridDim.x * QT) zero[i] = 0;  // the next launch's counters
     const long row = blockIdx.x;
     const float* xr = x + row * ldx;
     int8_t* qr = xq + row * ldq;
@@ -1043,12 +1045,18 @@ int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y,
 }
 
 
-int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream) {
+int kx_quant_rows_z(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, uint32_t* zero, int zero_words,
+                    void* stream) {
     if (rows <= 0) return 0;
-    if (k <= 0 || ldq < k || ldx < k) return -1;
-    if (kx::launch_pdl(k_quant_rows, dim3(rows), dim3(QT), 0, static_cast<cudaStream_t>(stream), x, ldx, k, xq, ldq, sx) != 0)
+    if (k <= 0 || ldq < k || ldx < k || (zero_words > 0 && zero == nullptr)) return -1;
+    if (kx::launch_pdl(k_quant_rows, dim3(rows), dim3(QT), 0, static_cast<cudaStream_t>(stream), x, ldx, k, xq, ldq, sx, zero,
+                       zero_words) != 0)
         return -1;
     return launch_ok();
+}
+
+int kx_quant_rows(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, void* stream) {
+    return kx_quant_rows_z(x, ldx, rows, k, xq, ldq, sx, nullptr, 0, stream);
 }
 
 int kx_bias_act(const float* x, float* y, long rows, int cols, const float* bias, int act, float alpha, void* stream) {

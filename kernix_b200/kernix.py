@@ -53,6 +53,10 @@ def lib():
         L.kernix_capi_ane_dump.restype = ctypes.c_int
         L.kernix_model_load_sharded.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, vp, vp]
         L.kernix_model_load_sharded.restype = vp
+        L.kernix_model_load_sharded_nccl.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p]
+        L.kernix_model_load_sharded_nccl.restype = vp
+        L.kernix_nccl_unique_id.argtypes = [ctypes.c_char_p]
+        L.kernix_nccl_unique_id.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -67,13 +71,21 @@ class Model:
         identical results. None = library default, 0 = unlimited. ane: there is no Apple Neural Engine on a
         B200 host, so ane=True warns and runs on the GPU.
         shard: (rank, world, gather) to split the wide fp32 dense layers by output columns across `world`
-        processes (kernix_model_load_sharded); gather(send_ptr, recv_ptr, count, stream) all-gathers `count`
-        device floats per rank on the CUDA stream (see kernix_b200.shard.torch_allgather)."""
+        processes. gather is either the 128-byte NCCL unique id shared by all ranks (bytes, from
+        kernix_b200.shard.nccl_unique_id() on one rank): the runtime then all-gathers with NCCL itself
+        (kernix_model_load_sharded_nccl); or a callable gather(send_ptr, recv_ptr, count, stream) that all-gathers
+        `count` device floats per rank on the CUDA stream (kernix_model_load_sharded; see
+        kernix_b200.shard.torch_allgather)."""
         self._lock = threading.Lock()
         L = lib()
         self._gather_cb = None
         if shard is None:
             self._h = L.kernix_capi_load(os.fsencode(path))
+        elif isinstance(shard[2], (bytes, bytearray)):
+            rank, world, nccl_id = shard
+            if len(nccl_id) != 128:
+                raise ValueError("an NCCL unique id has 128 bytes")
+            self._h = L.kernix_model_load_sharded_nccl(os.fsencode(path), int(rank), int(world), bytes(nccl_id))
         else:
             rank, world, gather = shard
 

@@ -8,8 +8,11 @@ re-interleaves the gathered [W][rows][out / W] block into full rows and runs the
     import torch.distributed as dist
     from kernix_b200 import Model, shard
     dist.init_process_group("nccl")                      # torchrun, one process per GPU
-    m = Model(path, shard=(dist.get_rank(), dist.get_world_size(), shard.torch_allgather()))
+    uid = shard.share_nccl_id()                          # rank 0 makes an NCCL id, every rank receives it
+    m = Model(path, shard=(dist.get_rank(), dist.get_world_size(), uid))   # the runtime all-gathers with NCCL
     y = m(x)                                             # every rank gets the full output
+
+A host callback instead of the id (shard.torch_allgather()) routes each all-gather through torch.distributed.
 
 This is the multi-GPU form of the reference's per-call row split of one sgemm between two devices
 (src/kernix_metal.m:161-265): a layer too narrow in batch to split by samples is split by output columns, with
@@ -50,3 +53,23 @@ def torch_allgather(group=None):
             dist.all_gather_into_tensor(dst, src, group=group)
 
     return gather
+
+
+def nccl_unique_id():
+    """A new 128-byte NCCL unique id (kernix_nccl_unique_id): make it on one rank and give it to all."""
+    import ctypes
+
+    from .kernix import lib
+    buf = ctypes.create_string_buffer(128)
+    if lib().kernix_nccl_unique_id(buf) != 0:
+        raise RuntimeError("NCCL is not available")
+    return buf.raw
+
+
+def share_nccl_id(group=None):
+    """nccl_unique_id() made on rank 0 of the torch.distributed group and broadcast to every rank (bytes)."""
+    import torch
+    import torch.distributed as dist
+    obj = [nccl_unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]

@@ -1,5 +1,7 @@
-"""torchrun worker of tests/test_gpu_shard.py: c5 split by output columns over the ranks (NCCL all-gather);
-every rank compares its output with the unsharded model on its own GPU and prints SHARD_OK."""
+"""torchrun worker of tests/test_gpu_shard.py: c5 split by output columns over the ranks, once with the runtime's
+own NCCL all-gather (kernix_model_load_sharded_nccl: the id made on rank 0, shared through torch.distributed) and
+once through the torch.distributed callback; every rank compares both with the unsharded model on its own GPU
+(and the two sharded results with each other, bit for bit) and prints SHARD_OK."""
 import datetime
 import os
 import sys
@@ -23,13 +25,19 @@ def main():
     path = configs.model_path("c5")
     os.environ["KERNIX_DEVICE"] = str(local)
     x = configs.inputs("c5", 24)
-    ys = Model(path, shard=(rank, world, shard.torch_allgather()))(x)
+    m_nccl = Model(path, shard=(rank, world, shard.share_nccl_id()))
+    ys_nccl = m_nccl(x)
+    ys_nccl2 = m_nccl(x[:5])  # a second call over the same communicator, a different row count
+    m_nccl.close()
+    ys_cb = Model(path, shard=(rank, world, shard.torch_allgather()))(x)
     y1 = Model(path)(x)
-    err = float(np.abs(ys - y1).max() / np.abs(y1).max())
+    err = float(np.abs(ys_nccl - y1).max() / np.abs(y1).max())
+    err2 = float(np.abs(ys_nccl2 - y1[:5]).max() / np.abs(y1).max())
+    same = np.array_equal(ys_nccl, ys_cb)
     dist.barrier()
     dist.destroy_process_group()
-    print(f"rank {rank}: max rel diff sharded vs whole {err:.2e}")
-    if err <= 1e-6:
+    print(f"rank {rank}: max rel diff sharded (C NCCL) vs whole {err:.2e}, 5 rows {err2:.2e}, C NCCL == callback: {same}")
+    if err <= 1e-6 and err2 <= 1.5e-5 and same:
         print("SHARD_OK")
 
 

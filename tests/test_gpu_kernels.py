@@ -538,3 +538,47 @@ def test_bounded_wait_reports_timeout(libkx, arrive):
     else:
         assert int(status.item()) == 1 and 20_000_000 <= ns < 1_000_000_000
     assert torch.ones(4, device="cuda").sum().item() == 4.0  # the context is still usable
+
+
+@pytest.mark.parametrize("m,k,n,act", [(4096, 1024, 4096, 1), (300, 4096, 1024, -1), (333, 200, 1000, 0), (1, 64, 512, 1),
+                                       (1500, 512, 2304, 1)])
+def test_gemm_i8_quantised_output_equals_quantiser(kx, m, k, n, act):
+    """A hidden int8 layer with its quantisation fused into the epilogue (kx_gemm_i8_q) gives bit for bit the int8
+    rows and row scales that kx_quant_rows computes from kx_gemm_i8's fp32 output: the same max over the row (NaN
+    and inf rows included), sx = m / 127, rint(y * (1 / sx)) clamped to +-127, zero padding up to ldq. Two launches
+    in a row, the second's row maxima and counters cleared by the first (clear-ahead), the first's by torch."""
+    from kernix_b200.knx_writer import quantize_int8
+    rng = np.random.default_rng(m + k + n)
+    scale, q = quantize_int8((rng.standard_normal((k, n)) * 0.05).astype(F32))
+    wq, ldw = _prep_i8(kx, q)
+    dscale, db = dev(scale), dev(rng.standard_normal(n).astype(F32) * 0.1)
+    ldq, ldo = (k + 15) // 16 * 16, (n + 15) // 16 * 16
+    words = m + (m + 127) // 128
+    ctl = [torch.zeros(words, dtype=torch.int32, device="cuda") for _ in range(2)]
+    for call in range(2):
+        x = (rng.standard_normal((m, k)) * rng.uniform(0.1, 3, (m, 1))).astype(F32)
+        if m > 4:
+            x[1] = 0.0
+            x[2, 5] = np.nan
+            x[3] *= 1e37  # overflows to inf in the dequantisation: an inf row
+        dx = dev(x)
+        xq = torch.empty((m, ldq), dtype=torch.int8, device="cuda")
+        sx = torch.empty(m, dtype=torch.float32, device="cuda")
+        kx.call("kx_quant_rows", dx.data_ptr(), k, m, k, xq.data_ptr(), ldq, sx.data_ptr(), sp())
+        y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        st = status()
+        kx.call("kx_gemm_i8", xq.data_ptr(), ldq, sx.data_ptr(), wq.data_ptr(), ldw, dscale.data_ptr(), db.data_ptr(),
+                y.data_ptr(), n, m, n, k, act, 0.0, st.data_ptr(), sp())
+        want_q = torch.full((m, ldo), 77, dtype=torch.int8, device="cuda")
+        want_sx = torch.empty(m, dtype=torch.float32, device="cuda")
+        kx.call("kx_quant_rows", y.data_ptr(), n, m, n, want_q.data_ptr(), ldo, want_sx.data_ptr(), sp())
+        got_q = torch.full((m, ldo), 77, dtype=torch.int8, device="cuda")
+        got_sx = torch.empty(m, dtype=torch.float32, device="cuda")
+        kx.call("kx_gemm_i8_q", xq.data_ptr(), ldq, sx.data_ptr(), wq.data_ptr(), ldw, dscale.data_ptr(), db.data_ptr(),
+                m, n, k, act, 0.0, got_q.data_ptr(), ldo, got_sx.data_ptr(), ctl[call].data_ptr(), ctl[1 - call].data_ptr(),
+                words, st.data_ptr(), sp())
+        torch.cuda.synchronize()
+        check_status(st)
+        assert np.array_equal(host(got_q), host(want_q)), f"call {call}: int8 rows differ"
+        assert np.array_equal(host(got_sx).view(np.uint32), host(want_sx).view(np.uint32)), f"call {call}: row scales differ"
+    assert not host(ctl[0]).any(), "the second launch clears the first's row maxima and counters"

@@ -292,3 +292,32 @@ def test_model_api_contract(libkx, model_dir):
     assert y and np.array_equal(np.ctypeslib.as_array(y.contents.tensor, (2, 4)), x4)
     assert not L.kernix_model_forward(m, y)
     L.kernix_model_free(m)
+
+
+def _replica_devices():
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    return ["0,0"] + (["0,1"] if n >= 2 else []) + (["all"] if n >= 3 else [])
+
+
+@pytest.mark.parametrize("gpus", _replica_devices())
+@pytest.mark.parametrize("cfg,batch,ws_mb", [("c2", 1000, None), ("c4", 9, None), ("c1", 301, 1)])
+def test_batch_sharded_over_devices_equals_one_device(Model, model_dir, monkeypatch, gpus, cfg, batch, ws_mb):
+    """$KERNIX_GPUS: the model is loaded whole on every listed device and a host forward splits its samples into
+    contiguous shares, one per device, run concurrently and written at their offsets: every row equals the one-device
+    forward bit for bit (samples are independent; with "0,0" two replicas share one GPU), also with workspace
+    chunking inside each share, on repeated calls and for a batch smaller than the device count."""
+    from kernix_b200 import configs
+    p = cfg_path(cfg, model_dir)
+    x = configs.inputs(cfg, batch)
+    monkeypatch.setenv("KERNIX_PIPELINE", "1")  # the same piece cut on every device and in the reference run
+    monkeypatch.delenv("KERNIX_GPUS", raising=False)
+    one = Model(p, workspace_mb=ws_mb)
+    want = one(x)
+    want1 = one(x[: (x.shape[0] // batch)])
+    one.close()
+    monkeypatch.setenv("KERNIX_GPUS", gpus)
+    m = Model(p, workspace_mb=ws_mb)
+    for _ in range(2):
+        assert np.array_equal(m(x), want)
+    assert np.array_equal(m(x[: (x.shape[0] // batch)]), want1)  # one sample: the first device alone
+    m.close()
