@@ -108,6 +108,23 @@ KERNIX_API int kx_gemm_f32_res(const float* x, int ldx, const float* w_hi, const
  * hi = tf32(w), lo = w - hi (exact), zero padded. */
 KERNIX_API int kx_prep_f32_weight(const float* w_kn, int k, int n, float* w_hi, float* w_lo, int ldw, void* stream);
 
+/* A chain of small fp32 dense layers y_l = act_l(y_{l-1} . W_l + b_l) (kernix_dense :544-550 step after step, each
+ * reading only the previous output) and, if softmax, a row softmax of the last (floats_softmax_into
+ * include/kernix.h:652-657; then the last layer has at most 64 outputs), in ONE cooperative launch: each layer a phase
+ * of CUDA-core tiles over K ranges, partial sums in scratch, added in a fixed order by the next layer (the last
+ * layer's by a final phase), a bounded grid barrier after each phase; each layer's K ranges depend on its k and n only, so a row's result does not depend on the
+ * batch it is in. For batches whose tensor-core GEMMs are dominated by per-launch costs (rows <=
+ * KX_MLP_MAX_ROWS). w[l]: k[l] x n[l] row-major fp32; bias[l] may be NULL; ldx and every n[l] but the last multiples of
+ * 4, x and scratch 16-byte aligned; scratch: kx_mlp_chain_scratch_floats(m, k, n, n_layers) floats; bar: two words,
+ * zero before the first launch, kept between launches (reset them after a timeout). */
+#define KX_MLP_MAX_LAYERS 8
+#define KX_MLP_MAX_SPLIT 8
+#define KX_MLP_MAX_ROWS 512
+KERNIX_API int kx_mlp_chain(const float* x, int ldx, int m, int n_layers, const float* const* w, const float* const* bias,
+                            const int* k, const int* n, const int* act, const float* alpha, int softmax, float* y,
+                            float* scratch, uint32_t* bar, int* status, void* stream);
+KERNIX_API size_t kx_mlp_chain_scratch_floats(int m, const int* k, const int* n, int n_layers);
+
 /* ---- elementwise / row ops (memory-bound) ---- */
 
 /* y[r][c] = act(x[r][c] + bias[c]) (kernix_bias_act :528-541; ACT step :1864-1866). x == y allowed; bias may be NULL. */

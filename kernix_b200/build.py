@@ -27,7 +27,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvi
 CC_FLAGS = ["-std=gnu11", "-O2", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wextra", "-Wno-unused-parameter",
             "-I" + INCLUDE, "-I" + CSRC, "-I" + os.path.join(CUDA_HOME, "include")]
 
-CU_SOURCES = ["kx_gemm.cu", "kx_ops.cu", "kx_noalloc.cu", "kx_attn.cu", "kx_tensor.cu"]
+CU_SOURCES = ["kx_gemm.cu", "kx_ops.cu", "kx_noalloc.cu", "kx_attn.cu", "kx_tensor.cu", "kx_mlp.cu"]
 C_SOURCES = ["knx_load.c", "knx_model.c", "knx_nccl.c"]
 HEADERS = ["kx_sm100.cuh", "kx_act.cuh", "kx_pdl.cuh", "kx_internal.h"]
 

@@ -63,6 +63,8 @@ struct kx_model_impl {
     size_t scratch_per_row_max;
     int no_qchain;        /* 1 while tracing: every int8 step writes its fp32 output (int8 chains off) */
     void* nccl_comm;      /* the communicator of kernix_model_load_sharded_nccl (owned), else NULL */
+    float* mlp_scratch;   /* partial sums of the fused small-MLP chains (kx_mlp_chain), NULL if the model has none */
+    uint32_t* mlp_bar;    /* their grid-barrier words (zeroed at load; reset after a timeout) */
     /* batch sharding over the devices of $KERNIX_GPUS: whole-model replicas on the other devices; a host-memory
      * forward gives each device a contiguous share of the samples */
     int n_rep;
@@ -428,19 +430,86 @@ static void plan_fusions(kx_graph* g) {
  * output as its input, runs kx_gemm_i8_q: its epilogue writes the next step's quantised rows and row scales (the
  * kernix_qmatmul quantisation, bit for bit) instead of fp32 rows, so neither the fp32 intermediate nor a separate
  * quantiser pass exists. The quantised rows alternate between two scratch slots along the chain. Needs CTA-pair
- * tiles (more than 128 columns) and at most 64 tiles of 256 columns (a row group's tiles are resident at once). */
+ * tiles (more than 128 columns), at most 64 tiles of 256 columns (a row group's tiles are resident at once) and a
+ * reduction of at least KX_QCHAIN_MIN_K (the two-pass epilogue must hide under the tile's MMAs). */
+#define KX_QCHAIN_MIN_K 2048 /* below this the epilogue, not the MMAs, paces a tile (measured: K = 1024 gains nothing) */
 static void plan_qchain(kx_graph* g) {
     for (int i = 0; i < g->n_steps; i++) g->steps[i].qout = g->steps[i].qin = g->steps[i].qpar = 0;
     for (int i = 0; i + 1 < g->n_steps; i++) {
         kx_step* s = &g->steps[i];
         kx_step* t = &g->steps[i + 1];
-        const int int8_pair = s->kind == KERNIX_OP_LINEAR && s->w.int8 && s->out > 128 && (s->out + 255) / 256 <= 64;
+        /* the fused epilogue pays only where the MMAs of a tile outlast it: long reductions */
+        const int int8_pair = s->kind == KERNIX_OP_LINEAR && s->w.int8 && s->out > 128 && (s->out + 255) / 256 <= 64 &&
+                              s->in >= KX_QCHAIN_MIN_K;
         if (!int8_pair || t->kind != KERNIX_OP_LINEAR || !t->w.int8 || t->n_in != 1 || t->inp[0] != i + 1) continue;
         if (g->vals[i + 1].last != i + 1 || g->out_v == i + 1 || t->in != s->out) continue;
         s->qout = 1;
         t->qin = 1;
         t->qpar = 1 - s->qpar;
     }
+}
+
+/* Small MLPs: a run of fp32 LINEAR steps, each after the first reading only the previous step's output, which
+ * nothing else reads, optionally followed by a SOFTMAX of the last output (at most 64 columns), runs as one
+ * kx_mlp_chain launch when a chunk has at most KX_MLP_MAX_ROWS rows (the tensor-core GEMMs' per-launch costs
+ * dominate there). Chains that end in a fused residual ADD are left to the GEMMs (their fusion keeps the forward
+ * bit-identical to running the steps one by one). */
+#define KX_MLP_MAX_WEIGHTS ((size_t)1 << 21) /* weight floats of a fused small-MLP chain (8 MB) */
+static void plan_mlp(kx_graph* g) {
+    for (int i = 0; i < g->n_steps; i++) g->steps[i].mlp_n = g->steps[i].mlp_layers = 0;
+    const char* off = getenv("KERNIX_NO_MLP_CHAIN"); /* 1: always the per-step GEMMs (tests compare the two) */
+    if (off && *off && *off != '0') return;
+    for (int i = 0; i < g->n_steps;) {
+        int j = i;
+        while (j < g->n_steps && j - i < KX_MLP_MAX_LAYERS) {
+            const kx_step* s = &g->steps[j];
+            if (s->kind != KERNIX_OP_LINEAR || s->w.int8 || s->shard_n > 0 || s->fuse_add) break;
+            if (j > i && (s->n_in != 1 || s->inp[0] != j || g->vals[j].last != j || g->out_v == j)) break;
+            j++;
+        }
+        const int layers = j - i;
+        int ok = layers >= 1 && g->steps[i].in % 4 == 0;
+        size_t wfloats = 0;
+        for (int l = i; l < j; l++) wfloats += (size_t)g->steps[l].in * (size_t)g->steps[l].out;
+        ok = ok && wfloats <= KX_MLP_MAX_WEIGHTS; /* small weights only: larger layers belong on the tensor cores */
+        for (int l = i; ok && l + 1 < j; l++) ok = g->steps[l].out % 4 == 0;
+        int sm = 0;
+        if (ok && j < g->n_steps) {
+            const kx_step* t = &g->steps[j];
+            sm = t->kind == KERNIX_OP_SOFTMAX && t->inp[0] == j && g->vals[j].last == j && g->out_v != j &&
+                 g->steps[j - 1].out <= 64;
+        }
+        if (ok && layers + sm >= 2) {
+            g->steps[i].mlp_layers = layers;
+            g->steps[i].mlp_n = layers + sm;
+            i = j + sm;
+        } else {
+            i++;
+        }
+    }
+}
+
+/* the fused small-MLP chain starting at step i over `rin` rows (kx_mlp_chain) */
+static int mlp_run(kernix_model* m, int i, long rin) {
+    struct kx_model_impl* im = m->impl;
+    kx_graph* g = im->g;
+    const kx_step* s0 = &g->steps[i];
+    const float* w[KX_MLP_MAX_LAYERS];
+    const float* b[KX_MLP_MAX_LAYERS];
+    int k[KX_MLP_MAX_LAYERS], n[KX_MLP_MAX_LAYERS], act[KX_MLP_MAX_LAYERS];
+    float alpha[KX_MLP_MAX_LAYERS];
+    for (int l = 0; l < s0->mlp_layers; l++) {
+        const kx_step* s = &g->steps[i + l];
+        w[l] = s->w.d_raw;
+        b[l] = s->d_bias;
+        k[l] = s->in;
+        n[l] = s->out;
+        act[l] = s->act;
+        alpha[l] = s->alpha;
+    }
+    return kx_mlp_chain(val_ptr(im, s0->inp[0]), s0->in, (int)rin, s0->mlp_layers, w, b, k, n, act, alpha,
+                        s0->mlp_n > s0->mlp_layers, val_ptr(im, i + s0->mlp_n), im->mlp_scratch, im->mlp_bar, im->status,
+                        im->stream);
 }
 
 /* one step over B samples; fused: the step's GEMM also performs the next step, an ADD (plan_fusions) */
@@ -665,6 +734,15 @@ static int chunk_run(kernix_model* m, int B) {
         const kx_step* s = &im->g->steps[i];
         /* a fused LINEAR must take the tensor-core path (the skinny path for few rows has no residual) */
         const long rin = (long)B * im->g->vals[s->inp[0]].r;
+        if (s->mlp_n > 0 && rin <= KX_MLP_MAX_ROWS && im->mlp_scratch != NULL && !im->no_qchain) {
+            if (mlp_run(m, i, rin) != 0) {
+                fprintf(stderr, "forward: the fused dense chain at step %d failed to launch: %s\n", i,
+                        cudaGetErrorString(cudaGetLastError()));
+                return -1;
+            }
+            i += s->mlp_n - 1;
+            continue;
+        }
         const int fused = s->fuse_add && (s->kind == KERNIX_OP_ATTENTION || !(rin <= KX_SKINNY_MAX_ROWS && s->w.d_raw != NULL &&
                                                                               im->skinny_part != NULL));
         if (step_run(m, i, B, fused) != 0) {
@@ -890,6 +968,7 @@ static int forward_one(kernix_model* m, const float* x, int rows, float* out) {
     if (*im->status_h != KX_STATUS_OK) {
         fprintf(stderr, "forward: a kernel gave up waiting (status %d)\n", *im->status_h);
         cudaMemsetAsync(im->status, 0, sizeof(int), st);
+        if (im->mlp_bar) cudaMemsetAsync(im->mlp_bar, 0, 2 * sizeof(uint32_t), st);
         return -1;
     }
     pipe_tune(im);
@@ -943,6 +1022,7 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
         }
     plan_fusions(g);
     plan_qchain(g);
+    plan_mlp(g);
     kernix_model* m = calloc(1, sizeof *m);
     struct kx_model_impl* im = calloc(1, sizeof *im);
     if (m == NULL || im == NULL) {
@@ -1012,6 +1092,24 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
         }
         if (mx > 0 && cudaMalloc((void**)&im->skinny_part, mx * sizeof(float)) != cudaSuccess) why = "cannot allocate device memory";
         im->skinny_floats = mx;
+    }
+    if (why == NULL) { /* fused small-MLP chains: partial sums for up to KX_MLP_MAX_ROWS rows, the largest chain */
+        size_t mx = 0;
+        for (int i = 0; i < g->n_steps; i++) {
+            const kx_step* s = &g->steps[i];
+            if (s->mlp_n == 0) continue;
+            int k[KX_MLP_MAX_LAYERS], n[KX_MLP_MAX_LAYERS];
+            for (int l = 0; l < s->mlp_layers; l++) {
+                k[l] = g->steps[i + l].in;
+                n[l] = g->steps[i + l].out;
+            }
+            const size_t f = kx_mlp_chain_scratch_floats(KX_MLP_MAX_ROWS, k, n, s->mlp_layers);
+            if (f > mx) mx = f;
+        }
+        if (mx > 0 && (cudaMalloc((void**)&im->mlp_scratch, mx * sizeof(float)) != cudaSuccess ||
+                       cudaMalloc((void**)&im->mlp_bar, 2 * sizeof(uint32_t)) != cudaSuccess ||
+                       cudaMemsetAsync(im->mlp_bar, 0, 2 * sizeof(uint32_t), im->stream) != cudaSuccess))
+            why = "cannot allocate device memory";
     }
     if (prev >= 0 && prev != im->device) cudaSetDevice(prev);
     if (why != NULL) {
@@ -1122,6 +1220,8 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
             for (int i = 0; i < im->g->n_steps; i++) step_dev_free(&im->g->steps[i]);
         if (im->status_h) cudaFreeHost(im->status_h);
         cudaFree(im->skinny_part);
+        cudaFree(im->mlp_scratch);
+        cudaFree(im->mlp_bar);
         for (int i = 0; i < KX_PIPE_MAX; i++) {
             cudaEvent_t* evs[3] = {im->ev_in, im->ev_comp, im->ev_out};
             for (int k = 0; k < 3; k++)
@@ -1217,7 +1317,10 @@ KERNIX_API int kernix_model_check(kernix_model* m) {
     int prev, v = 0;
     if (dev_guard_enter(m, &prev) != 0) return -1;
     if (cudaMemcpy(&v, m->impl->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) v = -1;
-    if (v != 0) cudaMemset(m->impl->status, 0, sizeof(int));
+    if (v != 0) {
+        cudaMemset(m->impl->status, 0, sizeof(int));
+        if (m->impl->mlp_bar) cudaMemset(m->impl->mlp_bar, 0, 2 * sizeof(uint32_t)); /* a barrier may have given up */
+    }
     dev_guard_leave(m, prev);
     return v == 0 ? 0 : -1;
 }

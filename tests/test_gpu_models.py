@@ -321,3 +321,50 @@ def test_batch_sharded_over_devices_equals_one_device(Model, model_dir, monkeypa
         assert np.array_equal(m(x), want)
     assert np.array_equal(m(x[: (x.shape[0] // batch)]), want1)  # one sample: the first device alone
     m.close()
+
+
+@pytest.mark.parametrize("dims,acts,softmax,rows", [
+    ((784, 512, 256, 10), ("relu", "relu"), True, 256),  # configuration c1's shapes
+    ((64, 128, 10), ("gelu",), True, 13),
+    ((32, 48, 8), ("tanh",), False, 1),
+    ((256, 256, 256, 128, 64), ("relu", "silu", "relu"), False, 500),
+    ((100, 36, 12), ("relu",), True, 333),
+    ((8, 2048, 4), ("sigmoid",), False, 77)])
+def test_fused_mlp_chain(Model, model_dir, monkeypatch, dims, acts, softmax, rows):
+    """A small fp32 MLP (+ softmax) runs as one kx_mlp_chain launch at <= 512 rows: within the dense-MLP bound 1e-5 of
+    the oracle and of the per-step tensor-core path ($KERNIX_NO_MLP_CHAIN=1), and every row independent of the batch
+    it is in (a host forward cut into 1 or 3 pieces, and the first 5 rows alone, give the same bits). Larger batches
+    take the per-step GEMMs, still within 1e-5."""
+    from kernix_b200 import knx_writer
+    rng = np.random.default_rng(sum(dims) + rows)
+    p = f"{model_dir}/mlp_{'_'.join(map(str, dims))}.knx"
+    s = knx_writer.Sequential()
+    for i in range(len(dims) - 1):
+        s.linear((rng.standard_normal((dims[i], dims[i + 1])) * np.sqrt(2.0 / dims[i])).astype(F32),
+                 rng.uniform(-0.1, 0.1, dims[i + 1]).astype(F32))
+        if i < len(dims) - 2:
+            s.act(acts[i])
+    if softmax:
+        s.softmax()
+    s.write(p)
+    x = rng.uniform(-1, 1, (rows, dims[0])).astype(F32)
+    want = ko.forward(ko.load(p), x)
+    monkeypatch.delenv("KERNIX_NO_MLP_CHAIN", raising=False)
+    outs = []
+    for pieces in ("1", "3"):
+        monkeypatch.setenv("KERNIX_PIPELINE", pieces)
+        m = Model(p)
+        outs.append(m(x))
+        if pieces == "1":
+            assert np.array_equal(m(x[:5]), outs[0][:5])
+        m.close()
+    assert np.array_equal(outs[0], outs[1])
+    monkeypatch.setenv("KERNIX_NO_MLP_CHAIN", "1")
+    gemm = Model(p)(x)
+    e_fused, e_gemm = rel_err(outs[0], want), rel_err(gemm, want)
+    print(f"{dims} x {rows}: fused chain {e_fused:.2e}, per-step GEMMs {e_gemm:.2e}")
+    assert e_fused <= 1e-5 and e_gemm <= 1e-5
+    monkeypatch.delenv("KERNIX_NO_MLP_CHAIN")
+    big = np.concatenate([x, x, x])  # above the chain's row limit: the GEMMs
+    got_big = Model(p)(big)
+    assert rel_err(got_big, np.concatenate([want, want, want])) <= 1e-5
