@@ -50,6 +50,19 @@ KERNIX_API int kx_gemm_i8_q(const int8_t* xq, int ldq, const float* sx, const in
                             const float* bias, int m, int n, int k, int act, float alpha, int8_t* q_out, int ldq_out,
                             float* sx_out, uint32_t* ctl, uint32_t* zero_next, int zero_words, int* status, void* stream);
 
+/* A chain of n_layers (2..4) int8 LINEAR steps (kernix_qmatmul :99-182 plus the activation :1854-1856, step after
+ * step, each hidden output quantised as the next step's input as kx_quant_rows would) in ONE persistent launch of the
+ * CTA-pair int8 GEMM, every layer's tiles in one walk: a tile of layer l > 0 starts once the rows it reads are
+ * quantised. a[0] / sx[0]: the chain input quantised (kx_quant_rows_z); a[l] / sx[l] = sx_out[l-1] for l > 0: the
+ * buffers layer l-1 writes (m x lda[l] int8, 16-byte aligned; m floats). y: m x n[last] fp32. ctl: (n_layers - 1) x
+ * (m + 2 * ceil(m / 128)) words, zero at launch (clear them with the quantiser before). Every n[l] > 128, at most 64
+ * tiles of 256 columns per layer, hidden layers of one activation class (ReLU, GELU, none or another); else -1.
+ * Bit for bit the results of running the steps one by one. */
+KERNIX_API int kx_i8_chain(int n_layers, int m, const int8_t* const* a, const int* lda, const float* const* sx,
+                           const int8_t* const* wq, const int* ldw, const float* const* scale, const float* const* bias,
+                           const int* k, const int* n, const int* act, const float* alpha, float* const* sx_out,
+                           uint32_t* ctl, float* y, int* status, void* stream);
+
 /* One int8 LINEAR step from fp32 activations, the whole of kernix_qmatmul plus the step's activation
  * (include/kernix_model.h:99-182, :1854-1856): quantise x's rows into xq_scratch (rows x ldq int8, ldq =
  * k rounded up to 16) and sx_scratch (rows floats), then y = act(((float)acc * sx) * scale + bias) with the

@@ -308,6 +308,11 @@ static size_t step_scratch(const kx_graph* g, const kx_step* s, size_t* per_samp
     const kx_val* vi = &g->vals[s->inp[0]];
     if (s->kind == KERNIX_OP_LINEAR && s->shard_n > 0) { /* local slice, then the gathered [world][rows][slice] */
         *per_sample = (size_t)vi->r * ((size_t)s->shard_n + (size_t)s->out) * sizeof(float) + 2 * KX_ALIGN;
+    } else if (s->kind == KERNIX_OP_LINEAR && s->w.int8 && s->i8c_n > 0) { /* a one-launch chain: int8 input of every
+                                                                               * layer + row scales, control words */
+        size_t b = 0;
+        for (int l = 0; l < s->i8c_n; l++) b += round_up((size_t)s[l].in, 16) + 4 + (l > 0 ? 3 * 4 : 0);
+        *per_sample = (size_t)vi->r * b + 4 * (size_t)s->i8c_n * KX_ALIGN;
     } else if (s->kind == KERNIX_OP_LINEAR && s->w.int8) { /* two int8 slots (rows x pitch + row scales), two ctl arrays */
         *per_sample = (size_t)vi->r * (2 * (int8_pitch(g) + 4) + 2 * 8) + 8 * KX_ALIGN;
     } else if (s->kind == KERNIX_OP_LSTM || s->kind == KERNIX_OP_GRU || s->kind == KERNIX_OP_RNN) {
@@ -432,6 +437,35 @@ static void plan_fusions(kx_graph* g) {
  * quantiser pass exists. The quantised rows alternate between two scratch slots along the chain. Needs CTA-pair
  * tiles (more than 128 columns), at most 64 tiles of 256 columns (a row group's tiles are resident at once) and a
  * reduction of at least KX_QCHAIN_MIN_K (the two-pass epilogue must hide under the tile's MMAs). */
+static int act_kind(int act) { return act == KERNIX_ACT_NONE || act == KERNIX_ACT_RELU || act == KERNIX_ACT_GELU ? act : 99; }
+
+/* int8 chains for one launch (kx_i8_chain): 2 to 4 int8 LINEAR steps, each after the first reading only the previous
+ * step's output, which nothing else reads; every layer on CTA-pair tiles (more than 128 outputs, at most 64 tiles of
+ * 256), the hidden layers' activations of one kind */
+static void plan_i8chain(kx_graph* g) {
+    for (int i = 0; i < g->n_steps; i++) g->steps[i].i8c_n = g->steps[i].i8c_in = 0;
+    const char* off = getenv("KERNIX_NO_I8_CHAIN"); /* 1: int8 layers launch one by one (tests compare the two) */
+    if (off && *off && *off != '0') return;
+    for (int i = 0; i < g->n_steps;) {
+        int j = i;
+        while (j < g->n_steps && j - i < 4) {
+            const kx_step* s = &g->steps[j];
+            if (s->kind != KERNIX_OP_LINEAR || !s->w.int8 || s->out <= 128 || (s->out + 255) / 256 > 64) break;
+            if (j > i && (s->n_in != 1 || s->inp[0] != j || g->vals[j].last != j || g->out_v == j || s->in != g->steps[j - 1].out))
+                break;
+            if (j > i + 1 && act_kind(g->steps[j - 1].act) != act_kind(g->steps[i].act)) break;
+            j++;
+        }
+        if (j - i >= 2) {
+            g->steps[i].i8c_n = j - i;
+            for (int l = i; l < j; l++) g->steps[l].i8c_in = 1;
+            i = j;
+        } else {
+            i++;
+        }
+    }
+}
+
 #define KX_QCHAIN_MIN_K 2048 /* below this the epilogue, not the MMAs, paces a tile (measured: K = 1024 gains nothing) */
 static void plan_qchain(kx_graph* g) {
     for (int i = 0; i < g->n_steps; i++) g->steps[i].qout = g->steps[i].qin = g->steps[i].qpar = 0;
@@ -442,6 +476,7 @@ static void plan_qchain(kx_graph* g) {
         const int int8_pair = s->kind == KERNIX_OP_LINEAR && s->w.int8 && s->out > 128 && (s->out + 255) / 256 <= 64 &&
                               s->in >= KX_QCHAIN_MIN_K;
         if (!int8_pair || t->kind != KERNIX_OP_LINEAR || !t->w.int8 || t->n_in != 1 || t->inp[0] != i + 1) continue;
+        if (s->i8c_in || t->i8c_in) continue; /* runs inside a one-launch chain */
         if (g->vals[i + 1].last != i + 1 || g->out_v == i + 1 || t->in != s->out) continue;
         s->qout = 1;
         t->qin = 1;
@@ -510,6 +545,47 @@ static int mlp_run(kernix_model* m, int i, long rin) {
     return kx_mlp_chain(val_ptr(im, s0->inp[0]), s0->in, (int)rin, s0->mlp_layers, w, b, k, n, act, alpha,
                         s0->mlp_n > s0->mlp_layers, val_ptr(im, i + s0->mlp_n), im->mlp_scratch, im->mlp_bar, im->status,
                         im->stream);
+}
+
+/* the one-launch int8 chain starting at step i over `rin` rows: quantise its input (clearing the chain's control
+ * words), then kx_i8_chain; scratch: per layer its int8 input (rows x K rounded to 16) and row scales, then the
+ * control words */
+static int i8chain_run(kernix_model* m, int i, long rin) {
+    struct kx_model_impl* im = m->impl;
+    kx_graph* g = im->g;
+    const kx_step* s0 = &g->steps[i];
+    const int n = s0->i8c_n;
+    const int8_t* a[4];
+    int lda[4], k[4], nn[4], act[4], ldw[4];
+    const float *sx[4], *scale[4], *bias[4];
+    float* sx_out[4] = {NULL, NULL, NULL, NULL};
+    float alpha[4];
+    const int8_t* wq[4];
+    uint8_t* p = (uint8_t*)align_ptr(im->scratch);
+    for (int l = 0; l < n; l++) {
+        const kx_step* s = &g->steps[i + l];
+        lda[l] = (int)round_up((size_t)s->in, 16);
+        a[l] = (const int8_t*)p;
+        p = (uint8_t*)align_ptr(p + (size_t)rin * lda[l]);
+        sx[l] = (const float*)p;
+        if (l > 0) sx_out[l - 1] = (float*)p;
+        p = (uint8_t*)align_ptr(p + (size_t)rin * sizeof(float));
+        wq[l] = s->w.d_q;
+        ldw[l] = s->w.ldw;
+        scale[l] = s->w.d_scale;
+        bias[l] = s->d_bias;
+        k[l] = s->in;
+        nn[l] = s->out;
+        act[l] = s->act;
+        alpha[l] = s->alpha;
+    }
+    uint32_t* ctl = (uint32_t*)p;
+    const size_t words = (size_t)(n - 1) * ((size_t)rin + 2 * (((size_t)rin + 127) / 128));
+    if (kx_quant_rows_z(val_ptr(im, s0->inp[0]), s0->in, (int)rin, s0->in, (int8_t*)a[0], lda[0], (float*)sx[0], ctl, (int)words,
+                        im->stream) != 0)
+        return -1;
+    return kx_i8_chain(n, (int)rin, a, lda, sx, wq, ldw, scale, bias, k, nn, act, alpha, sx_out, ctl, val_ptr(im, i + n),
+                       im->status, im->stream);
 }
 
 /* one step over B samples; fused: the step's GEMM also performs the next step, an ADD (plan_fusions) */
@@ -734,6 +810,15 @@ static int chunk_run(kernix_model* m, int B) {
         const kx_step* s = &im->g->steps[i];
         /* a fused LINEAR must take the tensor-core path (the skinny path for few rows has no residual) */
         const long rin = (long)B * im->g->vals[s->inp[0]].r;
+        if (s->i8c_n > 0 && !im->no_qchain) {
+            if (i8chain_run(m, i, rin) != 0) {
+                fprintf(stderr, "forward: the int8 chain at step %d failed to launch: %s\n", i,
+                        cudaGetErrorString(cudaGetLastError()));
+                return -1;
+            }
+            i += s->i8c_n - 1;
+            continue;
+        }
         if (s->mlp_n > 0 && rin <= KX_MLP_MAX_ROWS && im->mlp_scratch != NULL && !im->no_qchain) {
             if (mlp_run(m, i, rin) != 0) {
                 fprintf(stderr, "forward: the fused dense chain at step %d failed to launch: %s\n", i,
@@ -1021,6 +1106,7 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
             }
         }
     plan_fusions(g);
+    plan_i8chain(g);
     plan_qchain(g);
     plan_mlp(g);
     kernix_model* m = calloc(1, sizeof *m);

@@ -338,22 +338,25 @@ __device__ __forceinline__ uint32_t q_byte(uint32_t vbits, float inv) {
     return static_cast<uint32_t>(qi) & 0xFFu;
 }
 
-// pass 2 of one warp: thread = row r0 + lane (TMEM lane quarter), columns c_lo .. c_lo + 63 of the tile
+// pass 2 of one warp: thread = row r0 + lane (TMEM lane quarter), columns c_lo .. c_lo + 63 of the tile; both
+// 32-column loads are in flight before the first is used
 __device__ __forceinline__ void q_pass2(uint32_t tbase, int c_lo, int lane, float inv, bool nan_row, int gr, int gc0,
                                         const QOut& qo, int M, int N) {
+    uint32_t v[2][32];
+    kx::tmem_ld32(tbase + c_lo, v[0]);
+    kx::tmem_ld32(tbase + c_lo + 32, v[1]);
+    kx::tmem_ld_wait();
+    if (gr >= M) return;
 #pragma unroll
     for (int half = 0; half < 2; half++) {
-        uint32_t v[32];
-        kx::tmem_ld32(tbase + c_lo + 32 * half, v);
-        kx::tmem_ld_wait();
         uint32_t w[8];
 #pragma unroll
         for (int j = 0; j < 8; j++)
             w[j] = nan_row ? 0u
-                           : q_byte(v[4 * j], inv) | (q_byte(v[4 * j + 1], inv) << 8) | (q_byte(v[4 * j + 2], inv) << 16) |
-                                 (q_byte(v[4 * j + 3], inv) << 24);
+                           : q_byte(v[half][4 * j], inv) | (q_byte(v[half][4 * j + 1], inv) << 8) |
+                                 (q_byte(v[half][4 * j + 2], inv) << 16) | (q_byte(v[half][4 * j + 3], inv) << 24);
         const int gc = gc0 + 32 * half;
-        if (gr >= M || gc >= qo.ldq) continue;
+        if (gc >= qo.ldq) continue;
         if (gc + 32 > N) {  // the last columns: bytes at N and beyond are the zero padding up to ldq
 #pragma unroll
             for (int j = 0; j < 8; j++)
@@ -370,16 +373,13 @@ __device__ __forceinline__ void q_pass2(uint32_t tbase, int c_lo, int lane, floa
 // wait (bounded) until the counter reaches target; false on a timeout (status set, abort raised) or abort
 __device__ __forceinline__ bool q_wait_count(const uint32_t* cnt, uint32_t target, volatile int* abort, int* status) {
     const uint64_t t0 = kx::globaltimer();
-    for (uint32_t spin = 0;; spin++) {
+    for (uint32_t spin = 0;; spin++) {  // polled without sleeping: the other tiles of a row group finish together
         if (kx::ld_acquire_gpu(cnt) >= target) return true;
         if (*abort) return false;
-        if ((spin & 15) == 15) {
-            if (kx::globaltimer() - t0 > KX_WAIT_NS) {
-                *abort = 1;
-                if (status) atomicExch(status, KX_STATUS_TIMEOUT);
-                return false;
-            }
-            __nanosleep(128);
+        if ((spin & 63) == 63 && kx::globaltimer() - t0 > KX_WAIT_NS) {
+            *abort = 1;
+            if (status) atomicExch(status, KX_STATUS_TIMEOUT);
+            return false;
         }
     }
 }
@@ -738,6 +738,265 @@ k_gemm_i8_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     kx::tc_fence_before();
     kx::cluster_sync();  // no CTA leaves while its peer may still signal it or read its shared memory
+    if (warp == 1) {
+        kx::tc_fence_after();
+        kx::tmem_dealloc_pair(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ int8 layer chains in one launch
+// A chain of int8 LINEAR steps (kernix_qmatmul :99-182 and the activation :1854-1856 per step, each layer's output
+// quantised as the next layer's input) as ONE persistent launch of the CTA-pair GEMM: the launch, set-up and pipeline
+// fill are paid once, and a layer's first tiles start while the previous layer's last tiles finish. Tiles of every
+// layer are walked in one round-robin order (layer by layer, row-block-major inside a layer). Hidden layers use the
+// quantised-output epilogue (QOUT above); after a CTA tile's int8 rows are stored it counts the tile in its row
+// group's `ready` word. The producer of a tile of layer l > 0 waits (bounded) until its CTA's 128-row group of layer
+// l - 1 is complete -- every N-tile counted -- then issues its TMA loads of those rows. The last layer writes fp32.
+// Waits only ever point to tiles earlier in the walk, whose progress needs nothing later: no deadlock (all clusters
+// are resident; a wait that runs out sets the status word).
+constexpr int KX_I8C_MAX = 4;
+struct I8CLayer {
+    const float* sx;     // row scales of the layer's int8 input (layer 0: the quantiser's; else the previous layer's)
+    const float* scale;  // per-output-channel weight scales
+    const float* bias;
+    float* y;            // the last layer's fp32 output (n columns per row)
+    QOut qo;             // hidden layers: the next layer's int8 rows and row scales
+    uint32_t* ready;     // hidden layers: per 128-row group, CTA tiles whose int8 rows are stored
+    int n, k, act, n_tiles_n, tile0;
+    float alpha;
+};
+struct I8Chain {
+    I8CLayer L[KX_I8C_MAX];
+    int n_layers, total_tiles;
+};
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// bounded wait until *w >= target (acquire), then order the async proxy (TMA) after it
+__device__ __forceinline__ bool wait_ready(const uint32_t* w, uint32_t target, volatile int* abort, int* status) {
+    if (!q_wait_count(w, target, abort, status)) return false;
+    fence_proxy_async_global();
+    return true;
+}
+
+template <int STAGES, int ACTH, int ACTL>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(I8PairCfg<STAGES>::THREADS, 1)
+k_i8_chain(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+           const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmA3,
+           const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+           const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmB3, const I8Chain ch, int M,
+           int* status) {
+    using C = I8PairCfg<STAGES>;
+    constexpr int BN = C::BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align1024(smem_raw);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint8_t* sE = sB + STAGES * C::B_BYTES;
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(sE + C::STAGE_EPI);
+    volatile int* abort_flag = &ctl->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = kx::cluster_ctarank();
+    const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    const int m_tiles = (M + 2 * BM - 1) / (2 * BM);
+    const int last = ch.n_layers - 1;
+    // global tile t -> layer l, m-tile, n-tile (row-block-major inside a layer)
+    auto decode = [&](int t, int& l, int& mt, int& nt) {
+        l = 0;
+        while (l < last && t >= ch.L[l + 1].tile0) l++;
+        const int u = t - ch.L[l].tile0;
+        mt = u / ch.L[l].n_tiles_n;
+        nt = u - mt * ch.L[l].n_tiles_n;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            kx::mbar_init(&ctl->full[s], 1);
+            kx::mbar_init(&ctl->empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            kx::mbar_init(&ctl->acc_full[b], 1);
+            kx::mbar_init(&ctl->acc_empty[b], 2 * C::EPI_WARPS);
+        }
+        kx::mbar_init(&ctl->accf, 1);
+        ctl->abort = 0;
+        kx::fence_mbar_init();
+        kx::fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        kx::tmem_alloc_pair(&ctl->tmem, C::TMEM_COLS);
+        kx::tmem_relinquish_pair();
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();
+    kx::tc_fence_after();
+    const uint32_t tmem = ctl->tmem;
+    kx::griddep_wait();  // launched as a dependent of the quantiser of the chain's input
+    kx::griddep_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const CUtensorMap* mA[KX_I8C_MAX] = {&tmA0, &tmA1, &tmA2, &tmA3};
+            const CUtensorMap* mB[KX_I8C_MAX] = {&tmB0, &tmB1, &tmB2, &tmB3};
+            for (int l = 0; l < ch.n_layers; l++) {
+                kx::tma_prefetch_desc(mA[l]);
+                kx::tma_prefetch_desc(mB[l]);
+            }
+            int it = 0;
+            for (int t = cluster; t < ch.total_tiles && !*abort_flag; t += n_clusters) {
+                int l, mt, nt;
+                decode(t, l, mt, nt);
+                const int rg = mt * 2 + static_cast<int>(rank);
+                if (l > 0 && rg * BM < M &&
+                    !wait_ready(ch.L[l - 1].ready + rg, static_cast<uint32_t>(ch.L[l - 1].n_tiles_n), abort_flag, status))
+                    break;
+                const int arow = mt * 2 * BM + static_cast<int>(rank) * BM, brow = nt * BN + static_cast<int>(rank) * (BN / 2);
+                const int nk = (ch.L[l].k + C::BK - 1) / C::BK;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, status)) break;
+                    if (rank == 0) kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * (C::A_BYTES + C::B_BYTES));
+                    const uint32_t full0 = kx::mapa(kx::smem_u32(&ctl->full[s]), 0);
+                    kx::tma_load_2d_pair(sA + s * C::A_BYTES, mA[l], kb * C::BK, arow, full0);
+                    kx::tma_load_2d_pair(sB + s * C::B_BYTES, mB[l], kb * C::BK, brow, full0);
+                }
+            }
+            if (*abort_flag && rank == 0)
+                for (int i = it > STAGES ? it - STAGES : 0; i < it; i++) drain_wait(&ctl->full[i % STAGES], (i / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = kx::idesc_i8(2 * BM, BN);
+            int it = 0, j = 0;
+            for (int t = cluster; t < ch.total_tiles && !*abort_flag; t += n_clusters, j++) {
+                int l, mt, nt;
+                decode(t, l, mt, nt);
+                const int b = j & 1;
+                if (!kx::mbar_wait(&ctl->acc_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, status)) break;
+                kx::tc_fence_after();
+                const uint32_t d = tmem + b * BN;
+                const int nk = (ch.L[l].k + C::BK - 1) / C::BK;
+                bool ok = true;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!kx::mbar_wait(&ctl->full[s], (it / STAGES) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    kx::tc_fence_after();
+                    const uint32_t a0 = kx::smem_u32(sA + s * C::A_BYTES), b0 = kx::smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 32; kk++)
+                        kx::mma_i8_pair(d, kx::desc_sw128_kmajor(a0 + kk * 32), kx::desc_sw128_kmajor(b0 + kk * 32), idesc,
+                                        (kb | kk) != 0);
+                    const uint32_t e = kx::smem_u32(&ctl->empty[s]);
+                    kx::mma_commit_pair(e);
+                    kx::mma_commit_pair(kx::mapa(e, 1));
+                }
+                if (!ok) break;
+                const uint32_t f = kx::smem_u32(&ctl->acc_full[b]);
+                kx::mma_commit_pair(f);
+                kx::mma_commit_pair(kx::mapa(f, 1));
+            }
+            kx::mma_commit_pair(kx::smem_u32(&ctl->accf));
+            drain_wait(&ctl->accf, 0);
+        }
+        __syncwarp();
+    } else {
+        const int ew = warp - 2;
+        const int q = warp & 3;
+        const int c_lo = (ew >> 2) * (BN / 4);
+        float* stg = reinterpret_cast<float*>(sE + ew * 2048);
+        const int row_off = static_cast<int>(rank) * BM + q * 32;
+        const uint32_t acc_empty0 = kx::mapa(kx::smem_u32(&ctl->acc_empty[0]), 0);
+        int j = 0;
+        for (int t = cluster; t < ch.total_tiles; t += n_clusters, j++) {
+            int l, mt, nt;
+            decode(t, l, mt, nt);
+            const I8CLayer& L = ch.L[l];
+            const int b = j & 1;
+            const bool full_ok = __all_sync(0xffffffffu, kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status));
+            // the dequantisation factors after the accumulator: a layer's row scales are written by the previous one
+            EpiPre f{};
+            {
+                const int r0 = mt * 2 * BM + row_off;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int gr = r0 + 16 * (i >> 1) + 8 * (i & 1) + (lane >> 2);
+                    f.sx[i] = gr < M ? __ldcg(L.sx + gr) : 0.0f;
+                }
+                const int c = nt * BN + c_lo + 2 * lane;
+                f.sc.x = c < L.n ? __ldg(L.scale + c) : 0.0f;
+                f.sc.y = c + 1 < L.n ? __ldg(L.scale + c + 1) : 0.0f;
+                f.bi.x = L.bias && c < L.n ? __ldg(L.bias + c) : 0.0f;
+                f.bi.y = L.bias && c + 1 < L.n ? __ldg(L.bias + c + 1) : 0.0f;
+            }
+            const uint32_t tb = tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16);
+            if (l == last) {  // fp32 output; no barriers from here on (the last layer's tiles come last)
+                if (!full_ok) break;
+                kx::tc_fence_after();
+                epi_tile_i8<BN, false, ACTL>(tb, mt * 2 * BM + row_off, nt * BN, c_lo, stg, lane, f, L.y, nullptr, L.n, M, L.n,
+                                             L.act, L.alpha);
+            } else {  // the quantised-output epilogue of the QOUT kernel, then the tile counts as ready
+                const int r0 = mt * 2 * BM + row_off;
+                const int rg = mt * 2 + static_cast<int>(rank);
+                const bool live = rg * BM < M;
+                bool ok = full_ok;
+                if (ok) {
+                    kx::tc_fence_after();
+                    float4* cf = reinterpret_cast<float4*>(stg);
+                    __syncwarp();
+                    cf[lane] = make_float4(f.sc.x, f.sc.y, f.bi.x, f.bi.y);
+                    __syncwarp();
+                    uint32_t mx[4] = {0u, 0u, 0u, 0u};
+                    q_pass1<ACTH>(tb, c_lo, cf, lane, f, L.act, L.alpha, mx);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        mx[i] = max(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+                        mx[i] = max(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+                    }
+                    if ((lane & 3) == 0)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int gr = r0 + 16 * (i >> 1) + (lane >> 2) + 8 * (i & 1);
+                            if (gr < M) atomicMax(L.qo.rowmax + gr, mx[i]);
+                        }
+                    __threadfence();
+                }
+                kx::named_bar(1, C::EPI_WARPS * 32);
+                if (ok && live && ew == 0 && lane == 0) atomicAdd(L.qo.cnt + rg, 1u);
+                if (ok && live) {
+                    if (lane == 0) ok = q_wait_count(L.qo.cnt + rg, static_cast<uint32_t>(L.n_tiles_n), abort_flag, status);
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                }
+                if (ok) {
+                    const int gr = r0 + lane;
+                    const uint32_t m = gr < M ? kx::ld_relaxed_gpu(L.qo.rowmax + gr) : 0u;
+                    const bool nan_row = m >= 0x7F800000u;
+                    float sxv = 1.0f, inv = 1.0f;
+                    if (nan_row) {
+                        sxv = __uint_as_float(0x7FC00000u);
+                    } else if (m != 0u) {
+                        sxv = __fdiv_rn(__uint_as_float(m), 127.0f);
+                        inv = __fdiv_rn(1.0f, sxv);
+                    }
+                    if (nt == 0 && c_lo == 0 && gr < M) L.qo.sx[gr] = sxv;
+                    q_pass2(tb, c_lo, lane, inv, nan_row, gr, nt * BN + c_lo, L.qo, M, L.n);
+                    fence_proxy_async_global();  // the next layer reads these rows with TMA (the async proxy)
+                    __threadfence();
+                }
+                const bool stop = kx::named_bar_or(1, C::EPI_WARPS * 32, !ok || *abort_flag);
+                if (!stop && live && ew == 0 && lane == 0) atomicAdd(L.ready + rg, 1u);
+                if (stop) break;
+            }
+            kx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) kx::mbar_arrive_remote(acc_empty0 + b * static_cast<uint32_t>(sizeof(uint64_t)));
+        }
+    }
+    kx::tc_fence_before();
+    kx::cluster_sync();
     if (warp == 1) {
         kx::tc_fence_after();
         kx::tmem_dealloc_pair(tmem, C::TMEM_COLS);
@@ -2496,6 +2755,78 @@ int kx_gemm_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (n <= 128) return dispatch_i8<128>(xq, ldq, sx, wq, ldw, scale, bias, y, ldy, m, n, k, act, alpha, status, st);
     return dispatch_i8<256>(xq, ldq, sx, wq, ldw, scale, bias, y, ldy, m, n, k, act, alpha, status, st);
+}
+
+int kx_i8_chain(int n_layers, int m, const int8_t* const* a, const int* lda, const float* const* sx, const int8_t* const* wq,
+                const int* ldw, const float* const* scale, const float* const* bias, const int* k, const int* n, const int* act,
+                const float* alpha, float* const* sx_out, uint32_t* ctl, float* y, int* status, void* stream) {
+    if (m <= 0) return 0;
+    if (n_layers < 2 || n_layers > KX_I8C_MAX || ctl == nullptr || y == nullptr) return -1;
+    using C = I8PairCfg<6>;
+    const int rgs = (m + BM - 1) / BM;
+    I8Chain ch{};
+    ch.n_layers = n_layers;
+    CUtensorMap ta[KX_I8C_MAX], tb[KX_I8C_MAX];
+    std::memset(ta, 0, sizeof ta);
+    std::memset(tb, 0, sizeof tb);
+    const int m_tiles = (m + 2 * BM - 1) / (2 * BM);
+    int tiles = 0, lcm_n = 1;
+    for (int l = 0; l < n_layers; l++) {
+        if (k[l] <= 0 || n[l] <= 128 || k[l] > lda[l] || k[l] > ldw[l] || (lda[l] & 15) || (ldw[l] & 15) ||
+            (l > 0 && k[l] != n[l - 1]) || (reinterpret_cast<uintptr_t>(a[l]) & 15))
+            return -1;
+        if (make_map_2d(&ta[l], CU_TENSOR_MAP_DATA_TYPE_UINT8, a[l], static_cast<uint64_t>(lda[l]), static_cast<uint64_t>(m),
+                        static_cast<uint64_t>(lda[l]), C::BK, BM) != 0 ||
+            make_map_2d(&tb[l], CU_TENSOR_MAP_DATA_TYPE_UINT8, wq[l], static_cast<uint64_t>(ldw[l]), static_cast<uint64_t>(n[l]),
+                        static_cast<uint64_t>(ldw[l]), C::BK, C::BN / 2) != 0)
+            return -1;
+        I8CLayer& L = ch.L[l];
+        L.sx = sx[l];
+        L.scale = scale[l];
+        L.bias = bias[l];
+        L.n = n[l];
+        L.k = k[l];
+        L.act = act[l];
+        L.alpha = alpha[l];
+        L.n_tiles_n = (n[l] + C::BN - 1) / C::BN;
+        L.tile0 = tiles;
+        tiles += m_tiles * L.n_tiles_n;
+        if (l + 1 < n_layers) {  // the next layer's int8 rows, row scales and this layer's control words
+            uint32_t* w = ctl + static_cast<size_t>(l) * (m + 2 * rgs);
+            L.qo = QOut{const_cast<int8_t*>(a[l + 1]), sx_out[l], w, w + m, nullptr, lda[l + 1], 0};
+            L.ready = w + m + rgs;
+            if (lda[l + 1] < n[l]) return -1;
+            int g = lcm_n, h = L.n_tiles_n;  // clusters: a multiple of every hidden layer's tiles per row group
+            while (h) {
+                const int r = g % h;
+                g = h;
+                h = r;
+            }
+            lcm_n = lcm_n / g * L.n_tiles_n;
+        } else {
+            L.y = y;
+        }
+    }
+    ch.total_tiles = tiles;
+    const int ah = act_class(act[0]), al = act_class(act[n_layers - 1]);
+    for (int l = 1; l + 1 < n_layers; l++)
+        if (act_class(act[l]) != ah) return -1;  // hidden layers share one activation class (compiled in)
+    auto pick = [&](auto kern) -> int {
+        if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
+        int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
+        if (clusters <= 0) clusters = sm_count() / 2;
+        if (lcm_n > clusters) return -1;
+        clusters = clusters / lcm_n * lcm_n;
+        if (clusters > tiles) clusters = tiles;
+        return kx::launch_pdl(kern, dim3(2 * clusters), dim3(C::THREADS), C::SMEM, static_cast<cudaStream_t>(stream), ta[0],
+                              ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], ch, m, status);
+    };
+    if (ah == 1 && al == -1) return pick(k_i8_chain<6, 1, -1>);
+    if (ah == 1 && al == 1) return pick(k_i8_chain<6, 1, 1>);
+    if (ah == 0 && al == -1) return pick(k_i8_chain<6, 0, -1>);
+    if (ah == 0 && al == 0) return pick(k_i8_chain<6, 0, 0>);
+    if (ah == -1 && al == -1) return pick(k_i8_chain<6, -1, -1>);
+    return pick(k_i8_chain<6, ACT_GENERIC, ACT_GENERIC>);
 }
 
 int kx_gemm_i8_q(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale, const float* bias,

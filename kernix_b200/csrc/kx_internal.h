@@ -62,6 +62,8 @@ typedef struct {
     int shard_c0, shard_n;  /* sharded LINEAR: this rank keeps output columns [shard_c0, shard_c0 + shard_n); 0 = whole */
     int fuse_add, fuse_res; /* fp32 LINEAR / ATTENTION whose output only feeds the next step, an elementwise ADD: the
                              * GEMM writes that ADD's output, adding value fuse_res (the ADD's other operand) */
+    int i8c_n, i8c_in;      /* int8 LINEAR chains run as one launch (kx_i8_chain): i8c_n = its length on the first
+                             * step (0 elsewhere); i8c_in = 1 on every step of such a chain */
     int mlp_n, mlp_layers;  /* first step of a fused small-MLP chain: mlp_layers fp32 LINEAR steps (+ a SOFTMAX when
                              * mlp_n > mlp_layers) run as one kx_mlp_chain launch for small batches; 0 = none */
     int qout, qin, qpar;    /* int8 LINEAR chains: qout = the GEMM writes the next int8 step's quantised input (its

@@ -368,3 +368,38 @@ def test_fused_mlp_chain(Model, model_dir, monkeypatch, dims, acts, softmax, row
     big = np.concatenate([x, x, x])  # above the chain's row limit: the GEMMs
     got_big = Model(p)(big)
     assert rel_err(got_big, np.concatenate([want, want, want])) <= 1e-5
+
+
+@pytest.mark.parametrize("dims,acts,rows", [
+    ((1024, 4096, 4096, 1024), ("gelu", "gelu"), 4096),  # configuration c2's shapes
+    ((1024, 4096, 4096, 1024), ("gelu", "gelu"), 77),
+    ((200, 1000, 520, 300), ("relu", "relu"), 333),
+    ((256, 512, 512, 384, 264), ("silu", "silu", "silu"), 129),
+    ((512, 2304, 640), ("none",), 1)])
+def test_int8_chain_one_launch_equals_layer_by_layer(Model, model_dir, monkeypatch, dims, acts, rows):
+    """A chain of int8 LINEAR steps runs as one persistent launch (kx_i8_chain: each hidden layer quantises its own
+    output rows for the next, whose tiles start once those rows are stored): bit for bit the rows of running the
+    layers one launch at a time ($KERNIX_NO_I8_CHAIN=1), and within the int8 bound of the oracle."""
+    from kernix_b200 import knx_writer
+    rng = np.random.default_rng(sum(dims) + rows)
+    p = f"{model_dir}/i8chain_{'_'.join(map(str, dims))}.knx"
+    s = knx_writer.Sequential(int8=True)
+    for i in range(len(dims) - 1):
+        s.linear((rng.standard_normal((dims[i], dims[i + 1])) * 0.03).astype(F32), rng.uniform(-0.05, 0.05, dims[i + 1]).astype(F32))
+        if i < len(dims) - 2 and acts[i] != "none":
+            s.act(acts[i])
+    s.write(p)
+    x = rng.standard_normal((rows, dims[0])).astype(F32)
+    if rows > 3:
+        x[1] = 0.0
+        x[2, 7] = np.nan
+    monkeypatch.setenv("KERNIX_PIPELINE", "1")
+    monkeypatch.delenv("KERNIX_NO_I8_CHAIN", raising=False)
+    chain = Model(p)(x)
+    monkeypatch.setenv("KERNIX_NO_I8_CHAIN", "1")
+    steps = Model(p)(x)
+    assert np.array_equal(np.isnan(chain), np.isnan(steps))
+    assert np.array_equal(np.nan_to_num(chain).view(np.uint32), np.nan_to_num(steps).view(np.uint32))
+    ok = ~np.isnan(chain).any(axis=1)
+    ids = np.nonzero(ok)[0][:64]
+    assert rel_err(chain[ids], ko.forward(ko.load(p), x[ids])) <= 1e-4
