@@ -117,6 +117,20 @@ KERNIX_API int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const flo
 KERNIX_API int kx_gemm_f32_res(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
                     int ldy, int m, int n, int k, int act, float alpha, const float* res, int ldr, int* status, void* stream);
 
+/* kx_gemm_f32 for at most 128 rows with the reduction split into `splits` (<= KX_SPLITK_MAX) ranges of K (multiples
+ * of 256) run by separate CTAs -- for layers whose few output tiles would leave most SMs idle (a column-sharded wide
+ * layer at small batch) -- then y = act(P[0] + ... + P[splits-1] + bias) added in range order (kx_add_planes).
+ * part: splits x m x n floats of device scratch. x 16-byte aligned, ldx a multiple of 4. */
+#define KX_SPLITK_MAX 4
+KERNIX_API int kx_gemm_f32_split(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias,
+                                 float* y, int ldy, int m, int n, int k, int act, float alpha, int splits, float* part,
+                                 int* status, void* stream);
+/* the split count kx_gemm_f32_split should be given for an m x n x k layer: 1 (no split) unless m <= 128, k >= 2048 and
+ * the layer's output tiles fill fewer than half the SMs; at most KX_SPLITK_MAX, ranges of at least 1024 */
+KERNIX_API int kx_gemm_f32_splits(int m, int n, int k);
+KERNIX_API int kx_add_planes(const float* part, int planes, int m, int n, const float* bias, int act, float alpha, float* y,
+                             int ldy, void* stream);
+
 /* Load-time transpose + split of a float weight (k x n, in x out) into n x ldw K-major planes
  * hi = tf32(w), lo = w - hi (exact), zero padded. */
 KERNIX_API int kx_prep_f32_weight(const float* w_kn, int k, int n, float* w_hi, float* w_lo, int ldw, void* stream);

@@ -59,6 +59,7 @@ struct kx_model_impl {
     int* status;          /* device status word of bounded waits */
     float* skinny_part;   /* partial sums of the skinny dense path (LINEAR steps of <= KX_SKINNY_MAX_ROWS rows) */
     size_t skinny_floats;
+    float* split_part;    /* partial-sum planes of split-K dense steps (kx_gemm_f32_split), NULL if none splits */
     int* status_h;        /* pinned host copy */
     size_t scratch_per_row_max;
     int no_qchain;        /* 1 while tracing: every int8 step writes its fp32 output (int8 chains off) */
@@ -626,13 +627,16 @@ static int step_run(kernix_model* m, int i, int B, int fused) {
                               s->out, s->in, s->act, s->alpha, im->status, st);
         }
         const int skinny = rin <= KX_SKINNY_MAX_ROWS && s->w.d_raw != NULL && im->skinny_part != NULL;
+        const int ncols = s->shard_n > 0 ? s->shard_n : s->out;
+        /* 17..128 rows of a layer with few output tiles: K split over the idle SMs, planes added in a fixed order */
+        const int splits = !skinny && !res && im->split_part != NULL ? kx_gemm_f32_splits((int)rin, ncols, s->in) : 1;
         if (s->shard_n > 0) { /* this rank's columns, all-gather across ranks, re-interleave into full rows */
             float* yl = (float*)align_ptr(im->scratch);
             float* yg = (float*)align_ptr(yl + (size_t)rin * s->shard_n);
             if ((skinny ? kx_gemm_f32_skinny(a, s->in, s->w.d_raw, s->d_bias, yl, s->shard_n, (int)rin, s->shard_n, s->in, s->act,
                                              s->alpha, im->skinny_part, im->skinny_floats, st)
-                        : kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, yl, s->shard_n, (int)rin, s->shard_n,
-                                      s->in, s->act, s->alpha, im->status, st)) != 0)
+                        : kx_gemm_f32_split(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, yl, s->shard_n, (int)rin,
+                                            s->shard_n, s->in, s->act, s->alpha, splits, im->split_part, im->status, st)) != 0)
                 return -1;
             if (im->gather(im->gather_ctx, yl, yg, (size_t)rin * s->shard_n, st) != 0) {
                 fprintf(stderr, "forward: the all-gather of step %d failed\n", i);
@@ -646,6 +650,9 @@ static int step_run(kernix_model* m, int i, int B, int fused) {
         if (res)
             return kx_gemm_f32_res(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in,
                                    s->act, s->alpha, res, s->out, im->status, st);
+        if (splits > 1)
+            return kx_gemm_f32_split(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in,
+                                     s->act, s->alpha, splits, im->split_part, im->status, st);
         return kx_gemm_f32(a, s->in, s->w.d_hi, s->w.d_lo, s->w.ldw, s->d_bias, y, s->out, (int)rin, s->out, s->in, s->act,
                            s->alpha, im->status, st);
     case KERNIX_OP_ACT:
@@ -1179,6 +1186,17 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
         if (mx > 0 && cudaMalloc((void**)&im->skinny_part, mx * sizeof(float)) != cudaSuccess) why = "cannot allocate device memory";
         im->skinny_floats = mx;
     }
+    const char* no_split = getenv("KERNIX_NO_SPLITK"); /* 1: dense steps never split K (tests compare the two) */
+    if (why == NULL && !(no_split && *no_split && *no_split != '0')) { /* split-K planes: splits x 128 rows x columns, the largest step */
+        size_t mx = 0;
+        for (int i = 0; i < g->n_steps; i++) {
+            const kx_step* s = &g->steps[i];
+            if (s->kind != KERNIX_OP_LINEAR || s->w.int8 || s->fuse_add) continue;
+            const int n = s->shard_n > 0 ? s->shard_n : s->out, sp = kx_gemm_f32_splits(128, n, s->in);
+            if (sp > 1 && (size_t)sp * 128 * n > mx) mx = (size_t)sp * 128 * n;
+        }
+        if (mx > 0 && cudaMalloc((void**)&im->split_part, mx * sizeof(float)) != cudaSuccess) why = "cannot allocate device memory";
+    }
     if (why == NULL) { /* fused small-MLP chains: partial sums for up to KX_MLP_MAX_ROWS rows, the largest chain */
         size_t mx = 0;
         for (int i = 0; i < g->n_steps; i++) {
@@ -1306,6 +1324,7 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
             for (int i = 0; i < im->g->n_steps; i++) step_dev_free(&im->g->steps[i]);
         if (im->status_h) cudaFreeHost(im->status_h);
         cudaFree(im->skinny_part);
+        cudaFree(im->split_part);
         cudaFree(im->mlp_scratch);
         cudaFree(im->mlp_bar);
         for (int i = 0; i < KX_PIPE_MAX; i++) {

@@ -1321,11 +1321,19 @@ __global__ void __launch_bounds__(F32_THREADS, 1)
 k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUtensorMap tmBhi,
               const __grid_constant__ CUtensorMap tmBlo, const float* __restrict__ bias, float* __restrict__ y, int ldy,
               int M, int N, int K, int act, float alpha, int* status, const ConvGeom cv, const float* __restrict__ res,
-              int ldr) {
+              int ldr, int ksl) {
     using C = F32Cfg<BN, STAGES, DRAIN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + STAGES * C::STAGE_BYTES);
+    // dense split-K (ksl > 0): CTA z of the grid's third dimension takes K range [z ksl, (z + 1) ksl) (ksl a multiple of
+    // 256, whole drain chunks) and writes its raw sums into plane z of y (M x ldy each); the caller adds the planes
+    const int kz = !CONV && ksl > 0 ? static_cast<int>(blockIdx.z) * ksl : 0;
+    if (!CONV && ksl > 0) {
+        A += kz;
+        K = min(K - kz, ksl);
+        y += static_cast<size_t>(blockIdx.z) * M * ldy;
+    }
     volatile int* abort_flag = &ctl->abort;
     auto sAhi = [&](int s) { return smem + s * C::STAGE_BYTES; };
     auto sAlo = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES; };
@@ -1375,8 +1383,8 @@ k_gemm_tf32x3(const float* __restrict__ A, int lda, const __grid_constant__ CUte
                 const int s = kb % STAGES;
                 if (!kx::mbar_wait(&ctl->empty[s], ((kb / STAGES) & 1) ^ 1, abort_flag, status)) break;
                 kx::mbar_arrive_expect_tx(&ctl->full[s], 2 * C::B_BYTES);
-                kx::tma_load_2d(sBhi(s), &tmBhi, kb * C::BK, brow0 + n0, &ctl->full[s]);
-                kx::tma_load_2d(sBlo(s), &tmBlo, kb * C::BK, brow0 + n0, &ctl->full[s]);
+                kx::tma_load_2d(sBhi(s), &tmBhi, kz + kb * C::BK, brow0 + n0, &ctl->full[s]);
+                kx::tma_load_2d(sBlo(s), &tmBlo, kz + kb * C::BK, brow0 + n0, &ctl->full[s]);
                 issued = kb + 1;
             }
             if (*abort_flag)
@@ -2367,7 +2375,7 @@ int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq,
 template <int BN, bool CONV, int ACTC, bool DRAIN>
 int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int ldw, int wrows, const float* bias, float* y,
                int ldy, int m, int n, int k, int act, float alpha, int* status, cudaStream_t st, const ConvGeom& cv,
-               int groups, const float* res, int ldr) {
+               int groups, const float* res, int ldr, int splits = 1, int ksl = 0) {
     constexpr int STAGES = BN == 256 ? 2 : 3;
     using C = F32Cfg<BN, STAGES, DRAIN>;
     CUtensorMap th, tl;
@@ -2378,8 +2386,8 @@ int launch_f32(const float* x, int ldx, const float* whi, const float* wlo, int 
         return -1;
     auto kern = k_gemm_tf32x3<BN, STAGES, CONV, ACTC, DRAIN>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
-    dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, groups);
-    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr);
+    dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM, CONV ? groups : splits);
+    kern<<<grid, F32_THREADS, C::SMEM, st>>>(x, ldx, th, tl, bias, y, ldy, m, n, k, act, alpha, status, cv, res, ldr, ksl);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -2877,6 +2885,41 @@ int kx_gemm_f32(const float* x, int ldx, const float* w_hi, const float* w_lo, i
     const ConvGeom cv{};
     if (n <= 128) return dispatch_f32<128, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
     return dispatch_f32<256, false>(x, ldx, w_hi, w_lo, ldw, n, bias, y, ldy, m, n, k, act, alpha, status, st, cv, 1);
+}
+
+int kx_gemm_f32_splits(int m, int n, int k) {
+    if (m <= 0 || m > BM || n <= 0 || k < 2048) return 1;
+    const int bn = k > DRAIN_MIN_K || n <= 128 ? 128 : 256;
+    const int tiles = (n + bn - 1) / bn;
+    int s = sm_count() / tiles;
+    if (s > KX_SPLITK_MAX) s = KX_SPLITK_MAX;
+    if (s > k / 1024) s = k / 1024;
+    return s < 2 ? 1 : s;
+}
+
+int kx_gemm_f32_split(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
+                      int ldy, int m, int n, int k, int act, float alpha, int splits, float* part, int* status, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldx || k > ldw || (ldw & 3) || m > BM || splits < 1 || splits > KX_SPLITK_MAX || part == nullptr ||
+        (reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 3))
+        return -1;
+    if (splits == 1) return kx_gemm_f32(x, ldx, w_hi, w_lo, ldw, bias, y, ldy, m, n, k, act, alpha, status, stream);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const ConvGeom cv{};
+    const int ksl = ((k + splits - 1) / splits + 255) / 256 * 256;  // whole drain chunks per range
+    const int used = (k + ksl - 1) / ksl;                           // ranges that hold any K
+    int r;
+    if (k > DRAIN_MIN_K)
+        r = launch_f32<128, false, -1, true>(x, ldx, w_hi, w_lo, ldw, n, nullptr, part, n, m, n, k, -1, 0.0f, status, st, cv, 1,
+                                             nullptr, 0, used, ksl);
+    else if (n > 128)
+        r = launch_f32<256, false, -1, false>(x, ldx, w_hi, w_lo, ldw, n, nullptr, part, n, m, n, k, -1, 0.0f, status, st, cv, 1,
+                                              nullptr, 0, used, ksl);
+    else
+        r = launch_f32<128, false, -1, false>(x, ldx, w_hi, w_lo, ldw, n, nullptr, part, n, m, n, k, -1, 0.0f, status, st, cv, 1,
+                                              nullptr, 0, used, ksl);
+    if (r != 0) return r;
+    return kx_add_planes(part, used, m, n, bias, act, alpha, y, ldy, stream);
 }
 
 int kx_gemm_f32_res(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,

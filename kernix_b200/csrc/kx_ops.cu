@@ -44,6 +44,26 @@ __device__ __forceinline__ uint32_t warp_umax(uint32_t v) {
 // ---------------------------------------------------------------------------------- int8 quantise
 // One 128-thread block per row. max|x| is reduced on the IEEE bit patterns of |x| (non-negative floats order
 // like their bits; NaN > inf > finite), so a NaN anywhere makes the row's max NaN as in the reference.
+// y = act(P[0] + P[1] + ... + bias) over m x n, planes P[z] of m x n floats added in plane order (split-K partial sums)
+__global__ void k_add_planes(const float* __restrict__ part, int planes, int m, int n, const float* __restrict__ bias, int act,
+                             float alpha, float* __restrict__ y, int ldy) {
+    const long total = static_cast<long>(m) * n, plane = total;
+    for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < total; i += static_cast<long>(gridDim.x) * blockDim.x) {
+        float v[KX_SPLITK_MAX];
+#pragma unroll
+        for (int z = 0; z < KX_SPLITK_MAX; z++)
+            if (z < planes) v[z] = __ldcg(part + z * plane + i);
+        float s = v[0];
+#pragma unroll
+        for (int z = 1; z < KX_SPLITK_MAX; z++)
+            if (z < planes) s = __fadd_rn(s, v[z]);
+        const long r = i / n;
+        const int c = static_cast<int>(i - r * n);
+        if (bias) s = __fadd_rn(s, __ldg(bias + c));
+        y[r * ldy + c] = kx::act_apply(act, s, alpha);
+    }
+}
+
 constexpr int QT = 128;
 constexpr int QV = 8;  // float4 per thread kept in registers (rows up to 4096 columns in one read)
 
@@ -1044,6 +1064,15 @@ int kx_unshard_cols(const float* src, int world, long rows, int slice, float* y,
     return launch_ok();
 }
 
+
+int kx_add_planes(const float* part, int planes, int m, int n, const float* bias, int act, float alpha, float* y, int ldy,
+                  void* stream) {
+    const long total = static_cast<long>(m) * n;
+    if (total <= 0) return 0;
+    if (planes < 1 || planes > KX_SPLITK_MAX || part == nullptr || y == nullptr) return -1;
+    k_add_planes<<<grid_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(part, planes, m, n, bias, act, alpha, y, ldy);
+    return launch_ok();
+}
 
 int kx_quant_rows_z(const float* x, int ldx, int rows, int k, int8_t* xq, int ldq, float* sx, uint32_t* zero, int zero_words,
                     void* stream) {

@@ -57,6 +57,11 @@ def lib():
         L.kernix_model_load_sharded_nccl.restype = vp
         L.kernix_nccl_unique_id.argtypes = [ctypes.c_char_p]
         L.kernix_nccl_unique_id.restype = ctypes.c_int
+        # device pointers are 64-bit: without these declarations ctypes would pass them as C ints
+        L.kernix_model_forward_device.argtypes = [vp, vp, ctypes.c_int, vp, vp]
+        L.kernix_model_forward_device.restype = ctypes.c_int
+        L.kernix_model_check.argtypes = [vp]
+        L.kernix_model_check.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -227,6 +227,47 @@ def test_gemm_f32_3xtf32(kx, m, k, n, act):
     assert rel_err(got, ref) <= 1e-5
 
 
+@pytest.mark.parametrize("m,k,n,act,splits", [(64, 16384, 4096, 0, 4), (64, 16384, 8192, -1, 2), (128, 8192, 1024, 0, 4),
+                                              (17, 5000, 520, 1, 4), (100, 2048, 300, -1, 2), (64, 3000, 260, 0, 3),
+                                              (50, 2100, 130, 0, 4), (1, 4096, 64, -1, 4)])
+def test_gemm_f32_split_k(kx, m, k, n, act, splits):
+    """kx_gemm_f32_split: the reduction cut into `splits` ranges of whole 256-column chunks (ragged last range; fewer
+    ranges than asked when K is short), each run by its own CTAs into a partial-sum plane, the planes then added in
+    range order with bias and activation: within the same 1e-5 bound of float64 as the unsplit kernel, and the same
+    bits on a second call (a fixed order of additions)."""
+    rng = np.random.default_rng(m + 3 * k + n + splits)
+    x = rng.standard_normal((m, k)).astype(F32)
+    w = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(F32)
+    b = rng.standard_normal(n).astype(F32)
+    hi, lo, ldw = _prep_f32(kx, w)
+    part = torch.full((splits * m * n,), float("nan"), dtype=torch.float32, device="cuda")
+    st = status()
+    dx, db = dev(x), dev(b)
+    outs = []
+    for _ in range(2):
+        y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        kx.call("kx_gemm_f32_split", dx.data_ptr(), k, hi.data_ptr(), lo.data_ptr(), ldw, db.data_ptr(), y.data_ptr(), n, m,
+                n, k, act, 0.0, splits, part.data_ptr(), st.data_ptr(), sp())
+        outs.append(host(y))
+    check_status(st)
+    ref = ko.act((x.astype(np.float64) @ w.astype(np.float64) + b).astype(F32), act) if act == 1 else \
+        x.astype(np.float64) @ w.astype(np.float64) + b
+    if act == 0:
+        ref = np.maximum(ref, 0)
+    assert rel_err(outs[0], ref) <= 1e-5
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
+def test_gemm_f32_split_count(kx):
+    """The split policy: only <= 128 rows and K >= 2048, only when the output tiles leave SMs idle, at most 4 ranges
+    of at least 1024."""
+    f = kx.lib().kx_gemm_f32_splits
+    assert torch.cuda.get_device_properties(0).multi_processor_count == 148
+    assert f(200, 4096, 16384) == 1 and f(64, 300, 1024) == 1 and f(64, 16384, 8192) == 1  # 128 tiles: no room
+    assert f(64, 4096, 16384) == 4 and f(64, 8192, 16384) == 2  # 32 and 64 tiles of 128 columns
+    assert f(1, 128, 2048) == 2 and f(128, 128, 3000) == 2  # ranges of at least 1024
+
+
 @pytest.mark.parametrize("m,k,n,act,inplace", [(100, 300, 200, 0, False), (300, 512, 512, -1, True), (4096, 512, 1536, 1, False),
                                                (700, 2500, 130, -1, False), (5000, 1000, 520, 0, True)])
 def test_gemm_f32_residual_is_gemm_then_add(kx, m, k, n, act, inplace):

@@ -370,6 +370,38 @@ def test_fused_mlp_chain(Model, model_dir, monkeypatch, dims, acts, softmax, row
     assert rel_err(got_big, np.concatenate([want, want, want])) <= 1e-5
 
 
+@pytest.mark.parametrize("dims,rows", [((4096, 8192, 8192, 4096), 64), ((4096, 8192, 8192, 4096), 128),
+                                       ((3000, 2600, 260), 40), ((4096, 8192, 8192, 4096), 17)])
+def test_split_k_dense_steps(Model, model_dir, monkeypatch, dims, rows):
+    """Wide fp32 layers at 17..128 rows split K over the SMs their few output tiles leave idle (kx_gemm_f32_split):
+    within the dense-MLP bound 1e-5 of the oracle and of the unsplit kernels ($KERNIX_NO_SPLITK=1), and the same bits
+    on a second call (partial sums added in a fixed order)."""
+    from kernix_b200 import knx_writer
+    rng = np.random.default_rng(sum(dims) + rows)
+    p = f"{model_dir}/wide_{'_'.join(map(str, dims))}.knx"
+    s = knx_writer.Sequential()
+    for i in range(len(dims) - 1):
+        s.linear((rng.standard_normal((dims[i], dims[i + 1])) * np.sqrt(2.0 / dims[i])).astype(F32),
+                 rng.uniform(-0.1, 0.1, dims[i + 1]).astype(F32))
+        if i < len(dims) - 2:
+            s.act("relu")
+    s.write(p)
+    x = rng.uniform(-1, 1, (rows, dims[0])).astype(F32)
+    ids = np.arange(0, rows, max(1, rows // 16))
+    want = ko.forward(ko.load(p), x[ids])
+    monkeypatch.setenv("KERNIX_PIPELINE", "1")
+    monkeypatch.delenv("KERNIX_NO_SPLITK", raising=False)
+    m = Model(p)
+    split = m(x)
+    assert np.array_equal(m(x), split)
+    m.close()
+    monkeypatch.setenv("KERNIX_NO_SPLITK", "1")
+    whole = Model(p)(x)
+    e_split, e_whole, e_pair = rel_err(split[ids], want), rel_err(whole[ids], want), rel_err(split, whole)
+    print(f"{dims} x {rows}: split-K {e_split:.2e}, unsplit {e_whole:.2e}, split vs unsplit {e_pair:.2e}")
+    assert e_split <= 1e-5 and e_whole <= 1e-5 and e_pair <= 1e-5
+
+
 @pytest.mark.parametrize("dims,acts,rows", [
     ((1024, 4096, 4096, 1024), ("gelu", "gelu"), 4096),  # configuration c2's shapes
     ((1024, 4096, 4096, 1024), ("gelu", "gelu"), 77),
