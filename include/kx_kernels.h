@@ -120,7 +120,7 @@ KERNIX_API int kx_gemm_f32_res(const float* x, int ldx, const float* w_hi, const
 /* kx_gemm_f32 for at most 128 rows with the reduction split into `splits` (<= KX_SPLITK_MAX) ranges of K (multiples
  * of 256) run by separate CTAs -- for layers whose few output tiles would leave most SMs idle (a column-sharded wide
  * layer at small batch) -- then y = act(P[0] + ... + P[splits-1] + bias) added in range order (kx_add_planes).
- * part: splits x m x n floats of device scratch. x 16-byte aligned, ldx a multiple of 4. */
+ * part: splits x m x n floats of device scratch. splits = 1 is kx_gemm_f32 (any m; part unused). */
 #define KX_SPLITK_MAX 4
 KERNIX_API int kx_gemm_f32_split(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias,
                                  float* y, int ldy, int m, int n, int k, int act, float alpha, int splits, float* part,

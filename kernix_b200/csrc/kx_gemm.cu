@@ -2899,11 +2899,10 @@ int kx_gemm_f32_splits(int m, int n, int k) {
 
 int kx_gemm_f32_split(const float* x, int ldx, const float* w_hi, const float* w_lo, int ldw, const float* bias, float* y,
                       int ldy, int m, int n, int k, int act, float alpha, int splits, float* part, int* status, void* stream) {
-    if (m <= 0 || n <= 0) return 0;
-    if (k <= 0 || k > ldx || k > ldw || (ldw & 3) || m > BM || splits < 1 || splits > KX_SPLITK_MAX || part == nullptr ||
-        (reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 3))
-        return -1;
     if (splits == 1) return kx_gemm_f32(x, ldx, w_hi, w_lo, ldw, bias, y, ldy, m, n, k, act, alpha, status, stream);
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldx || k > ldw || (ldw & 3) || m > BM || splits < 1 || splits > KX_SPLITK_MAX || part == nullptr)
+        return -1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const ConvGeom cv{};
     const int ksl = ((k + splits - 1) / splits + 255) / 256 * 256;  // whole drain chunks per range

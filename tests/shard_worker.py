@@ -28,16 +28,23 @@ def main():
     m_nccl = Model(path, shard=(rank, world, shard.share_nccl_id()))
     ys_nccl = m_nccl(x)
     ys_nccl2 = m_nccl(x[:5])  # a second call over the same communicator, a different row count
+    x3 = configs.inputs("c5", 300, seed=7)  # more than 128 rows: the CTA-pair tiles, no K split
+    ys_nccl3 = m_nccl(x3)
     m_nccl.close()
     ys_cb = Model(path, shard=(rank, world, shard.torch_allgather()))(x)
     y1 = Model(path)(x)
     err = float(np.abs(ys_nccl - y1).max() / np.abs(y1).max())
     err2 = float(np.abs(ys_nccl2 - y1[:5]).max() / np.abs(y1).max())
+    m1 = Model(path)
+    y3 = m1(x3)
+    m1.close()
+    err3 = float(np.abs(ys_nccl3 - y3).max() / np.abs(y3).max())
     same = np.array_equal(ys_nccl, ys_cb)
     dist.barrier()
     dist.destroy_process_group()
-    print(f"rank {rank}: max rel diff sharded (C NCCL) vs whole {err:.2e}, 5 rows {err2:.2e}, C NCCL == callback: {same}")
-    if err <= 1e-6 and err2 <= 1.5e-5 and same:
+    print(f"rank {rank}: max rel diff sharded (C NCCL) vs whole {err:.2e}, 5 rows {err2:.2e}, 300 rows {err3:.2e}, "
+          f"C NCCL == callback: {same}")
+    if err <= 1e-6 and err2 <= 1.5e-5 and err3 <= 1e-5 and same:
         print("SHARD_OK")
 
 
