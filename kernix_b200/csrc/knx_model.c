@@ -55,6 +55,8 @@ struct kx_model_impl {
     float** st;           /* device storage buffers as the running steps see them (a piece's rows) */
     float** st_base;      /* the same buffers from their first sample */
     float* xin;           /* device input rows */
+    float* yout;          /* when set, the model output value lives here (a device forward writes the caller's
+                           * buffer directly), else in its storage buffer */
     uint8_t* scratch;     /* per-step scratch: int8 activations, attention Q/K/V/context */
     int* status;          /* device status word of bounded waits */
     float* skinny_part;   /* partial sums of the skinny dense path (LINEAR steps of <= KX_SKINNY_MAX_ROWS rows) */
@@ -404,6 +406,7 @@ static int model_alloc(kernix_model* m, int rows) {
 
 /* device pointer of value v in the current chunk */
 static float* val_ptr(const struct kx_model_impl* im, int v) {
+    if (v == im->g->out_v && im->yout != NULL) return im->yout;
     const kx_val* val = &im->g->vals[v];
     return val->st < 0 ? im->xin : im->st[val->st];
 }
@@ -868,7 +871,8 @@ static void piece_view(struct kx_model_impl* im, float* xin_base, int a, size_t 
 }
 
 /* Enqueue the forward of device rows d_x into d_out (samples x out_dim) on im->stream, chunk by chunk. The model
- * input is never written (the plan keeps it read-only), so each chunk reads it in place. */
+ * input is never written (the plan keeps it read-only), so each chunk reads it in place. The step that produces the
+ * model output writes the caller's rows directly unless that output is a RESHAPE view (then it is copied out). */
 static int forward_enqueue_device(kernix_model* m, const float* x, int rows, float* out) {
     struct kx_model_impl* im = m->impl;
     const int samples = rows / m->seq_len;
@@ -876,16 +880,21 @@ static int forward_enqueue_device(kernix_model* m, const float* x, int rows, flo
     const int chunk = chunk_samples(m, samples);
     const int crow = chunk * m->seq_len;
     if (crow != m->batch && model_alloc(m, crow) != 0) return -1;
+    const kx_graph* g = im->g;
+    const int direct = g->out_v > 0 && g->steps[g->out_v - 1].kind != KERNIX_OP_RESHAPE && ((uintptr_t)out & 15) == 0;
     float* const xin_own = im->xin;
     for (int s0 = 0; s0 < samples; s0 += chunk) {
         const int n = samples - s0 < chunk ? samples - s0 : chunk;
+        float* yo = out + (size_t)s0 * m->out_dim;
         im->xin = (float*)(x + (size_t)s0 * m->seq_len * m->in_dim);
+        im->yout = direct ? yo : NULL;
         const int rc = chunk_run(m, n);
-        const float* yc = val_ptr(im, im->g->out_v); /* the input itself when the graph is only views of it */
+        const float* yc = val_ptr(im, g->out_v); /* the input itself when the graph is only views of it */
         im->xin = xin_own;
+        im->yout = NULL;
         if (rc != 0) return -1;
-        if (cudaMemcpyAsync(out + (size_t)s0 * m->out_dim, yc, (size_t)n * m->out_dim * sizeof(float),
-                            cudaMemcpyDeviceToDevice, im->stream) != cudaSuccess)
+        if (!direct && cudaMemcpyAsync(yo, yc, (size_t)n * m->out_dim * sizeof(float), cudaMemcpyDeviceToDevice,
+                                       im->stream) != cudaSuccess)
             return -1;
     }
     return 0;

@@ -30,6 +30,14 @@ __device__ __forceinline__ float rcp_approx(float d) {
 }
 __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 
+// max(m, |v|) on the bit patterns of non-negative floats (m: a previous result, 0 at first), NaN winning over every
+// number (its bits exceed +inf's): one float max with NaN propagation instead of an and and an integer max
+__device__ __forceinline__ uint32_t absmax_nan(uint32_t m, float v) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(__uint_as_float(m)), "f"(fabsf(v)));
+    return __float_as_uint(r);
+}
+
 // Packed f32x2 arithmetic (sm_100): each component rounded to nearest like the scalar operation. The code
 // generator may still contract a packed mul followed by a packed add into one fma (measured), so chains of
 // these are not bitwise equal to chains of scalar __fmul_rn / __fadd_rn; exact dequantisation stays scalar.

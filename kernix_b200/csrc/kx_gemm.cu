@@ -309,10 +309,9 @@ __device__ __forceinline__ void q_pass1(uint32_t tbase, int c_lo, const float4* 
         for (int k = 0; k < 4; k++)
 #pragma unroll
             for (int e = 0; e < 2; e++) {
-                const uint32_t bx = __float_as_uint(o[2 * k + e].x), by = __float_as_uint(o[2 * k + e].y);
-                mx[2 * h + e] = max(mx[2 * h + e], max(bx & 0x7FFFFFFFu, by & 0x7FFFFFFFu));
-                r[4 * k + 2 * e] = bx;
-                r[4 * k + 2 * e + 1] = by;
+                mx[2 * h + e] = kx::absmax_nan(kx::absmax_nan(mx[2 * h + e], o[2 * k + e].x), o[2 * k + e].y);
+                r[4 * k + 2 * e] = __float_as_uint(o[2 * k + e].x);
+                r[4 * k + 2 * e + 1] = __float_as_uint(o[2 * k + e].y);
             }
         kx::tmem_st16x256b_x4(taddr(i), r);
     };
@@ -331,11 +330,14 @@ __device__ __forceinline__ void q_pass1(uint32_t tbase, int c_lo, const float4* 
     kx::tmem_st_wait();
 }
 
-// one quantised byte of v (the quantiser's steps: rint(v * inv), clamp to +-127); inv is finite here
-__device__ __forceinline__ uint32_t q_byte(uint32_t vbits, float inv) {
-    const float t = __fadd_rn(__fmul_rn(__uint_as_float(vbits), inv), 12582912.0f);  // 1.5 * 2^23: rounds to an integer
-    const int qi = min(max(static_cast<int>(__float_as_uint(t)) - 0x4B400000, -127), 127);
-    return static_cast<uint32_t>(qi) & 0xFFu;
+// four quantised bytes of v[0..3] (the quantiser's steps: rint(v * inv), clamped to +-127), inv finite. t = v inv
+// rounded, plus 1.5 2^23, is the integer q = rint(v inv) in the last bits of 0x4B400000 + q, so q's byte is t's low
+// byte; |v inv| <= 127 (1 + 2^-22) since |v| <= the row's maximum, so the clamp never acts and is not applied
+__device__ __forceinline__ uint32_t q_word(const uint32_t* v, float inv) {
+    uint32_t t[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) t[e] = __float_as_uint(__fadd_rn(__fmul_rn(__uint_as_float(v[e]), inv), 12582912.0f));
+    return __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
 }
 
 // pass 2 of one warp: thread = row r0 + lane (TMEM lane quarter), columns c_lo .. c_lo + 63 of the tile; both
@@ -351,10 +353,7 @@ __device__ __forceinline__ void q_pass2(uint32_t tbase, int c_lo, int lane, floa
     for (int half = 0; half < 2; half++) {
         uint32_t w[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-            w[j] = nan_row ? 0u
-                           : q_byte(v[half][4 * j], inv) | (q_byte(v[half][4 * j + 1], inv) << 8) |
-                                 (q_byte(v[half][4 * j + 2], inv) << 16) | (q_byte(v[half][4 * j + 3], inv) << 24);
+        for (int j = 0; j < 8; j++) w[j] = nan_row ? 0u : q_word(&v[half][4 * j], inv);
         const int gc = gc0 + 32 * half;
         if (gc >= qo.ldq) continue;
         if (gc + 32 > N) {  // the last columns: bytes at N and beyond are the zero padding up to ldq
@@ -984,10 +983,14 @@ k_i8_chain(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUt
                     if (nt == 0 && c_lo == 0 && gr < M) L.qo.sx[gr] = sxv;
                     q_pass2(tb, c_lo, lane, inv, nan_row, gr, nt * BN + c_lo, L.qo, M, L.n);
                     fence_proxy_async_global();  // the next layer reads these rows with TMA (the async proxy)
-                    __threadfence();
                 }
+                // the barrier orders every warp's stores before one thread's gpu-scope fence and count (the pattern of
+                // a grid barrier): the other warps go on to the next tile instead of each waiting for its stores
                 const bool stop = kx::named_bar_or(1, C::EPI_WARPS * 32, !ok || *abort_flag);
-                if (!stop && live && ew == 0 && lane == 0) atomicAdd(L.ready + rg, 1u);
+                if (!stop && live && ew == 0 && lane == 0) {
+                    __threadfence();
+                    atomicAdd(L.ready + rg, 1u);
+                }
                 if (stop) break;
             }
             kx::tc_fence_before();
@@ -2363,10 +2366,10 @@ int launch_i8_pair(const int8_t* xq, int ldq, const float* sx, const int8_t* wq,
     const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * n_tiles_n;
     int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
     if (clusters <= 0) clusters = sm_count() / 2;
-    if (QOUT) {  // a row group's tiles must all be resident at once, and a round of the walk covers whole row groups
-        if (n_tiles_n > clusters) return -1;
-        clusters = clusters / n_tiles_n * n_tiles_n;
-    }
+    // QOUT: a tile's pass 2 waits for every tile of its row group (consecutive in the walk) to finish pass 1, and a
+    // cluster takes tile t + clusters only after finishing tile t; with at least n_tiles_n clusters every wait points
+    // to tiles earlier in the walk, so the waits always end, whatever the cluster count
+    if (QOUT && n_tiles_n > clusters) return -1;
     if (clusters > tiles) clusters = tiles;
     return kx::launch_pdl(kern, dim3(2 * clusters), dim3(C::THREADS), C::SMEM, st, ta, tb, sx, scale, bias, y, acc, ldy, m, n,
                           k, act, alpha, status, qo);
@@ -2778,7 +2781,7 @@ int kx_i8_chain(int n_layers, int m, const int8_t* const* a, const int* lda, con
     std::memset(ta, 0, sizeof ta);
     std::memset(tb, 0, sizeof tb);
     const int m_tiles = (m + 2 * BM - 1) / (2 * BM);
-    int tiles = 0, lcm_n = 1;
+    int tiles = 0, max_nt = 1;
     for (int l = 0; l < n_layers; l++) {
         if (k[l] <= 0 || n[l] <= 128 || k[l] > lda[l] || k[l] > ldw[l] || (lda[l] & 15) || (ldw[l] & 15) ||
             (l > 0 && k[l] != n[l - 1]) || (reinterpret_cast<uintptr_t>(a[l]) & 15))
@@ -2804,13 +2807,7 @@ int kx_i8_chain(int n_layers, int m, const int8_t* const* a, const int* lda, con
             L.qo = QOut{const_cast<int8_t*>(a[l + 1]), sx_out[l], w, w + m, nullptr, lda[l + 1], 0};
             L.ready = w + m + rgs;
             if (lda[l + 1] < n[l]) return -1;
-            int g = lcm_n, h = L.n_tiles_n;  // clusters: a multiple of every hidden layer's tiles per row group
-            while (h) {
-                const int r = g % h;
-                g = h;
-                h = r;
-            }
-            lcm_n = lcm_n / g * L.n_tiles_n;
+            if (L.n_tiles_n > max_nt) max_nt = L.n_tiles_n;  // clusters: at least every hidden layer's tiles per row group
         } else {
             L.y = y;
         }
@@ -2823,8 +2820,7 @@ int kx_i8_chain(int n_layers, int m, const int8_t* const* a, const int* lda, con
         if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
         int clusters = max_pair_clusters(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
         if (clusters <= 0) clusters = sm_count() / 2;
-        if (lcm_n > clusters) return -1;
-        clusters = clusters / lcm_n * lcm_n;
+        if (max_nt > clusters) return -1;
         if (clusters > tiles) clusters = tiles;
         return kx::launch_pdl(kern, dim3(2 * clusters), dim3(C::THREADS), C::SMEM, static_cast<cudaStream_t>(stream), ta[0],
                               ta[1], ta[2], ta[3], tb[0], tb[1], tb[2], tb[3], ch, m, status);

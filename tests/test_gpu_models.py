@@ -167,23 +167,49 @@ def test_chunked_equals_unchunked_and_trim(Model, model_dir):
     assert np.array_equal(m(x[: 3 * 128]), want[:3])
 
 
-def test_device_forward_matches_host_forward(Model, model_dir, libkx):
+def _reshape_tail_model(path):
+    """LINEAR 40 -> 64, ReLU, LINEAR 64 -> 48, then a RESHAPE to (6, 8): the model output is a view."""
+    from kernix_b200 import knx_writer
+    rng = np.random.default_rng(3)
+    g = knx_writer.Graph((40,))
+    h = g.act(g.linear(0, rng.standard_normal((40, 64)).astype(F32) * 0.2, rng.standard_normal(64).astype(F32)), "relu")
+    h = g.linear(h, rng.standard_normal((64, 48)).astype(F32) * 0.2, rng.standard_normal(48).astype(F32))
+    g.reshape(h, (6, 8))
+    g.write(path)
+    return path
+
+
+@pytest.mark.parametrize("case", ["c1", "c1-unaligned-out", "c1-chunked", "reshape-tail", "c2"])
+def test_device_forward_matches_host_forward(Model, model_dir, libkx, case):
+    """kernix_model_forward_device gives the host forward's bits. The step that makes the output writes the caller's
+    buffer directly (aligned buffer, one chunk or several under a workspace limit, the int8 chain's last layer);
+    an unaligned buffer or an output that is a RESHAPE view is copied out of the workspace instead."""
     from kernix_b200 import configs
-    p = cfg_path("c1", model_dir)
-    m = Model(p)
-    x = configs.inputs("c1", 300)
+    if case == "reshape-tail":
+        p, rows = _reshape_tail_model(f"{model_dir}/reshape_tail.knx"), 300
+        x = np.random.default_rng(4).standard_normal((rows, 40)).astype(F32)
+    else:
+        cfg = case.split("-")[0]
+        p, rows = cfg_path(cfg, model_dir), 300 if cfg == "c1" else 4096
+        x = configs.inputs(cfg, rows)
+    m = Model(p, workspace_mb=0.25 if case == "c1-chunked" else None)
     want = m(x)
     dx = torch.from_numpy(x).cuda()
-    dy = torch.empty((300, 10), dtype=torch.float32, device="cuda")
+    off = 1 if case == "c1-unaligned-out" else 0
+    buf = torch.full((rows * m.out_dim + off,), float("nan"), dtype=torch.float32, device="cuda")
     libkx.kernix_model_forward_device.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
     libkx.kernix_model_forward_device.restype = ctypes.c_int
     libkx.kernix_model_check.argtypes = [ctypes.c_void_p]
     libkx.kernix_model_check.restype = ctypes.c_int
-    rc = libkx.kernix_model_forward_device(m._h, dx.data_ptr(), 300, dy.data_ptr(), torch.cuda.current_stream().cuda_stream)
-    assert rc == 0
-    torch.cuda.synchronize()
-    assert libkx.kernix_model_check(m._h) == 0
-    assert np.array_equal(dy.cpu().numpy(), want)
+    for _ in range(2):  # the second call reuses the workspace the first one sized
+        rc = libkx.kernix_model_forward_device(m._h, dx.data_ptr(), rows, buf.data_ptr() + 4 * off,
+                                               torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert libkx.kernix_model_check(m._h) == 0
+        got = buf.cpu().numpy()[off:].reshape(want.shape)
+        assert np.array_equal(got, want)
+    assert np.array_equal(m(x), want)  # the host forward after device forwards: its own workspace output again
 
 
 @pytest.mark.parametrize("cfg,batch,ws_mb", [("c2", 1000, 0), ("c2", 1000, 40), ("c3", 37, 0), ("c4", 9, 0)])
