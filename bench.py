@@ -40,10 +40,10 @@ DIMS = [1024, 4096, 4096, 1024]
 METRIC = "samples/s, int8 MLP 1024-4096-4096-1024 (config c2), batch 4096 per GPU"
 WORKLOAD = "c2: int8-quantised MLP 1024-4096-4096-1024, GELU hidden, I8_COL per-output-channel weights, batch 4096"
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) per int8-GEMM op from an ncu capture of the int8 GEMM at M = 8192, K = N = 4096 with GELU
-# (dram__bytes_read.sum + dram__bytes_write.sum): 167.3 MB for 274.9 GOP; the roofline's traffic per launch is this
-# ratio times the launch's ops.
-GEMM_DRAM_BYTES_PER_OP = 167.3e6 / 274.9e9
+# DRAM bytes (read + write) of one k_i8_chain launch at M = 4096 from an ncu capture (dram__bytes_read.sum 29.80 MB +
+# dram__bytes_write.sum 11.80 MB): the weights and the layer-0 rows are read once, the output written once, the hidden
+# int8 rows stay in L2
+CHAIN_DRAM_BYTES = 41.60e6
 
 
 def parse():
@@ -57,9 +57,10 @@ def parse():
                     help="profiling case: only run the int8 GEMM of c2's 4096x4096 layer with M rows, 3 launches, then exit")
     ap.add_argument("--kernel-k", type=int, default=4096, help="K of the profiling case (1024: c2's first layer)")
     ap.add_argument("--kernel-act", type=int, default=1, help="activation of the profiling case (1 GELU, -1 none)")
-    ap.add_argument("--kernel-dtype", choices=["i8", "f32", "attn"], default="i8",
-                    help="kernel of the profiling case: int8 or 3xTF32 GEMM, or (attn) the attention core on c4's shape "
-                         "(M samples x 128 positions, 8 heads of 64)")
+    ap.add_argument("--kernel-dtype", choices=["i8", "f32", "attn", "chain"], default="i8",
+                    help="kernel of the profiling case: int8 or 3xTF32 GEMM, (attn) the attention core on c4's shape "
+                         "(M samples x 128 positions, 8 heads of 64), or (chain) c2's three int8 layers as the forward "
+                         "runs them, one k_i8_chain launch over M rows")
     ap.add_argument("--workload", choices=["c2", "c5-rows", "c1", "c3", "c4", "c5"], default="c2",
                     help="c5-rows: config c5 with its wide layers split by output columns over the torchrun ranks "
                          "(one NCCL all-gather per layer; every rank runs the same batch: strong scaling). c1, c3, c4, "
@@ -74,6 +75,52 @@ def parse():
     return ap.parse_args()
 
 
+class ChainCase:
+    """c2's three int8 layers (1024-4096-4096-1024, GELU hidden) as one kx_i8_chain launch over m rows, the forward's
+    dominant kernel: seeded int8 rows and weights (timing does not depend on the values), the quantised hidden rows
+    in scratch, control words cleared before every launch as the forward's quantiser clears them."""
+
+    def __init__(self, L, torch, np, m):
+        import ctypes
+        rng = np.random.default_rng(3)
+        self.L, self.torch, self.m = L, torch, m
+        self.ctypes = ctypes
+        d = DIMS
+        self.keep = []
+        dev = lambda a: self._k(torch.from_numpy(np.ascontiguousarray(a)).cuda())  # noqa: E731
+        self.a = [dev(rng.integers(-127, 128, (m, d[0]), dtype=np.int8))] + \
+            [self._k(torch.zeros((m, d[l + 1]), dtype=torch.int8, device="cuda")) for l in range(2)]
+        self.sx = [self._k(torch.full((m,), 0.01, device="cuda")) for _ in range(3)]
+        self.wq = [dev(rng.integers(-127, 128, (d[l + 1], d[l]), dtype=np.int8)) for l in range(3)]
+        self.sc = [self._k(torch.full((d[l + 1],), 0.002, device="cuda")) for l in range(3)]
+        self.bi = [self._k(torch.zeros(d[l + 1], device="cuda")) for l in range(3)]
+        rgs = (m + 127) // 128
+        self.ctl = self._k(torch.zeros(2 * (m + 2 * rgs), dtype=torch.int32, device="cuda"))
+        self.y = self._k(torch.empty((m, d[-1]), device="cuda"))
+        self.status = self._k(torch.zeros(1, dtype=torch.int32, device="cuda"))
+        P = lambda ts: (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])  # noqa: E731
+        I = lambda v: (ctypes.c_int * len(v))(*v)  # noqa: E731, E741
+        self.args = [P(self.a), I(d[:3]), P(self.sx), P(self.wq), I(d[:3]), P(self.sc), P(self.bi), I(d[:3]), I(d[1:]),
+                     I([1, 1, -1]), (ctypes.c_float * 3)(0.0, 0.0, 0.0), P(self.sx[1:])]
+
+    def _k(self, t):
+        self.keep.append(t)
+        return t
+
+    def clear(self):
+        self.ctl.zero_()
+
+    def launch(self, stream):
+        vp = self.ctypes.c_void_p
+        if self.L.kx_i8_chain(3, self.m, *self.args, vp(self.ctl.data_ptr()), vp(self.y.data_ptr()),
+                              vp(self.status.data_ptr()), vp(stream.cuda_stream)) != 0:
+            raise RuntimeError("kx_i8_chain failed")
+
+    def check(self):
+        if int(self.status.item()) != 0:
+            raise RuntimeError("the int8 chain reported a timeout")
+
+
 def kernel_case(m_rows, k=4096, act=1, dtype="i8"):
     """Three launches of the int8 GEMM (GELU epilogue by default), or with dtype "f32" of the 3xTF32 GEMM, on an
     M x K x 4096 problem -- for an ncu capture of one kernel on a case larger than L2 (M = 8192, K = 4096: 32 MB A
@@ -86,6 +133,16 @@ def kernel_case(m_rows, k=4096, act=1, dtype="i8"):
     L = kx_abi.lib()
     n = 4096
     rng = np.random.default_rng(0)
+    if dtype == "chain":
+        case = ChainCase(L, torch, np, m_rows)
+        st = torch.cuda.current_stream()
+        for _ in range(3):
+            case.clear()
+            case.launch(st)
+        torch.cuda.synchronize()
+        case.check()
+        print(json.dumps({"kernel_case": "k_i8_chain", "m": m_rows, "dims": DIMS, "launches": 3}))
+        return
     if dtype == "attn":  # c4's attention core: S = 128, 8 heads, d = 64, Q / K / V packed in one row as the model does
         S, H, d = 128, 8, 64
         qkv = torch.from_numpy(rng.standard_normal((m_rows * S, 3 * H * d)).astype(np.float32)).cuda()
@@ -444,7 +501,7 @@ def run_kernix(args):
             "per_config": per_config,
             "strong_scaling": strong,
             "clocks": clk.summary(),
-            "gpu_launches": 6 * args.steps,
+            "gpu_launches": 2 * args.steps,  # per forward: the row quantiser, then the one-launch int8 chain
             "peaks_file": bool(peaks),
         }
         print(json.dumps(line), flush=True)
@@ -453,11 +510,12 @@ def run_kernix(args):
         dist.destroy_process_group()
 
 
-def gemm_roofline(L, torch, np, steps, flush):
-    """Time kx_gemm_i8 on the three c2 layer shapes (M = 4096) with CUDA events around each launch."""
+def layer_gemm_times(L, torch, np, steps, flush):
+    """Each c2 layer shape as its own kx_gemm_i8 launch (M = 4096, fp32 output, GELU), CUDA events around each
+    launch, L2 flushed before each: the per-layer context of the roofline."""
     rng = np.random.default_rng(3)
     st = torch.cuda.current_stream()
-    tot_ops, tot_t, per = 0.0, 0.0, []
+    per = []
     for k, n in zip(DIMS[:-1], DIMS[1:]):
         xq = torch.from_numpy(rng.integers(-127, 128, (BATCH, k), dtype=np.int8)).cuda()
         wq = torch.from_numpy(rng.integers(-127, 128, (n, k), dtype=np.int8)).cuda()
@@ -484,12 +542,32 @@ def gemm_roofline(L, torch, np, steps, flush):
         if int(status.item()) != 0:
             raise RuntimeError("GEMM reported a timeout")
         t = sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3 / steps
-        ops = 2.0 * BATCH * k * n
-        per.append({"m": BATCH, "k": k, "n": n, "us": t * 1e6, "tops": ops / t / 1e12})
-        tot_ops += ops
-        tot_t += t
-    achieved = tot_ops / tot_t / 1e12
-    peak, basis = None, None
+        per.append({"m": BATCH, "k": k, "n": n, "us": t * 1e6, "tops": 2.0 * BATCH * k * n / t / 1e12})
+    return per
+
+
+def gemm_roofline(L, torch, np, steps, flush):
+    """Roofline of the forward's dominant kernel, k_i8_chain (c2's three int8 layers in one persistent launch; the
+    quantiser that feeds it is the rest of the forward), timed alone on c2's M = 4096 as the forward runs it: CUDA
+    events on the launching stream around each launch, L2 flushed and the chain's control words cleared before each.
+    Achieved = 206.16 GOP per launch / mean launch time; peak = 2 x the measured dense bf16 burst."""
+    st = torch.cuda.current_stream()
+    case = ChainCase(L, torch, np, BATCH)
+    for _ in range(3):
+        case.clear()
+        case.launch(st)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in evs:
+        flush.zero_()
+        case.clear()
+        e0.record(st)
+        case.launch(st)
+        e1.record(st)
+    torch.cuda.synchronize()
+    case.check()
+    t = sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3 / steps
+    ops = 2.0 * BATCH * sum(k * n for k, n in zip(DIMS[:-1], DIMS[1:]))
+    achieved = ops / t / 1e12
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
         peak = 2.0 * float(peaks["bf16_tflops"])
@@ -497,11 +575,13 @@ def gemm_roofline(L, torch, np, steps, flush):
     except (OSError, ValueError, KeyError):
         peak = 2.0 * 1590.0
         basis = "2 x fallback dense bf16 1.59 PFLOP/s"
-    return {"kernel": "k_gemm_i8_pair (tcgen05 kind::i8, cta_group::2, 256x256 tiles)", "bound": "tensor", "achieved": achieved, "peak": peak,
-            "unit": "TOP/s (int8, 2 ops per MAC)", "frac": achieved / peak, "peak_basis": basis,
-            "traffic": GEMM_DRAM_BYTES_PER_OP * tot_ops / len(per),
-            "traffic_note": "bytes per launch, scaled by ops from the ncu capture of M=8192 (profiles/)", "per_layer": per,
-            "algorithmic_ops_per_forward": tot_ops, "gemm_us_per_forward": tot_t * 1e6}
+    per = layer_gemm_times(L, torch, np, steps, flush)
+    return {"kernel": "k_i8_chain (tcgen05 kind::i8, cta_group::2, 256x256 tiles of all three layers in one persistent "
+                      "launch; hidden layers quantise their own output rows)",
+            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s (int8, 2 ops per MAC)",
+            "frac": achieved / peak, "peak_basis": basis, "us_per_launch": t * 1e6, "traffic": CHAIN_DRAM_BYTES,
+            "traffic_note": "dram read + write bytes of one k_i8_chain launch at M = 4096 from an ncu capture (profiles/)",
+            "algorithmic_ops_per_launch": ops, "per_layer_standalone": per}
 
 
 def c5_sharded_times(L, torch, dist, rank, world, local, batches, steps, warmup):

@@ -16,6 +16,7 @@ SIGNATURES = {
     "kx_probe_bounded_wait": [_i, ctypes.c_ulonglong, _vp, _vp, _vp],
     "kx_gemm_i8_q": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _f, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp],
     "kx_quant_rows_z": [_vp, _i, _i, _i, _vp, _i, _vp, _vp, _i, _vp],
+    "kx_i8_chain": [_i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "kx_prep_i8_weight": [_vp, _i, _i, _vp, _i, _vp],
     "kx_gemm_f32": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp],
     "kx_gemm_f32_res": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _i, _vp, _vp],
