@@ -13,14 +13,19 @@
 //   1. every thread splits its Q and K values into hi / lo and stores them in the canonical K-major 128-byte-swizzle
 //      layout as 128-row tiles of 32 floats of K;
 //   2. thread 0 issues S = Q . K^T (N = 128 keys) into TMEM columns [0, 128), while the threads store V transposed
-//      (rows = head dim, K index = key), the B operand of P . V, and then issue the global loads of the NEXT pair's
-//      rows into the same registers: their latency is hidden behind this pair's MMAs and softmax;
+//      (rows = head dim, K index = key), the B operand of P . V; the NEXT pair's rows are then loaded into the same
+//      registers in three parts (Q here, K after the softmax's partial maxima, V after the P . V MMAs are issued), so
+//      that no part stalls its warps on the load queue and the loads complete behind this pair's MMAs and softmax;
 //   3. row r's scores are shared by the four warps of its quarter, 32 keys each (one tcgen05.ld of 32 columns): each
 //      finds its partial max, the four meet through shared memory (max; then the sum of e = exp(s - max), added in
-//      key-group order), and p = e * (1 / sum) is split into hi / lo and written as the A operand tiles of P . V over
-//      the Q / K tiles, whose MMAs have completed;
+//      key-group order; the scores are kept in base-2 units, s log2(e), so e is one ex2.approx, ~2 ulp), and
+//      p = e * (1 / sum) is split into hi / lo and written as the A operand tiles of P . V over the Q / K tiles,
+//      whose MMAs have completed;
 //   4. thread 0 issues ctx = P . V (N = 64) into TMEM columns [128, 192);
-//   5. warp (q, g) stores rows 32 q .. 32 q + 31, head-dim columns 16 g .. 16 g + 15.
+//   5. warp (q, g) takes rows 32 q .. 32 q + 31, head-dim columns 16 g .. 16 g + 15 of ctx out of TMEM and stages
+//      them in the V^T tiles (free once P . V has completed); when the quarter's rows are staged, whole rows go to
+//      global memory by bulk copies (cp.async.bulk) that run while the next pair starts (plain stores where rows are
+//      not 16-byte aligned). The softmax's exchanges between the four warps of a quarter use a barrier per quarter.
 // Every wait is bounded; a timeout records KX_STATUS_TIMEOUT in the status word and the CTA stops.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -28,6 +33,7 @@
 #include <cmath>
 #include <cstdint>
 
+#include "kx_act.cuh"
 #include "kx_kernels.h"
 #include "kx_sm100.cuh"
 
@@ -48,6 +54,8 @@ struct AtCtl {
 };
 constexpr int AT_SMEM = AT_QK_BYTES + AT_V_BYTES + 1024 + static_cast<int>(sizeof(AtCtl));
 constexpr uint32_t AT_S = 0, AT_O = 128, AT_TMEM_COLS = 256;
+constexpr int AT_CROW = 272;  // bytes per staged ctx row (64 floats + 16: 16-byte aligned, fewer bank conflicts)
+static_assert(AT_MAX * AT_CROW <= AT_V_BYTES, "the staged ctx rows fit in the V^T tiles");
 constexpr int AT_NQ = AT_MAX * 16 / AT_THREADS;  // float4s of Q (and of K) per thread
 
 // byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled tile
@@ -76,23 +84,25 @@ struct AtArgs {
     float scale;
 };
 
-// the rows of pair p into registers: Q and K as float4s (row, d4) = (i / 16, i % 16), i = t + 512 u (a half-warp
-// reads one row's 256 contiguous bytes); V as keys 32 (w % 4) + lane, head dims 16 (w / 4) .. +15
-__device__ __forceinline__ void at_load(const AtArgs& A, int p, int tid, int quarter, int grp, int lane, float4 (&xq)[AT_NQ],
-                                        float4 (&xk)[AT_NQ], float4 (&xv)[4]) {
-    const int b = p / A.H, h = p - b * A.H;
-    const float* qb = A.q + static_cast<long>(b) * A.Rq * A.ldq + h * A.dk;
-    const float* kb = A.k + static_cast<long>(b) * A.S * A.ldk + h * A.dk;
-    const float* vb = A.v + static_cast<long>(b) * A.S * A.ldv + h * A.dv;
-    const bool vq = ((A.ldq | A.dk) & 3) == 0 && (reinterpret_cast<uintptr_t>(qb) & 15) == 0;
-    const bool vk = ((A.ldk | A.dk) & 3) == 0 && (reinterpret_cast<uintptr_t>(kb) & 15) == 0;
-    const bool vv = ((A.ldv | A.dv) & 3) == 0 && (reinterpret_cast<uintptr_t>(vb) & 15) == 0;
+// The rows of pair p into registers, in three calls (Q, K, V: 32 KB per CTA each) made at different points of the
+// previous pair, so that no call puts more loads in flight than the load queue takes without stalling its warps.
+// Q and K as float4s (row, d4) = (i / 16, i % 16), i = t + 512 u (a half-warp reads one row's 256 contiguous bytes);
+// V as keys 32 (w % 4) + lane, head dims 16 (w / 4) .. +15.
+__device__ __forceinline__ void at_load_qk(const float* base, int ld, int rows, int d, int p, int H, int tid,
+                                           float4 (&x)[AT_NQ]) {
+    const int b = p / H, h = p - b * H;
+    const float* xb = base + static_cast<long>(b) * rows * ld + h * d;
+    const bool vec = ((ld | d) & 3) == 0 && (reinterpret_cast<uintptr_t>(xb) & 15) == 0;
 #pragma unroll
     for (int u = 0; u < AT_NQ; u++) {
-        const int i = u * AT_THREADS + tid, row = i >> 4, d = (i & 15) * 4;
-        xq[u] = row < A.Rq ? load_row4(qb + static_cast<long>(row) * A.ldq, d, A.dk, vq) : make_float4(0.f, 0.f, 0.f, 0.f);
-        xk[u] = row < A.S ? load_row4(kb + static_cast<long>(row) * A.ldk, d, A.dk, vk) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int i = u * AT_THREADS + tid, row = i >> 4, c = (i & 15) * 4;
+        x[u] = row < rows ? load_row4(xb + static_cast<long>(row) * ld, c, d, vec) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+}
+__device__ __forceinline__ void at_load_v(const AtArgs& A, int p, int quarter, int grp, int lane, float4 (&xv)[4]) {
+    const int b = p / A.H, h = p - b * A.H;
+    const float* vb = A.v + static_cast<long>(b) * A.S * A.ldv + h * A.dv;
+    const bool vv = ((A.ldv | A.dv) & 3) == 0 && (reinterpret_cast<uintptr_t>(vb) & 15) == 0;
     const int vj = quarter * 32 + lane, vd0 = grp * 16;
 #pragma unroll
     for (int u = 0; u < 4; u++)
@@ -121,7 +131,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attention_tc(const AtArgs A, 
     }
     float4 xq[AT_NQ], xk[AT_NQ], xv[4];
     int p = blockIdx.x;
-    if (p < A.pairs) at_load(A, p, tid, quarter, grp, lane, xq, xk, xv);
+    if (p < A.pairs) {
+        at_load_qk(A.q, A.ldq, A.Rq, A.dk, p, A.H, tid, xq);
+        at_load_qk(A.k, A.ldk, A.S, A.dk, p, A.H, tid, xk);
+        at_load_v(A, p, quarter, grp, lane, xv);
+    }
+    // the scores in base-2 units: exp(s - m) = 2^(s log2(e) - m log2(e)), one ex2.approx per score (~2 ulp)
+    const float scale2 = A.scale * 1.4426950408889634f;
+    // whole ctx rows by bulk copy: every row start 16-byte aligned and the row a multiple of 16 bytes
+    const bool bulk_out = ((A.ldc | A.dv) & 3) == 0 && (reinterpret_cast<uintptr_t>(A.ctx) & 15) == 0;
     kx::tc_fence_before();
     __syncthreads();
     kx::tc_fence_after();
@@ -131,6 +149,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attention_tc(const AtArgs A, 
 
     for (; p < A.pairs; p += gridDim.x) {
         const int b = p / A.H, h = p - b * A.H;
+        if (bulk_out && lane < 8) kx::bulk_wait_read();  // the previous pair's staged rows (in the V^T tiles) are read
         // 1. Q and K of this pair into the operand tiles (the previous pair's MMAs have completed)
 #pragma unroll
         for (int u = 0; u < AT_NQ; u++) {
@@ -180,8 +199,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attention_tc(const AtArgs A, 
                 }
             }
         }
-        if (p + static_cast<int>(gridDim.x) < A.pairs)
-            at_load(A, p + static_cast<int>(gridDim.x), tid, quarter, grp, lane, xq, xk, xv);
+        const int pn = p + static_cast<int>(gridDim.x);  // the next pair: Q now, K after the softmax's max, V later
+        if (pn < A.pairs) at_load_qk(A.q, A.ldq, A.Rq, A.dk, pn, A.H, tid, xq);
         // the warps read TMEM with warp-collective loads: agree on the outcome first
         if (!__syncthreads_and(kx::mbar_wait(&ctl->bar, 0, &ctl->abort, status))) {
             pending = 0;
@@ -199,26 +218,27 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attention_tc(const AtArgs A, 
 #pragma unroll
             for (int j = 0; j < 32; j++) {
                 const int key = key0 + j;
-                const float t = __fmul_rn(__uint_as_float(sv[j]), A.scale);
+                const float t = __fmul_rn(__uint_as_float(sv[j]), scale2);
                 e[j] = (key >= A.S || (A.causal && key > r)) ? -INFINITY : t;
                 m = fmaxf(m, e[j]);
             }
             ctl->red[grp][r] = m;
         }
-        __syncthreads();
+        if (pn < A.pairs) at_load_qk(A.k, A.ldk, A.S, A.dk, pn, A.H, tid, xk);
+        kx::named_bar(1 + quarter, 128);  // the four warps of this lane quarter (the rows they share)
         {
             const float m = fmaxf(fmaxf(ctl->red[0][r], ctl->red[1][r]), fmaxf(ctl->red[2][r], ctl->red[3][r]));
 #pragma unroll
-            for (int j = 0; j < 32; j++) e[j] = expf(__fsub_rn(e[j], m));
+            for (int j = 0; j < 32; j++) e[j] = kx::ex2_approx(__fsub_rn(e[j], m));
         }
-        __syncthreads();  // every partial max has been read before the partial sums overwrite them
+        kx::named_bar(1 + quarter, 128);  // every partial max has been read before the partial sums overwrite them
         {
             float part = 0.0f;
 #pragma unroll
             for (int j = 0; j < 32; j++) part = __fadd_rn(part, e[j]);
             ctl->red[grp][r] = part;
         }
-        __syncthreads();
+        kx::named_bar(1 + quarter, 128);
         {
             const float sum = __fadd_rn(__fadd_rn(__fadd_rn(ctl->red[0][r], ctl->red[1][r]), ctl->red[2][r]), ctl->red[3][r]);
             const float inv = __fdiv_rn(1.0f, sum);
@@ -256,18 +276,39 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attention_tc(const AtArgs A, 
             kx::mma_commit(&ctl->bar);
         }
         __syncwarp();
+        if (pn < A.pairs) at_load_v(A, pn, quarter, grp, lane, xv);
         if (!__syncthreads_and(kx::mbar_wait(&ctl->bar, 1, &ctl->abort, status))) {
             pending = 1;
             break;
         }
         kx::tc_fence_after();
 
-        // 5. ctx rows 32 quarter .. +31, head-dim columns 16 grp .. 16 grp + 15
+        // 5. ctx rows 32 quarter .. +31, head-dim columns 16 grp .. 16 grp + 15: staged in the V^T tiles (free once
+        // P . V has completed), then written by bulk copies of whole rows that run while the next pair starts; plain
+        // stores where the rows are not 16-byte aligned
         {
             uint32_t ov[16];
             kx::tmem_ld16(tmem + lanes + AT_O + vd0, ov);
             kx::tmem_ld_wait();
-            if (r < A.Rq && vd0 < A.dv) {
+            if (bulk_out) {
+                if (vd0 < A.dv) {
+                    float4* srow = reinterpret_cast<float4*>(vt + r * AT_CROW + vd0 * 4);
+#pragma unroll
+                    for (int j4 = 0; j4 < 4; j4++)
+                        srow[j4] = make_float4(__uint_as_float(ov[4 * j4]), __uint_as_float(ov[4 * j4 + 1]),
+                                               __uint_as_float(ov[4 * j4 + 2]), __uint_as_float(ov[4 * j4 + 3]));
+                }
+                kx::fence_proxy_async_smem();
+                kx::named_bar(1 + quarter, 128);  // the quarter's 32 rows are staged
+                if (lane < 8) {  // warp (quarter, grp) copies rows 32 quarter + 8 grp .. + 7
+                    const int rr = quarter * 32 + grp * 8 + lane;
+                    if (rr < A.Rq) {
+                        kx::bulk_store(A.ctx + (static_cast<long>(b) * A.Rq + rr) * A.ldc + h * A.dv, vt + rr * AT_CROW,
+                                       static_cast<uint32_t>(A.dv) * 4);
+                        kx::bulk_commit();
+                    }
+                }
+            } else if (r < A.Rq && vd0 < A.dv) {
                 float* dst = A.ctx + (static_cast<long>(b) * A.Rq + r) * A.ldc + h * A.dv + vd0;
                 const int nv = A.dv - vd0;
                 if (nv >= 16 && ((A.ldc | A.dv) & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
@@ -286,6 +327,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_attention_tc(const AtArgs A, 
         __syncthreads();  // every warp has read this pair's ctx before the next pair's MMAs write TMEM
         kx::tc_fence_after();
     }
+    if (bulk_out && lane < 8) kx::bulk_wait_all();  // the last pair's rows are written before the CTA ends
     if (pending >= 0) {
         // the MMAs of the timed-out phase may still be running: give them time to finish (bounded) before the TMEM
         // and the shared memory go away

@@ -2589,24 +2589,34 @@ __global__ void __launch_bounds__(256) k_conv_direct(const float* __restrict__ x
         if (pn < M) geom(buf ^ 1, pn);
         __syncthreads();
         if (pn < M) gather(buf ^ 1, pn, v);
-        for (int p = warp; p < DC_PIX; p += 8) {
-            const int m = p0 + p;
-            if (m >= M) break;
-            float a0 = 0.0f, a1 = 0.0f;
+        // four pixels per warp at a time: eight independent fma chains per lane (each still sums k in order, so the
+        // same bits as one pixel at a time), the pixels' inputs broadcast from shared memory as float4s
+        for (int p = warp * 4; p < DC_PIX; p += 32) {
+            if (p0 + p >= M) break;
+            float a0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, a1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int k4 = 0; k4 < DC_MAXK / 4; k4++) {
                 if (4 * k4 >= K) break;
-                const float4 xv = *reinterpret_cast<const float4*>(&xs[p][4 * k4]);
-                const float xk[4] = {xv.x, xv.y, xv.z, xv.w};
+                float4 xv[4];
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    a0 = __fmaf_rn(xk[e], w0[4 * k4 + e], a0);
-                    a1 = __fmaf_rn(xk[e], w1[4 * k4 + e], a1);
-                }
+                for (int i = 0; i < 4; i++) xv[i] = *reinterpret_cast<const float4*>(&xs[p + i][4 * k4]);
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float xk = e == 0 ? xv[i].x : (e == 1 ? xv[i].y : (e == 2 ? xv[i].z : xv[i].w));
+                        a0[i] = __fmaf_rn(xk, w0[4 * k4 + e], a0[i]);
+                        a1[i] = __fmaf_rn(xk, w1[4 * k4 + e], a1[i]);
+                    }
             }
-            float* yr = y + static_cast<size_t>(m) * Co + g * cog;
-            if (c0 < cog) yr[c0] = epi_act<ACTC>(bias ? __fadd_rn(a0, b0) : a0, act, alpha);
-            if (c1 < cog) yr[c1] = epi_act<ACTC>(bias ? __fadd_rn(a1, b1) : a1, act, alpha);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int m = p0 + p + i;
+                if (m >= M) break;
+                float* yr = y + static_cast<size_t>(m) * Co + g * cog;
+                if (c0 < cog) yr[c0] = epi_act<ACTC>(bias ? __fadd_rn(a0[i], b0) : a0[i], act, alpha);
+                if (c1 < cog) yr[c1] = epi_act<ACTC>(bias ? __fadd_rn(a1[i], b1) : a1[i], act, alpha);
+            }
         }
     }
 }

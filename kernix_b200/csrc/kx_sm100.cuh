@@ -321,6 +321,19 @@ __device__ __forceinline__ void tmem_st16x256b_x4(uint32_t taddr, const uint32_t
         : "memory");
 }
 
+// bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from this CTA's shared memory to global
+// memory by the async proxy, tracked in the issuing thread's bulk group (a generic-proxy write of the source must be
+// followed by fence_proxy_async_smem() before the copy is issued)
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until this thread's committed bulk copies have read their shared-memory sources (the buffer may be reused)
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// wait until this thread's committed bulk copies are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // named barrier over `count` threads (a multiple of 32) of the CTA; barrier 0 is __syncthreads'
 __device__ __forceinline__ void named_bar(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
