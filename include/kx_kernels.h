@@ -94,6 +94,21 @@ KERNIX_API int kx_linear_i8_noalloc(const float* x, int ldx, int rows, int k, co
 KERNIX_API int kx_probe_bounded_wait(int arrive, unsigned long long limit_ns, int* status, unsigned long long* waited_ns,
                                      void* stream);
 
+/* Small-batch int8 layers with the reduction split over the SMs. kx_i8_split_blocks: K blocks (of 128) per range for an
+ * m x n x k layer so that its output tiles times its ranges about fill the SMs (at most KX_I8_SPLIT_MAX ranges).
+ * kx_gemm_i8_split_acc: the int32 sums of each K range into plane z of part (ceil(ceil(k / 128) / kbs) planes of
+ * m x n int32). kx_i8_rows: one row per block adds the planes (exactly), then ((float)acc * sx) * scale + bias and the
+ * activation as the int8 GEMM epilogue does, and stores the fp32 row (q == NULL) or quantises it for the next int8
+ * layer exactly as the quantised-output epilogue does (q: m x ldq int8, columns n .. ldq - 1 written 0; sx_out: row
+ * scales). n, ldq <= 8192. Bit for bit the results of kx_gemm_i8 / kx_gemm_i8_q (the per-step kernels the
+ * reference's kernix_qmatmul :99-182 maps to). */
+#define KX_I8_SPLIT_MAX 64
+KERNIX_API int kx_i8_split_blocks(int m, int n, int k);
+KERNIX_API int kx_gemm_i8_split_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int m, int n, int k, int kbs,
+                                   int32_t* part, int* status, void* stream);
+KERNIX_API int kx_i8_rows(const int32_t* part, int planes, int m, int n, const float* sx, const float* scale, const float* bias,
+                          int act, float alpha, float* y, int ldy, int8_t* q, int ldq, float* sx_out, void* stream);
+
 /* int32 accumulators only (acc[row][col], leading dimension ldacc): exposes the integer result for tests. */
 KERNIX_API int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
                    int* status, void* stream);

@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(I8Cfg<BN, STAGES>::THREADS, 1)
 k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
           const float* __restrict__ sx, const float* __restrict__ scale, const float* __restrict__ bias,
           float* __restrict__ y, int32_t* __restrict__ acc_out, int ldy, int M, int N, int K, int act, float alpha,
-          int* status) {
+          int* status, int kbs) {
     using C = I8Cfg<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align1024(smem_raw);
@@ -399,9 +399,20 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     volatile int* abort_flag = &ctl->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = (K + C::BK - 1) / C::BK;
+    // split-K (ACC_ONLY, kbs > 0): the reduction is cut into ranges of kbs K blocks; tile t covers output tile
+    // t % (m_tiles n_tiles) over range t / (m_tiles n_tiles) and writes its int32 sums into plane z of acc_out (M x
+    // ldy each). kbs <= 0: one range.
+    const int nk_all = (K + C::BK - 1) / C::BK;
+    const int kpr = kbs > 0 ? kbs : nk_all;
     const TileMap tm{(M + BM - 1) / BM, (N + BN - 1) / BN, false};
-    const int n_tiles = tm.m_tiles * tm.n_tiles;
+    const int mn_tiles = tm.m_tiles * tm.n_tiles;
+    const int n_tiles = mn_tiles * ((nk_all + kpr - 1) / kpr);
+    auto at = [&](int t, int& mt, int& nt, int& kb0, int& nk) {  // tile t: output tile and its K blocks
+        const int z = t / mn_tiles;
+        tm.at(t - z * mn_tiles, mt, nt);
+        kb0 = z * kpr;
+        nk = min(nk_all - kb0, kpr);
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -432,9 +443,9 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             kx::tma_prefetch_desc(&tmB);
             int it = 0;
             for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
-                int mt, nt;
-                tm.at(t, mt, nt);
-                for (int kb = 0; kb < nk; kb++, it++) {
+                int mt, nt, kb0, nk;
+                at(t, mt, nt, kb0, nk);
+                for (int kb = kb0; kb < kb0 + nk; kb++, it++) {
                     const int s = it % STAGES;
                     if (!kx::mbar_wait(&ctl->empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, status)) break;
                     kx::mbar_arrive_expect_tx(&ctl->full[s], C::A_BYTES + C::B_BYTES);
@@ -451,6 +462,10 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             int it = 0, j = 0;
             for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x, j++) {
                 const int b = j & 1;
+                int mt, nt, kb0, nk;
+                at(t, mt, nt, kb0, nk);
+                (void)mt;
+                (void)nt;
                 if (!kx::mbar_wait(&ctl->acc_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, status)) break;
                 kx::tc_fence_after();
                 const uint32_t d = tmem + b * BN;
@@ -483,24 +498,25 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         float* stg = reinterpret_cast<float*>(sE + ew * 2048);
         EpiPre cur{}, nxt{};
         if (!ACC_ONLY && blockIdx.x < n_tiles) {
-            int mt, nt;
-            tm.at(blockIdx.x, mt, nt);
+            int mt, nt, kb0, nk;
+            at(blockIdx.x, mt, nt, kb0, nk);
             epi_prefetch(cur, mt * BM + q * 32, nt * BN + c_lo, lane, M, N, sx, scale, bias);
         }
         int j = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, j++) {
-            int mt, nt;
-            tm.at(t, mt, nt);
+            int mt, nt, kb0, nk;
+            at(t, mt, nt, kb0, nk);
             const int b = j & 1;
             if (!ACC_ONLY && t + static_cast<int>(gridDim.x) < n_tiles) {
-                int mt2, nt2;
-                tm.at(t + gridDim.x, mt2, nt2);
+                int mt2, nt2, kb2, nk2;
+                at(t + gridDim.x, mt2, nt2, kb2, nk2);
                 epi_prefetch(nxt, mt2 * BM + q * 32, nt2 * BN + c_lo, lane, M, N, sx, scale, bias);
             }
             if (!kx::mbar_wait(&ctl->acc_full[b], (j >> 1) & 1, abort_flag, status)) break;
             kx::tc_fence_after();
+            int32_t* plane = ACC_ONLY ? acc_out + static_cast<size_t>(kb0 / kpr) * M * ldy : acc_out;
             epi_tile_i8<BN, ACC_ONLY, ACTC>(tmem + b * BN + (static_cast<uint32_t>(q * 32) << 16), mt * BM + q * 32, nt * BN,
-                                            c_lo, stg, lane, cur, y, acc_out, ldy, M, N, act, alpha);
+                                            c_lo, stg, lane, cur, y, plane, ldy, M, N, act, alpha);
             cur = nxt;
             kx::tc_fence_before();
             __syncwarp();
@@ -2296,7 +2312,7 @@ int sm_count() {
 template <int BN, bool ACC_ONLY, int ACTC>
 int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int ldw, const float* scale,
               const float* bias, float* y, int32_t* acc, int ldy, int m, int n, int k, int act, float alpha, int* status,
-              cudaStream_t st) {
+              cudaStream_t st, int kbs = 0) {
     constexpr int STAGES = 4;
     using C = I8Cfg<BN, STAGES>;
     CUtensorMap ta, tb;
@@ -2307,10 +2323,86 @@ int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int 
         return -1;
     auto kern = k_gemm_i8<BN, STAGES, ACC_ONLY, ACTC>;
     if (set_smem_once(reinterpret_cast<const void*>(kern), C::SMEM) != 0) return -1;
-    const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+    const int nk = (k + C::BK - 1) / C::BK;
+    const int ranges = kbs > 0 ? (nk + kbs - 1) / kbs : 1;
+    const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN) * ranges;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status);
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status, kbs);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// The rows of a split-K int8 layer (kx_gemm_i8_split_acc's int32 planes [z][row][column]): one block per row adds the
+// planes (exact: int32 sums modulo 2^32 do not depend on the order), then applies the epilogue's steps in its order --
+// ((float)acc * sx) * scale + bias (0 without one), the activation on pairs of columns -- and either stores the fp32
+// row or (QOUT) quantises it as the quantised-output epilogue does: the row's maximum |y| (NaN wins), sx = m / 127,
+// inv = 1 / sx, q = rint(y inv) as the low byte of y inv + 1.5 2^23; columns N .. ldq - 1 are written as 0.
+constexpr int I8R_THREADS = 256, I8R_PAIRS = 16, I8R_MAXN = 2 * I8R_THREADS * I8R_PAIRS;
+template <int ACTC, bool QOUT>
+__global__ void __launch_bounds__(I8R_THREADS) k_i8_rows(const int32_t* __restrict__ part, int planes, int M, int N,
+                                                          const float* __restrict__ sx, const float* __restrict__ scale,
+                                                          const float* __restrict__ bias, int act, float alpha,
+                                                          float* __restrict__ y, int ldy, int8_t* __restrict__ q, int ldq,
+                                                          float* __restrict__ sx_out) {
+    __shared__ uint32_t red[I8R_THREADS / 32];
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const float sxr = __ldg(sx + row);
+    const size_t plane = static_cast<size_t>(M) * N;
+    float2 v[I8R_PAIRS];
+    uint32_t mx = 0u;
+#pragma unroll
+    for (int j = 0; j < I8R_PAIRS; j++) {
+        const int c = 2 * (tid + j * I8R_THREADS);
+        v[j] = make_float2(0.0f, 0.0f);
+        if (c >= N) continue;
+        const bool two = c + 1 < N;
+        const int32_t* src = part + static_cast<size_t>(row) * N + c;
+        uint32_t a0 = 0u, a1 = 0u;  // modulo 2^32, as the MMA's int32 accumulator
+        for (int z = 0; z < planes; z++) {
+            a0 += static_cast<uint32_t>(__ldg(src + z * plane));
+            if (two) a1 += static_cast<uint32_t>(__ldg(src + z * plane + 1));
+        }
+        const float2 f = kx::mul2(kx::mul2(make_float2(static_cast<float>(static_cast<int32_t>(a0)),
+                                                       static_cast<float>(static_cast<int32_t>(a1))), kx::f2(sxr)),
+                                  make_float2(__ldg(scale + c), two ? __ldg(scale + c + 1) : 0.0f));
+        const float2 b = make_float2(bias ? __ldg(bias + c) : 0.0f, bias && two ? __ldg(bias + c + 1) : 0.0f);
+        v[j] = epi_act2<ACTC>(make_float2(__fadd_rn(f.x, b.x), __fadd_rn(f.y, b.y)), act, alpha);
+        if constexpr (QOUT) {
+            mx = kx::absmax_nan(mx, v[j].x);
+            if (two) mx = kx::absmax_nan(mx, v[j].y);
+        } else {
+            float* dst = y + static_cast<size_t>(row) * ldy + c;
+            dst[0] = v[j].x;
+            if (two) dst[1] = v[j].y;
+        }
+    }
+    if constexpr (QOUT) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((tid & 31) == 0) red[tid >> 5] = mx;
+        __syncthreads();
+        mx = red[0];
+#pragma unroll
+        for (int w = 1; w < I8R_THREADS / 32; w++) mx = max(mx, red[w]);
+        const bool nan_row = mx >= 0x7F800000u;
+        float sxv = 1.0f, inv = 1.0f;
+        if (nan_row) {
+            sxv = __uint_as_float(0x7FC00000u);
+        } else if (mx != 0u) {
+            sxv = __fdiv_rn(__uint_as_float(mx), 127.0f);
+            inv = __fdiv_rn(1.0f, sxv);
+        }
+        if (tid == 0) sx_out[row] = sxv;
+        uint16_t* qrow = reinterpret_cast<uint16_t*>(q + static_cast<size_t>(row) * ldq);
+#pragma unroll
+        for (int j = 0; j < I8R_PAIRS; j++) {
+            const int c = 2 * (tid + j * I8R_THREADS);
+            if (c >= ldq) continue;
+            uint32_t b0 = 0u, b1 = 0u;
+            if (!nan_row && c < N) b0 = __float_as_uint(__fadd_rn(__fmul_rn(v[j].x, inv), 12582912.0f)) & 0xFFu;
+            if (!nan_row && c + 1 < N) b1 = __float_as_uint(__fadd_rn(__fmul_rn(v[j].y, inv), 12582912.0f)) & 0xFFu;
+            qrow[c >> 1] = static_cast<uint16_t>(b0 | (b1 << 8));
+        }
+    }
 }
 
 // clusters of the pair kernel that can be resident at once (per kernel and device; 0 if the query fails)
@@ -2871,6 +2963,58 @@ int kx_linear_i8(const float* x, int ldx, int rows, int k, const int8_t* wq, int
     const int ldq = (k + 15) / 16 * 16;
     if (kx_quant_rows(x, ldx, rows, k, xq_scratch, ldq, sx_scratch, stream) != 0) return -1;
     return kx_gemm_i8(xq_scratch, ldq, sx_scratch, wq, ldw, scale, bias, y, ldy, rows, n, k, act, alpha, status, stream);
+}
+
+int kx_i8_split_blocks(int m, int n, int k) {
+    if (m <= 0 || n <= 0 || k <= 0) return 1;
+    const int bn = n <= 128 ? 128 : 256, nk = (k + 127) / 128;
+    const int tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
+    int ranges = sm_count() / tiles;
+    if (ranges < 1) ranges = 1;
+    if (ranges > nk) ranges = nk;
+    if (ranges > KX_I8_SPLIT_MAX) ranges = KX_I8_SPLIT_MAX;
+    return (nk + ranges - 1) / ranges;
+}
+
+int kx_gemm_i8_split_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int m, int n, int k, int kbs, int32_t* part,
+                         int* status, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (k <= 0 || k > ldq || k > ldw || (ldq & 15) || (ldw & 15) || kbs <= 0 || part == nullptr) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n <= 128)
+        return launch_i8<128, true, -1>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, part, n, m, n, k, -1, 0.0f, status,
+                                        st, kbs);
+    return launch_i8<256, true, -1>(xq, ldq, nullptr, wq, ldw, nullptr, nullptr, nullptr, part, n, m, n, k, -1, 0.0f, status,
+                                    st, kbs);
+}
+
+int kx_i8_rows(const int32_t* part, int planes, int m, int n, const float* sx, const float* scale, const float* bias, int act,
+               float alpha, float* y, int ldy, int8_t* q, int ldq, float* sx_out, void* stream) {
+    if (m <= 0 || n <= 0) return 0;
+    if (planes < 1 || part == nullptr || sx == nullptr || scale == nullptr || n > I8R_MAXN) return -1;
+    if (q == nullptr ? (y == nullptr || ldy < n) : (sx_out == nullptr || ldq < n || ldq > I8R_MAXN || (ldq & 15)))
+        return -1;  // (the blocks' column pairs cover I8R_MAXN columns: every byte up to ldq is written)
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const dim3 grid(static_cast<unsigned>(m));
+#define KX_I8R_LAUNCH(A, Q) \
+    k_i8_rows<A, Q><<<grid, I8R_THREADS, 0, st>>>(part, planes, m, n, sx, scale, bias, act, alpha, y, ldy, q, ldq, sx_out)
+    if (q != nullptr) {
+        switch (act_class(act)) {
+        case -1: KX_I8R_LAUNCH(-1, true); break;
+        case 0: KX_I8R_LAUNCH(0, true); break;
+        case 1: KX_I8R_LAUNCH(1, true); break;
+        default: KX_I8R_LAUNCH(ACT_GENERIC, true);
+        }
+    } else {
+        switch (act_class(act)) {
+        case -1: KX_I8R_LAUNCH(-1, false); break;
+        case 0: KX_I8R_LAUNCH(0, false); break;
+        case 1: KX_I8R_LAUNCH(1, false); break;
+        default: KX_I8R_LAUNCH(ACT_GENERIC, false);
+        }
+    }
+#undef KX_I8R_LAUNCH
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,

@@ -20,6 +20,9 @@ SIGNATURES = {
     "kx_prep_i8_weight": [_vp, _i, _i, _vp, _i, _vp],
     "kx_gemm_f32": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp],
     "kx_gemm_f32_res": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _i, _vp, _vp],
+    "kx_i8_split_blocks": [_i, _i, _i],
+    "kx_gemm_i8_split_acc": [_vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp],
+    "kx_i8_rows": [_vp, _i, _i, _i, _vp, _vp, _vp, _i, _f, _vp, _i, _vp, _i, _vp, _vp],
     "kx_gemm_f32_split": [_vp, _i, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _vp, _vp, _vp],
     "kx_gemm_f32_splits": [_i, _i, _i],
     "kx_add_planes": [_vp, _i, _i, _i, _vp, _i, _f, _vp, _i, _vp],

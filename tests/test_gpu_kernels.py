@@ -268,6 +268,56 @@ def test_gemm_f32_split_count(kx):
     assert f(1, 128, 2048) == 2 and f(128, 128, 3000) == 2  # ranges of at least 1024
 
 
+@pytest.mark.parametrize("m,k,n", [(32, 1024, 4096), (32, 4096, 4096), (32, 4096, 1024), (1, 4096, 1024), (77, 2000, 520),
+                                   (128, 4096, 300), (5, 96, 100)])
+def test_gemm_i8_split_k_is_exact(kx, m, k, n):
+    """Small-batch int8 layers with K split over the SMs: the int32 planes add up to kx_gemm_i8_acc's accumulators
+    exactly; kx_i8_rows gives kx_gemm_i8's fp32 rows bit for bit (GELU and none), and its quantised rows and row scales
+    are kx_quant_rows applied to those rows (as kx_gemm_i8_q's are): a zero row, a NaN row, an inf input included."""
+    rng = np.random.default_rng(m + k + n)
+    x = rng.standard_normal((m, k)).astype(F32)
+    x[0] = 0.0
+    if m > 2:
+        x[1, 3] = np.nan
+        x[2, 5] = np.inf
+    from kernix_b200.knx_writer import quantize_int8
+    scale, qw = quantize_int8((rng.standard_normal((k, n)) * 0.02).astype(F32))
+    b = rng.standard_normal(n).astype(F32) * 0.1
+    ldq, ldo = (k + 15) // 16 * 16, (n + 15) // 16 * 16
+    xq = torch.empty((m, ldq), dtype=torch.int8, device="cuda")
+    sx = torch.empty(m, dtype=torch.float32, device="cuda")
+    kx.call("kx_quant_rows", dev(x).data_ptr(), k, m, k, xq.data_ptr(), ldq, sx.data_ptr(), sp())
+    wq, ldw = _prep_i8(kx, qw)
+    kbs = kx.lib().kx_i8_split_blocks(m, n, k)
+    planes = ((k + 127) // 128 + kbs - 1) // kbs
+    part = torch.empty((planes, m, n), dtype=torch.int32, device="cuda")
+    st = status()
+    kx.call("kx_gemm_i8_split_acc", xq.data_ptr(), ldq, wq.data_ptr(), ldw, m, n, k, kbs, part.data_ptr(), st.data_ptr(), sp())
+    acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    kx.call("kx_gemm_i8_acc", xq.data_ptr(), ldq, wq.data_ptr(), ldw, acc.data_ptr(), n, m, n, k, st.data_ptr(), sp())
+    check_status(st)
+    assert np.array_equal(host(part).astype(np.int64).sum(0).astype(np.int32), host(acc))
+    ds, db = dev(scale), dev(b)
+    for act in (1, -1):
+        want = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        kx.call("kx_gemm_i8", xq.data_ptr(), ldq, sx.data_ptr(), wq.data_ptr(), ldw, ds.data_ptr(), db.data_ptr(), want.data_ptr(),
+                n, m, n, k, act, 0.0, st.data_ptr(), sp())
+        got = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        kx.call("kx_i8_rows", part.data_ptr(), planes, m, n, sx.data_ptr(), ds.data_ptr(), db.data_ptr(), act, 0.0, got.data_ptr(),
+                n, None, 0, None, sp())
+        check_status(st)
+        assert np.array_equal(host(got).view(np.uint32), host(want).view(np.uint32)), f"act {act}"
+        q_got = torch.full((m, ldo), 7, dtype=torch.int8, device="cuda")
+        s_got = torch.empty(m, dtype=torch.float32, device="cuda")
+        kx.call("kx_i8_rows", part.data_ptr(), planes, m, n, sx.data_ptr(), ds.data_ptr(), db.data_ptr(), act, 0.0, None, 0,
+                q_got.data_ptr(), ldo, s_got.data_ptr(), sp())
+        q_want = torch.full((m, ldo), 9, dtype=torch.int8, device="cuda")
+        s_want = torch.empty(m, dtype=torch.float32, device="cuda")
+        kx.call("kx_quant_rows", want.data_ptr(), n, m, n, q_want.data_ptr(), ldo, s_want.data_ptr(), sp())
+        assert np.array_equal(host(q_got), host(q_want)), f"act {act}: int8 rows differ"
+        assert np.array_equal(host(s_got).view(np.uint32), host(s_want).view(np.uint32)), f"act {act}: row scales differ"
+
+
 @pytest.mark.parametrize("m,k,n,act,inplace", [(100, 300, 200, 0, False), (300, 512, 512, -1, True), (4096, 512, 1536, 1, False),
                                                (700, 2500, 130, -1, False), (5000, 1000, 520, 0, True)])
 def test_gemm_f32_residual_is_gemm_then_add(kx, m, k, n, act, inplace):
