@@ -62,6 +62,7 @@ struct kx_model_impl {
     float* skinny_part;   /* partial sums of the skinny dense path (LINEAR steps of <= KX_SKINNY_MAX_ROWS rows) */
     size_t skinny_floats;
     float* split_part;    /* partial-sum planes of split-K dense steps (kx_gemm_f32_split), NULL if none splits */
+    int32_t* i8s_part;    /* int32 planes of the small-batch int8 chains (kx_gemm_i8_split_acc), NULL if none */
     int* status_h;        /* pinned host copy */
     size_t scratch_per_row_max;
     int no_qchain;        /* 1 while tracing: every int8 step writes its fp32 output (int8 chains off) */
@@ -551,6 +552,38 @@ static int mlp_run(kernix_model* m, int i, long rin) {
                         im->stream);
 }
 
+#define KX_I8S_MAX_ROWS 64 /* measured on c2: the chain kernel wins from ~128 rows */
+/* small batches of an int8 chain (KX_I8S_MAX_ROWS rows or fewer): each layer's reduction split over the SMs into int32
+ * planes (kx_gemm_i8_split_acc), then one block per row adds them and dequantises, activates and quantises the row for
+ * the next layer or stores the last layer's fp32 rows (kx_i8_rows). Few rows give the chain kernel few tiles, so its
+ * layers stream their weights through a few SMs one after another; here every layer's weights spread over all SMs.
+ * Bit for bit the chain kernel's result. */
+static int i8split_planes(int m, int n, int k) {
+    const int kbs = kx_i8_split_blocks(m, n, k), nk = (k + 127) / 128;
+    return (nk + kbs - 1) / kbs;
+}
+static int i8split_ok(const kx_graph* g, int i) { /* every layer within kx_i8_rows' row width */
+    for (int l = 0; l < g->steps[i].i8c_n; l++)
+        if (round_up((size_t)g->steps[i + l].out, 16) > 8192) return 0;
+    return 1;
+}
+static int i8split_run(struct kx_model_impl* im, int n, long rin, const int8_t* const* a, const int* lda, const float* const* sx,
+                       const int8_t* const* wq, const int* ldw, const float* const* scale, const float* const* bias,
+                       const int* k, const int* nn, const int* act, const float* alpha, float* const* sx_out, float* y) {
+    for (int l = 0; l < n; l++) {
+        const int kbs = kx_i8_split_blocks((int)rin, nn[l], k[l]), planes = ((k[l] + 127) / 128 + kbs - 1) / kbs;
+        if (kx_gemm_i8_split_acc(a[l], lda[l], wq[l], ldw[l], (int)rin, nn[l], k[l], kbs, im->i8s_part, im->status,
+                                 im->stream) != 0)
+            return -1;
+        const int last = l == n - 1;
+        if (kx_i8_rows(im->i8s_part, planes, (int)rin, nn[l], sx[l], scale[l], bias[l], act[l], alpha[l], last ? y : NULL,
+                       last ? nn[l] : 0, last ? NULL : (int8_t*)a[l + 1], last ? 0 : lda[l + 1], last ? NULL : sx_out[l],
+                       im->stream) != 0)
+            return -1;
+    }
+    return 0;
+}
+
 /* the one-launch int8 chain starting at step i over `rin` rows: quantise its input (clearing the chain's control
  * words), then kx_i8_chain; scratch: per layer its int8 input (rows x K rounded to 16) and row scales, then the
  * control words */
@@ -584,6 +617,11 @@ static int i8chain_run(kernix_model* m, int i, long rin) {
         alpha[l] = s->alpha;
     }
     uint32_t* ctl = (uint32_t*)p;
+    if (rin <= KX_I8S_MAX_ROWS && im->i8s_part != NULL && i8split_ok(g, i)) {
+        if (kx_quant_rows(val_ptr(im, s0->inp[0]), s0->in, (int)rin, s0->in, (int8_t*)a[0], lda[0], (float*)sx[0], im->stream) != 0)
+            return -1;
+        return i8split_run(im, n, rin, a, lda, sx, wq, ldw, scale, bias, k, nn, act, alpha, sx_out, val_ptr(im, i + n));
+    }
     const size_t words = (size_t)(n - 1) * ((size_t)rin + 2 * (((size_t)rin + 127) / 128));
     if (kx_quant_rows_z(val_ptr(im, s0->inp[0]), s0->in, (int)rin, s0->in, (int8_t*)a[0], lda[0], (float*)sx[0], ctl, (int)words,
                         im->stream) != 0)
@@ -1206,6 +1244,20 @@ static kernix_model* model_load(const char* path, int rank, int world, kernix_al
         }
         if (mx > 0 && cudaMalloc((void**)&im->split_part, mx * sizeof(float)) != cudaSuccess) why = "cannot allocate device memory";
     }
+    const char* no_i8s = getenv("KERNIX_NO_I8_SPLIT"); /* 1: small batches of int8 chains run the chain kernel too */
+    if (why == NULL && !(no_i8s && *no_i8s && *no_i8s != '0')) { /* int8 chain planes: ranges x 128 rows x columns */
+        size_t mx = 0;
+        for (int i = 0; i < g->n_steps; i++) {
+            const kx_step* s = &g->steps[i];
+            if (s->i8c_n == 0 || !i8split_ok(g, i)) continue;
+            for (int l = 0; l < s->i8c_n; l++) {
+                const kx_step* t = &g->steps[i + l];
+                const size_t f = (size_t)i8split_planes(KX_I8S_MAX_ROWS, t->out, t->in) * KX_I8S_MAX_ROWS * (size_t)t->out;
+                if (f > mx) mx = f;
+            }
+        }
+        if (mx > 0 && cudaMalloc((void**)&im->i8s_part, mx * sizeof(int32_t)) != cudaSuccess) why = "cannot allocate device memory";
+    }
     if (why == NULL) { /* fused small-MLP chains: partial sums for up to KX_MLP_MAX_ROWS rows, the largest chain */
         size_t mx = 0;
         for (int i = 0; i < g->n_steps; i++) {
@@ -1334,6 +1386,7 @@ KERNIX_API void kernix_model_free(kernix_model* m) {
         if (im->status_h) cudaFreeHost(im->status_h);
         cudaFree(im->skinny_part);
         cudaFree(im->split_part);
+        cudaFree(im->i8s_part);
         cudaFree(im->mlp_scratch);
         cudaFree(im->mlp_bar);
         for (int i = 0; i < KX_PIPE_MAX; i++) {

@@ -436,6 +436,8 @@ k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
     __syncthreads();
     kx::tc_fence_after();
     const uint32_t tmem = ctl->tmem;
+    kx::griddep_wait();  // a programmatic dependent (the split-K form) reads the kernel before's rows after this
+    kx::griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -2327,16 +2329,21 @@ int launch_i8(const int8_t* xq, int ldq, const float* sx, const int8_t* wq, int 
     const int ranges = kbs > 0 ? (nk + kbs - 1) / kbs : 1;
     const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN) * ranges;
     const int grid = tiles < sm_count() ? tiles : sm_count();
+    if (kbs > 0)  // split-K: a dependent of the quantiser or row kernel before it
+        return kx::launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, ta, tb, sx, scale, bias, y, acc, ldy, m, n, k,
+                              act, alpha, status, kbs);
     kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, sx, scale, bias, y, acc, ldy, m, n, k, act, alpha, status, kbs);
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-// The rows of a split-K int8 layer (kx_gemm_i8_split_acc's int32 planes [z][row][column]): one block per row adds the
-// planes (exact: int32 sums modulo 2^32 do not depend on the order), then applies the epilogue's steps in its order --
+// The rows of a split-K int8 layer (kx_gemm_i8_split_acc's int32 planes [z][row][column]): one block of 1024 threads
+// per row adds the planes (exact: int32 sums modulo 2^32 do not depend on the order; four columns per thread group read
+// as one 16-byte load per plane, four planes' loads in flight at once; a row of fewer than 512 four-column groups gives
+// each group G = 2..8 adjacent threads, which take every G-th plane and then add their sums by shuffles), then applies the epilogue's steps in its order --
 // ((float)acc * sx) * scale + bias (0 without one), the activation on pairs of columns -- and either stores the fp32
 // row or (QOUT) quantises it as the quantised-output epilogue does: the row's maximum |y| (NaN wins), sx = m / 127,
 // inv = 1 / sx, q = rint(y inv) as the low byte of y inv + 1.5 2^23; columns N .. ldq - 1 are written as 0.
-constexpr int I8R_THREADS = 256, I8R_PAIRS = 16, I8R_MAXN = 2 * I8R_THREADS * I8R_PAIRS;
+constexpr int I8R_THREADS = 1024, I8R_QUADS = 2, I8R_MAXN = 4 * I8R_THREADS * I8R_QUADS;
 template <int ACTC, bool QOUT>
 __global__ void __launch_bounds__(I8R_THREADS) k_i8_rows(const int32_t* __restrict__ part, int planes, int M, int N,
                                                           const float* __restrict__ sx, const float* __restrict__ scale,
@@ -2345,34 +2352,85 @@ __global__ void __launch_bounds__(I8R_THREADS) k_i8_rows(const int32_t* __restri
                                                           float* __restrict__ sx_out) {
     __shared__ uint32_t red[I8R_THREADS / 32];
     const int row = blockIdx.x, tid = threadIdx.x;
+    kx::griddep_wait();  // launched as a dependent of the split-K GEMM that writes the planes
+    kx::griddep_launch_dependents();
     const float sxr = __ldg(sx + row);
     const size_t plane = static_cast<size_t>(M) * N;
-    float2 v[I8R_PAIRS];
+    const bool vec = (N & 3) == 0 && (reinterpret_cast<uintptr_t>(part) & 15) == 0;
+    const bool yvec = !QOUT && ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+    const int quads = (N + 3) / 4;
+    int G = 1;  // threads per four-column group
+    while (G < 8 && quads * G * 2 <= I8R_THREADS) G *= 2;
+    const int g = tid % G, per_pass = I8R_THREADS / G;
+    float v[I8R_QUADS][4];
     uint32_t mx = 0u;
 #pragma unroll
-    for (int j = 0; j < I8R_PAIRS; j++) {
-        const int c = 2 * (tid + j * I8R_THREADS);
-        v[j] = make_float2(0.0f, 0.0f);
-        if (c >= N) continue;
-        const bool two = c + 1 < N;
-        const int32_t* src = part + static_cast<size_t>(row) * N + c;
-        uint32_t a0 = 0u, a1 = 0u;  // modulo 2^32, as the MMA's int32 accumulator
-        for (int z = 0; z < planes; z++) {
-            a0 += static_cast<uint32_t>(__ldg(src + z * plane));
-            if (two) a1 += static_cast<uint32_t>(__ldg(src + z * plane + 1));
+    for (int j = 0; j < I8R_QUADS; j++) {
+        const int c = 4 * (tid / G + j * per_pass);
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[j][e] = 0.0f;
+        uint32_t acc[4] = {0u, 0u, 0u, 0u};  // modulo 2^32, as the MMA's int32 accumulator
+        if (c < N) {
+            const int32_t* src = part + static_cast<size_t>(row) * N + c;
+            if (vec) {
+                int z = g;
+                for (; z + 3 * G < planes; z += 4 * G) {
+                    int4 t[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) t[u] = __ldg(reinterpret_cast<const int4*>(src + (z + u * G) * plane));
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        acc[0] += static_cast<uint32_t>(t[u].x);
+                        acc[1] += static_cast<uint32_t>(t[u].y);
+                        acc[2] += static_cast<uint32_t>(t[u].z);
+                        acc[3] += static_cast<uint32_t>(t[u].w);
+                    }
+                }
+                for (; z < planes; z += G) {
+                    const int4 t = __ldg(reinterpret_cast<const int4*>(src + z * plane));
+                    acc[0] += static_cast<uint32_t>(t.x);
+                    acc[1] += static_cast<uint32_t>(t.y);
+                    acc[2] += static_cast<uint32_t>(t.z);
+                    acc[3] += static_cast<uint32_t>(t.w);
+                }
+            } else {
+                for (int z = g; z < planes; z += G)
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        if (c + e < N) acc[e] += static_cast<uint32_t>(__ldg(src + z * plane + e));
+            }
         }
-        const float2 f = kx::mul2(kx::mul2(make_float2(static_cast<float>(static_cast<int32_t>(a0)),
-                                                       static_cast<float>(static_cast<int32_t>(a1))), kx::f2(sxr)),
-                                  make_float2(__ldg(scale + c), two ? __ldg(scale + c + 1) : 0.0f));
-        const float2 b = make_float2(bias ? __ldg(bias + c) : 0.0f, bias && two ? __ldg(bias + c + 1) : 0.0f);
-        v[j] = epi_act2<ACTC>(make_float2(__fadd_rn(f.x, b.x), __fadd_rn(f.y, b.y)), act, alpha);
-        if constexpr (QOUT) {
-            mx = kx::absmax_nan(mx, v[j].x);
-            if (two) mx = kx::absmax_nan(mx, v[j].y);
-        } else {
+        // the group's lanes are adjacent within a warp (G divides 32); every lane takes part in the shuffles
+        for (int o = 1; o < G; o <<= 1)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+        if (c >= N || g != 0) continue;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {  // column pairs (c, c + 1) and (c + 2, c + 3), as the epilogue pairs them
+            const int c0 = c + 2 * h;
+            const bool has0 = c0 < N, has1 = c0 + 1 < N;
+            const float2 f = kx::mul2(kx::mul2(make_float2(static_cast<float>(static_cast<int32_t>(acc[2 * h])),
+                                                           static_cast<float>(static_cast<int32_t>(acc[2 * h + 1]))),
+                                               kx::f2(sxr)),
+                                      make_float2(has0 ? __ldg(scale + c0) : 0.0f, has1 ? __ldg(scale + c0 + 1) : 0.0f));
+            const float2 b = make_float2(bias && has0 ? __ldg(bias + c0) : 0.0f, bias && has1 ? __ldg(bias + c0 + 1) : 0.0f);
+            const float2 o = epi_act2<ACTC>(make_float2(__fadd_rn(f.x, b.x), __fadd_rn(f.y, b.y)), act, alpha);
+            v[j][2 * h] = o.x;
+            v[j][2 * h + 1] = o.y;
+            if constexpr (QOUT) {
+                if (has0) mx = kx::absmax_nan(mx, o.x);
+                if (has1) mx = kx::absmax_nan(mx, o.y);
+            }
+        }
+        if constexpr (!QOUT) {
             float* dst = y + static_cast<size_t>(row) * ldy + c;
-            dst[0] = v[j].x;
-            if (two) dst[1] = v[j].y;
+            if (yvec && c + 3 < N) {
+                *reinterpret_cast<float4*>(dst) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (c + e < N) dst[e] = v[j][e];
+            }
         }
     }
     if constexpr (QOUT) {
@@ -2392,15 +2450,17 @@ __global__ void __launch_bounds__(I8R_THREADS) k_i8_rows(const int32_t* __restri
             inv = __fdiv_rn(1.0f, sxv);
         }
         if (tid == 0) sx_out[row] = sxv;
-        uint16_t* qrow = reinterpret_cast<uint16_t*>(q + static_cast<size_t>(row) * ldq);
+        uint32_t* qrow = reinterpret_cast<uint32_t*>(q + static_cast<size_t>(row) * ldq);
 #pragma unroll
-        for (int j = 0; j < I8R_PAIRS; j++) {
-            const int c = 2 * (tid + j * I8R_THREADS);
-            if (c >= ldq) continue;
-            uint32_t b0 = 0u, b1 = 0u;
-            if (!nan_row && c < N) b0 = __float_as_uint(__fadd_rn(__fmul_rn(v[j].x, inv), 12582912.0f)) & 0xFFu;
-            if (!nan_row && c + 1 < N) b1 = __float_as_uint(__fadd_rn(__fmul_rn(v[j].y, inv), 12582912.0f)) & 0xFFu;
-            qrow[c >> 1] = static_cast<uint16_t>(b0 | (b1 << 8));
+        for (int j = 0; j < I8R_QUADS; j++) {
+            const int c = 4 * (tid / G + j * per_pass);
+            if (c >= ldq || g != 0) continue;
+            uint32_t w = 0u;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (!nan_row && c + e < N)
+                    w |= (__float_as_uint(__fadd_rn(__fmul_rn(v[j][e], inv), 12582912.0f)) & 0xFFu) << (8 * e);
+            qrow[c >> 2] = w;
         }
     }
 }
@@ -2996,8 +3056,10 @@ int kx_i8_rows(const int32_t* part, int planes, int m, int n, const float* sx, c
         return -1;  // (the blocks' column pairs cover I8R_MAXN columns: every byte up to ldq is written)
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const dim3 grid(static_cast<unsigned>(m));
-#define KX_I8R_LAUNCH(A, Q) \
-    k_i8_rows<A, Q><<<grid, I8R_THREADS, 0, st>>>(part, planes, m, n, sx, scale, bias, act, alpha, y, ldy, q, ldq, sx_out)
+    int rc = -1;
+#define KX_I8R_LAUNCH(A, Q)                                                                                     \
+    rc = kx::launch_pdl(k_i8_rows<A, Q>, grid, dim3(I8R_THREADS), 0, st, part, planes, m, n, sx, scale, bias, act, alpha, y, \
+                        ldy, q, ldq, sx_out)
     if (q != nullptr) {
         switch (act_class(act)) {
         case -1: KX_I8R_LAUNCH(-1, true); break;
@@ -3014,7 +3076,7 @@ int kx_i8_rows(const int32_t* part, int planes, int m, int n, const float* sx, c
         }
     }
 #undef KX_I8R_LAUNCH
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    return rc;
 }
 
 int kx_gemm_i8_acc(const int8_t* xq, int ldq, const int8_t* wq, int ldw, int32_t* acc, int ldacc, int m, int n, int k,
