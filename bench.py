@@ -642,8 +642,8 @@ PER_CONFIG = [("c1", 256), ("c2", 32), ("c3", 1024), ("c4", 512), ("c5", 1), ("c
 # biases), c5's fp32 weights (+ biases)
 WEIGHT_BYTES = {"c2": 1024 * 4096 + 4096 * 4096 + 4096 * 1024 + 8 * (4096 + 4096 + 1024),
                 "c5": 4 * (8192 * 16384 + 16384 * 16384 + 16384 * 8192) + 4 * (16384 + 16384 + 8192)}
-DOMINANT = {"c1": "k_gemm_tf32x3 (3xTF32 tcgen05, one CTA per 128-row tile)",
-            "c2": "k_gemm_i8 / k_gemm_i8_pair (tcgen05 kind::i8) streaming the int8 weights",
+DOMINANT = {"c1": "k_mlp_chain (the three layers and the softmax in one cooperative launch, CUDA cores)",
+            "c2": "k_gemm_i8 with K ranges + k_i8_rows (split-K int8 layers: tcgen05 kind::i8 over every SM)",
             "c3": "k_conv_tf32x3_cmt (3xTF32 tcgen05 implicit-GEMM convolution fed by TMA)",
             "c4": "k_gemm_tf32x3_pp / k_gemm_tf32x3_pair (3xTF32 tcgen05 GEMMs)",
             "c5@1": "k_skinny (fp32 weight streaming on the CUDA cores)",
