@@ -83,6 +83,7 @@ class Model:
         kernix_b200.shard.torch_allgather)."""
         self._lock = threading.Lock()
         L = lib()
+        self._free = L.kernix_capi_free  # held here: at interpreter exit the module globals may already be gone
         self._gather_cb = None
         if shard is None:
             self._h = L.kernix_capi_load(os.fsencode(path))
@@ -164,7 +165,7 @@ class Model:
     def close(self):
         if getattr(self, "_h", None):
             with self._lock:
-                lib().kernix_capi_free(self._h)
+                self._free(self._h)
                 self._h = None
 
     __del__ = close
