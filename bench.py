@@ -769,7 +769,8 @@ def run_config(args):
             "metric": f"samples/s, configuration {cfg}, device-resident forward", "value": world * B * args.steps / t,
             "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32 (3xTF32 tensor cores)", "data": "synthetic: the configuration's seeded inputs and weights",
+            "dtype": "f32 (CUDA-core fp32 FMA)" if cfg == "c1" else "f32 (3xTF32 tensor cores)",
+            "data": "synthetic: the configuration's seeded inputs and weights",
             "config": {"workload": cfg, "batch_per_gpu": B, "global_batch": B * world, "parallelism": f"dp{world}",
                        "l2": "flushed (256 MB write) before every step"},
             "achieved_tflops": CONFIG_FLOPS[cfg] * B * world * args.steps / t / 1e12,
