@@ -158,8 +158,8 @@ KERNIX_API int kx_prep_f32_weight(const float* w_kn, int k, int n, float* w_hi, 
  * each layer's K ranges depend on its k and n only, so a row's result does not depend on the batch it is in. For batches whose tensor-core GEMMs are dominated by per-launch costs (rows <=
  * KX_MLP_MAX_ROWS). w[l]: k[l] x n[l] row-major fp32; bias[l] may be NULL; ldx and every n[l] but the last multiples of
  * 4, x and scratch 16-byte aligned; scratch: kx_mlp_chain_scratch_floats(m, k, n, n_layers) floats; bar: two words
- * (the first counts barrier arrivals and only grows), zero before the first launch, kept between launches (reset them
- * after a timeout). */
+ * (arrivals at the current grid barrier, barrier generation), zero before the first launch, kept between launches
+ * (reset them after a timeout). */
 #define KX_MLP_MAX_LAYERS 8
 #define KX_MLP_MAX_SPLIT 8
 #define KX_MLP_MAX_ROWS 512

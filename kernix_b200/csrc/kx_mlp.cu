@@ -23,12 +23,12 @@
 // how the batch is cut. fp32 accumulation over K <= 8192 stays within ~1e-6 of the exact product, inside the
 // dense-MLP bound of 1e-5.
 //
-// The grid barrier counts arrivals in bar[0], which only grows: each CTA reads it when it starts (every arrival of
-// earlier launches has landed by then) and barrier l of the launch is passed once it reaches that base plus (l + 1)
-// times the grid, so a barrier costs one reduction and the wait, the word needs no reset between launches, and a
-// launch of another grid size starts from wherever the last one left it (bounded wait: a timeout writes
-// KX_STATUS_TIMEOUT and the CTA leaves; the runtime then zeroes the word). A cooperative launch makes every CTA
-// resident at once.
+// The grid barrier counts arrivals in bar[0]; the last arriver resets it and advances the generation bar[1], on which
+// the others wait (bounded: a timeout writes KX_STATUS_TIMEOUT and the CTA leaves; the runtime then zeroes both
+// words), so the words need no clearing between launches. Each CTA reads the generation once when it starts: it
+// advances only when every CTA has arrived, so even a CTA that starts after the others have reached the first barrier
+// reads the value from before it (an arrival count read at the start would not be: a late CTA would see the others'
+// arrivals). A cooperative launch makes every CTA resident at once.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -69,7 +69,7 @@ struct MlpChain {
     float* y;
     int M;
     int softmax;
-    uint32_t* bar;  // [0] arrivals (only grows)
+    uint32_t* bar;  // [0] arrivals at the current barrier, [1] generation
     int* status;
 };
 
@@ -88,22 +88,28 @@ __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefe
 
 __device__ __forceinline__ float f4(const float4& v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
 
-// bounded grid barrier: arrive, then wait until the arrival count reaches `target`; false (status set) if it gave up
+// bounded grid barrier over gridDim.x CTAs, passed when the generation reaches `target`; false (status set) if it
+// gave up
 __device__ bool grid_barrier(uint32_t* bar, uint32_t target, int* status, int* s_ok) {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        atomicAdd(bar, 1u);
         bool ok = true;
-        const uint64_t t0 = kx::globaltimer();
-        for (uint32_t spin = 0; static_cast<int>(kx::ld_acquire_gpu(bar) - target) < 0; spin++) {
-            if ((spin & 15) == 15) {
-                if (kx::globaltimer() - t0 > KX_WAIT_NS) {
-                    if (status) atomicExch(status, KX_STATUS_TIMEOUT);
-                    ok = false;
-                    break;
+        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            const uint64_t t0 = kx::globaltimer();
+            for (uint32_t spin = 0; static_cast<int>(kx::ld_acquire_gpu(bar + 1) - target) < 0; spin++) {
+                if ((spin & 15) == 15) {
+                    if (kx::globaltimer() - t0 > KX_WAIT_NS) {
+                        if (status) atomicExch(status, KX_STATUS_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(32);
                 }
-                __nanosleep(32);
             }
         }
         *s_ok = ok;
@@ -263,8 +269,8 @@ __global__ void __launch_bounds__(THREADS) k_mlp_chain(const MlpChain c) {
     const int ar = tid >> 2, akq = (tid & 3) * 4;  // A staging: row, first k of the thread's four (+16 for the second)
     const int wk = tid >> 4, wn = (tid & 15) * 4;  // W staging: k row (+16 for the second), first of four columns
     const int n_gemm = c.n_layers - c.fuse;
-    uint32_t base = 0;  // the arrival count before this launch (thread 0 waits on it)
-    if (tid == 0) base = kx::ld_acquire_gpu(c.bar);
+    uint32_t gen = 0;  // the generation before this launch's first barrier (thread 0 waits on it)
+    if (tid == 0) gen = kx::ld_acquire_gpu(c.bar + 1);
     // in flight while the first layer runs: the last layer's weights into shared memory, later layers' towards L2
     if (c.fuse) {
         const MlpLayer& F = c.L[c.n_layers - 1];
@@ -338,7 +344,7 @@ __global__ void __launch_bounds__(THREADS) k_mlp_chain(const MlpChain c) {
             }
             __syncthreads();  // the staging buffers are reused by the next item
         }
-        if (!grid_barrier(c.bar, base + (l + 1) * gridDim.x, c.status, &s_ok)) {
+        if (!grid_barrier(c.bar, gen + l + 1, c.status, &s_ok)) {
             cp_async_wait<0>();
             return;
         }
