@@ -396,6 +396,22 @@ def test_fused_mlp_chain(Model, model_dir, monkeypatch, dims, acts, softmax, row
     assert rel_err(got_big, np.concatenate([want, want, want])) <= 1e-5
 
 
+def test_fused_mlp_chain_back_to_back_grids(Model, model_dir, monkeypatch):
+    """Chain launches of different grid sizes one after another on one model (c1 at 1 to 512 rows: 32 to 148 CTAs)
+    keep the grid-barrier words consistent from launch to launch: no call reports a barrier that gave up, and each
+    batch gives the bits of its first call every time."""
+    from kernix_b200 import configs
+    monkeypatch.delenv("KERNIX_NO_MLP_CHAIN", raising=False)
+    monkeypatch.setenv("KERNIX_PIPELINE", "1")
+    m = Model(cfg_path("c1", model_dir), workspace_mb=0)
+    xs = {r: configs.inputs("c1", r, seed=7 + r) for r in (1, 17, 64, 256, 512)}
+    first = {r: m(xs[r]).copy() for r in xs}
+    for _ in range(8):
+        for r in (512, 1, 256, 17, 64, 512, 512):
+            assert np.array_equal(m(xs[r]), first[r])
+    m.close()
+
+
 @pytest.mark.parametrize("dims,rows", [((4096, 8192, 8192, 4096), 64), ((4096, 8192, 8192, 4096), 128),
                                        ((3000, 2600, 260), 40), ((4096, 8192, 8192, 4096), 17)])
 def test_split_k_dense_steps(Model, model_dir, monkeypatch, dims, rows):
